@@ -1,0 +1,361 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 absorbed-MLA decode-attention path (one JSON line on rank 0).
+
+A step is one attention task (K1 prologue + K2 split-KV attention + K3 merge/W_UV)
+over one batch, with the latent cache resident in HBM. Metric: KV GB/s, the latent
+cache bytes a step must read (sum_b (T_b + 1) * 1152) over its device time; the line
+also gives µs per layer-step and the HBM roofline fraction of the attention kernel.
+
+    python bench.py [--workload config5a] [--steps K] [--warmup W]
+    torchrun --nproc-per-node N bench.py --gpus N ...     # by-request shards, weak scaling
+    python bench.py --impl reference ...                  # the CPU oracle on the host cores
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+fleet = importlib.import_module("fleet-mi300x_b200")
+workloads = importlib.import_module("fleet-mi300x_b200.workloads")
+native = importlib.import_module("fleet-mi300x_b200.native")
+
+METRIC = "MLA decode attn KV GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+def ncu_traffic(workload: str) -> float | None:
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / f"attention_{workload}_ncu.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- set-up
+def build_workload(name: str, dev: torch.device, rank: int):
+    wl = workloads.WORKLOADS[name]
+    lengths = wl.seq_lens()
+    cfg = fleet.ModelConfig()
+    lw = workloads.make_layer_weights(wl.seed)
+    w = fleet.LayerWeights(*(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm,
+                                                   lw.kv_b_proj)))
+    cos, sin = fleet.device_rope_tables(cfg, max(lengths) + 8, dev)
+    cache = fleet.PagedLatentCache.for_lengths(lengths, permute=wl.permute, zero=False,
+                                               generator=torch.Generator().manual_seed(wl.seed + rank), device=dev)
+    workloads.fill_pool_random(cache.pages, wl.seed + 1000 * rank)
+    x_n = workloads.make_hidden(wl.seed + 1, len(lengths)).to(dev)
+    runner = fleet.MlaDecodeAttention(cfg, w, cos, sin)
+    q, kv_a = runner.project(x_n)
+    q, kv_a = q.contiguous(), kv_a.contiguous()
+    return wl, lengths, runner, cache, x_n, q, kv_a
+
+
+def time_loop(fn, steps: int, stream: torch.cuda.Stream) -> float:
+    """Device ms per call, CUDA events on the launching stream."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def cpu_oracle_sample(name: str, budget_s: float, faithful: bool) -> dict:
+    """Times the CPU oracle on a bounded sample of the workload's requests."""
+    from oracle import mla_oracle as O
+    wl = workloads.WORKLOADS[name]
+    lengths = wl.seq_lens()
+    cfg = O.Config()
+    lw = workloads.make_layer_weights(wl.seed)
+    f = lambda t: t.float().numpy()
+    w = O.Weights(f(lw.q_proj), f(lw.kv_a_proj_with_mqa), f(lw.kv_a_layernorm), f(lw.kv_b_proj))
+    x_n = workloads.make_hidden(wl.seed + 1, min(len(lengths), 64)).float().numpy()
+    rng = np.random.default_rng(wl.seed)
+    attend = O.attend_rows if faithful else O.attend_rows_fast
+    cos, sin = cfg.cos_sin(max(lengths) + 8)
+    done_bytes, done_req, t_total = 0, 0, 0.0
+    i = 0
+    while t_total < budget_s and done_req < 4 * len(lengths):
+        b = i % len(lengths)
+        T = lengths[b]
+        rows = O.bf16_round(rng.standard_normal((T, 576), dtype=np.float32))
+        q, kv_a = O.project(cfg, w, x_n[b % len(x_n)])
+        t0 = time.perf_counter()
+        row = O.kv_post(cfg, w, kv_a, T, cos, sin)
+        allr = np.concatenate([rows, row[None]], 0)
+        attend(cfg, w, q, allr, T, cos, sin)
+        t_total += time.perf_counter() - t0
+        done_bytes += (T + 1) * 1152
+        done_req += 1
+        i += 1
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([x.get("num_threads", 1) for x in threadpool_info()] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    return {"value": done_bytes / t_total / 1e9, "unit": "GB/s", "cores": int(cores), "kind": "port",
+            "sample": f"{done_req} requests of {name} ({done_bytes / 1e6:.1f} MB of cache rows), "
+                      f"{'per-head loop (reference_decode.py:245-254)' if faithful else 'all-heads vectorised'} "
+                      f"NumPy/BLAS, {t_total:.2f} s",
+            "seconds": t_total}
+
+
+# ---------------------------------------------------------------------------- arms
+def run_reference_arm(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    steps_out = []
+    per_step_budget = max(0.5, min(6.0, 120.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_oracle_sample(args.workload, per_step_budget / 4, faithful=True)
+    info = None
+    for _ in range(args.steps):
+        info = cpu_oracle_sample(args.workload, per_step_budget, faithful=True)
+        steps_out.append(info)
+    total_s = sum(s["seconds"] for s in steps_out)
+    total_b = sum(s["value"] * s["seconds"] * 1e9 for s in steps_out)
+    value = total_b / total_s / 1e9
+    wl = workloads.WORKLOADS[args.workload]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total_s / max(1, args.steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": args.workload, "batch_per_gpu": wl.batch, "parallelism": "cpu-host"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": info["cores"], "kind": "port",
+                         "sample": info["sample"] + " per step"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    wl, lengths, runner, cache, x_n, q, kv_a = build_workload(args.workload, dev, rank)
+    B = len(lengths)
+    out = torch.empty(B, 2048, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    step = lambda: runner.attend(q, kv_a, cache, out)
+
+    # warm-up (also JIT-free: the library is prebuilt)
+    for _ in range(max(3, args.warmup)):
+        step()
+    runner.check_errors()
+
+    # ---- timed region: K steps of the whole task, inputs resident
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ms = time_loop(step, args.steps, stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+    ms_max = ms
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    runner.check_errors()
+
+    kv_b = workloads.kv_bytes(lengths)
+    tot_b = workloads.total_bytes(lengths)
+    value = world * kv_b / (ms_max * 1e-3) / 1e9
+
+    # ---- stage timings: the attention kernel alone (roofline) and the other two
+    p = runner.params(q, kv_a, cache, out)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    lib = runner.lib
+    native.check(lib.mla_prologue(ctypes.byref(p), sptr), "prologue")
+    k1_ms = time_loop(lambda: lib.mla_prologue(ctypes.byref(p), sptr), max(5, args.steps), stream)
+    k2_ms = time_loop(lambda: lib.mla_attention(ctypes.byref(p), sptr), max(5, args.steps), stream)
+    k3_ms = time_loop(lambda: lib.mla_merge_uv(ctypes.byref(p), sptr), max(5, args.steps), stream)
+    peak, peak_src = measured_peak()
+    k2_gbs = kv_b / (k2_ms * 1e-3) / 1e9
+    traffic = ncu_traffic(args.workload)
+
+    # ---- e2e through the public call: pinned host x_n -> device, task, R(out) -> host
+    x_host = x_n.cpu().pin_memory()
+    out_host = torch.empty(B, 2048, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x_n)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        fleet.attention_absorbed(runner.cfg, runner.w, x_dev, cache, runner=runner)
+        out_host.copy_(out, non_blocking=True)
+
+    def e2e_step_real():
+        x_dev.copy_(x_host, non_blocking=True)
+        o = runner(x_dev, cache, out)
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step_real()
+    if dist:
+        dist.barrier()
+    e2e_ms = time_loop(e2e_step_real, args.steps, stream)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * kv_b / (e2e_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_oracle_sample(args.workload, args.cpu_seconds, faithful=False)
+        cpu.pop("seconds", None)
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    us = ms_max * 1e3
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents, N(0,0.02) weights)",
+        "config": {"workload": args.workload, "batch_per_gpu": B, "context": (lengths[0] if len(set(lengths)) == 1
+                                                                            else [min(lengths), max(lengths)]),
+                   "page_size": 64, "block_table": "permuted" if wl.permute else "contiguous",
+                   "parallelism": f"by-request x{world}" if world > 1 else "single GPU",
+                   "kv_bytes_per_gpu_step": kv_b,
+                   "l2": "no flush: each step reads %.0f MB of cache rows, > 126 MB L2" % (kv_b / 1e6)
+                   if kv_b > 126e6 else "inputs smaller than L2; steps re-read from L2"},
+        "us_per_layer_step": round(us, 3),
+        "kv_frac_of_hbm_peak": round(value / world / peak, 4),
+        "attn_tokens_per_s_27_layers": round(world * B / (27 * us * 1e-6), 1),
+        "stages_us": {"prologue": round(k1_ms * 1e3, 2), "attention": round(k2_ms * 1e3, 2),
+                      "merge_uv": round(k3_ms * 1e3, 2)},
+        "roofline": {"bound": "hbm", "kernel": "k2_attention_tc", "achieved": round(k2_gbs, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(k2_gbs / peak, 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": kv_b, "peak_source": peak_src},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": int(x_n.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2),
+                "path": "attention_absorbed-style call: pinned x_n H2D, cuBLAS q|kv_a, K1-K3, R(out) D2H"},
+        "gpu_launches": native.load_library().mla_launches_per_step() * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="config5a", choices=sorted(workloads.WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+    else:
+        run_gpu_arm(args, rank, world, local_rank)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

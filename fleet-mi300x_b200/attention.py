@@ -1,0 +1,188 @@
+"""Host side of the attention task: the drop-in for reference_decode.attention_absorbed.
+
+The reference's `attention_absorbed(cfg, w, x, cache, pos, cos, sin)`
+(src/host/reference_decode.py:210-256) normalises x, projects q and kv_a, appends
+this token's cache row, attends and returns o_proj of the result. The north-star
+slice kept here starts at the post-RMSNorm hidden state x_n (:224) and ends at the
+head-concatenated bf16 output R(out) before o_proj (:256):
+
+    q, kv_a      = R(W_q x_n), R(W_kv_a x_n)       cuBLAS bf16 GEMM (torch), one fused [W_q; W_kv_a]
+    K1 prologue  kv_post + cache append + q_pe RoPE + q_c = q_nope W_UK      (libmla_decode.so)
+    K2 attention split-KV scores, online softmax, P c_kv on tcgen05         (libmla_decode.so)
+    K3 merge     fixed-order LSE merge + W_UV up-projection, bf16 out       (libmla_decode.so)
+
+Everything after the GEMM runs in the C-ABI library; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import native
+from .cache import PagedLatentCache
+from .config import ModelConfig, rope_tables
+
+
+@dataclass
+class LayerWeights:
+    """The attention weights of one layer, as device tensors (names follow HF /
+    reference_decode.LayerWeights, reference_decode.py:139-159)."""
+
+    q_proj: torch.Tensor               # [heads*192, hidden] bf16
+    kv_a_proj_with_mqa: torch.Tensor   # [576, hidden] bf16
+    kv_a_layernorm: torch.Tensor       # [512] bf16
+    kv_b_proj: torch.Tensor            # [heads*256, 512] bf16
+
+    def fused_qkv(self) -> torch.Tensor:
+        return torch.cat([self.q_proj, self.kv_a_proj_with_mqa], dim=0).contiguous()
+
+
+def device_rope_tables(cfg: ModelConfig, max_pos: int, device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    cos, sin = rope_tables(cfg, max_pos)
+    return (torch.from_numpy(np.ascontiguousarray(cos)).to(device),
+            torch.from_numpy(np.ascontiguousarray(sin)).to(device))
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class MlaDecodeAttention:
+    """One layer's attention task over a PagedLatentCache.
+
+    Owns the fused q|kv_a weight, the workspace and a device error word; the
+    library itself allocates nothing. Calls are stream-ordered on the current
+    torch stream and can be captured in a CUDA graph.
+    """
+
+    def __init__(self, cfg: ModelConfig, w: LayerWeights, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
+                 *, num_ctas: int = 0, check_kernel: bool = False):
+        cfg.check_supported()
+        self.cfg = cfg
+        self.lib = native.load_library()
+        dev = w.kv_b_proj.device
+        if dev.type != "cuda":
+            raise RuntimeError("MlaDecodeAttention needs CUDA tensors (sm_100a); there is no CPU path")
+        self.device = dev
+        self.w = w
+        self.w_qkv = w.fused_qkv()
+        self.kv_b = w.kv_b_proj.contiguous()
+        self.norm_w = w.kv_a_layernorm.contiguous()
+        self.cos = rope_cos.contiguous().float()
+        self.sin = rope_sin.contiguous().float()
+        self.num_ctas = int(num_ctas)
+        self.flags = native.FLAG_CHECK_KERNEL if check_kernel else 0
+        self.error_word = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._ws: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------ params
+    def params(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
+               out: torch.Tensor) -> native.MlaDecodeParams:
+        B = q.shape[0]
+        p = native.new_params()
+        p.softmax_scale = self.cfg.softmax_scale
+        p.rms_eps = self.cfg.rms_eps
+        p.batch = B
+        p.max_blocks = cache.max_blocks
+        p.n_pages = cache.n_pages
+        p.max_pos = self.cos.shape[0]
+        p.q, p.q_stride = _ptr(q), q.stride(0)
+        p.kv_a, p.kv_a_stride = _ptr(kv_a), kv_a.stride(0)
+        p.kv_a_norm_w = _ptr(self.norm_w)
+        p.kv_b = _ptr(self.kv_b)
+        p.rope_cos, p.rope_sin = _ptr(self.cos), _ptr(self.sin)
+        p.block_table = _ptr(cache.block_table)
+        p.seq_lens = _ptr(cache.seq_lens)
+        p.kv_cache = _ptr(cache.pages)
+        p.out, p.out_stride = _ptr(out), out.stride(0)
+        p.error_word = _ptr(self.error_word)
+        p.num_ctas = self.num_ctas
+        p.flags = self.flags
+        need = ctypes.c_uint64()
+        native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
+        if self._ws is None or self._ws.numel() < need.value:
+            self._ws = torch.empty(int(need.value), dtype=torch.uint8, device=self.device)
+        p.workspace = _ptr(self._ws)
+        p.workspace_bytes = self._ws.numel()
+        return p
+
+    def _check_inputs(self, q, kv_a, cache):
+        if q.dtype != torch.bfloat16 or kv_a.dtype != torch.bfloat16:
+            raise TypeError("q and kv_a must be bf16")
+        if q.shape[0] != cache.batch or kv_a.shape[0] != cache.batch:
+            raise ValueError(f"batch {q.shape[0]} does not match the cache's {cache.batch} requests")
+        if q.stride(-1) != 1 or kv_a.stride(-1) != 1:
+            raise ValueError("q and kv_a rows must be contiguous")
+
+    # ------------------------------------------------------------------ calls
+    def attend(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
+               out: torch.Tensor | None = None, stage: str = "all") -> torch.Tensor:
+        """K1+K2+K3 from q [B, 3072] and kv_a [B, 576] (bf16 views allowed).
+        Appends each request's row at seq_lens[b]; does not advance seq_lens."""
+        self._check_inputs(q, kv_a, cache)
+        if out is None:
+            out = torch.empty(q.shape[0], self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16,
+                              device=self.device)
+        p = self.params(q, kv_a, cache, out)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        fn = {"all": self.lib.mla_decode_step, "prologue": self.lib.mla_prologue,
+              "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv}[stage]
+        native.check(fn(ctypes.byref(p), stream), f"mla {stage}")
+        return out
+
+    def project(self, x_n: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """q = R(W_q x_n), kv_a = R(W_kv_a x_n) as views of one bf16 GEMM output."""
+        qkv = torch.nn.functional.linear(x_n, self.w_qkv)
+        nq = self.cfg.heads * self.cfg.q_head_dim
+        return qkv[:, :nq], qkv[:, nq:]
+
+    def __call__(self, x_n: torch.Tensor, cache: PagedLatentCache,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        q, kv_a = self.project(x_n)
+        return self.attend(q, kv_a, cache, out)
+
+    def check_errors(self, reset: bool = True) -> None:
+        """Raise if a kernel recorded a device error (synchronises)."""
+        code = int(self.error_word.item())
+        if reset and code:
+            self.error_word.zero_()
+        if code:
+            raise native.MlaError(code, "device")
+
+    def workspace_bytes(self, batch: int) -> int:
+        p = native.new_params()
+        p.batch = batch
+        p.num_ctas = self.num_ctas
+        need = ctypes.c_uint64()
+        native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
+        return int(need.value)
+
+
+def attention_absorbed(cfg: ModelConfig, w: LayerWeights, x_n: torch.Tensor, cache: PagedLatentCache,
+                       pos=None, cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                       *, runner: MlaDecodeAttention | None = None) -> torch.Tensor:
+    """Drop-in for the attention slice of reference_decode.attention_absorbed.
+
+    x_n: post-RMSNorm hidden state, bf16 [hidden] or [B, hidden], on the GPU.
+    cache: PagedLatentCache; request b's new row is written at `pos` (an int for
+    B = 1, a sequence, or None to use cache.seq_lens) and attention runs over rows
+    0..pos inclusive. As in the reference, the cache is appended in place and the
+    caller advances positions (cache.advance()).
+    Returns R(out): bf16 [B, heads*v_head] (or [heads*v_head] for 1-D x_n), the
+    head-concatenated attention output before o_proj.
+    """
+    squeeze = x_n.dim() == 1
+    if squeeze:
+        x_n = x_n[None, :]
+    if pos is not None:
+        pos_t = torch.as_tensor(np.atleast_1d(np.asarray(pos, dtype=np.int32)))
+        cache.seq_lens.copy_(pos_t.to(cache.device))
+    if runner is None:
+        if cos is None or sin is None:
+            raise ValueError("cos/sin tables are required (device_rope_tables)")
+        runner = MlaDecodeAttention(cfg, w, cos, sin)
+    out = runner(x_n, cache)
+    return out[0] if squeeze else out

@@ -1,0 +1,253 @@
+// extern "C" entry points of libmla_decode.so (declared in include/mla_decode.h).
+//
+// Host glue that replaces the attention part of the reference's launcher
+// (src/host/fleet_launch.hip): the shape refusal (:573-577), the per-launch
+// argument packing and launch (fleet_kernel.hip:1068-1078) and the error
+// decoding (:284-311). The YaRN tables and softmax scale (:186-219, :564-571)
+// are computed by the caller (the Python host) and passed in.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "mla_common.cuh"
+
+namespace mla {
+cudaError_t launch_prologue(const MlaDecodeParams& p, cudaStream_t stream);
+cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, const CUtensorMap& tmap_q,
+                                float scale_log2, cudaStream_t stream);
+cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream);
+cudaError_t launch_merge_uv(const MlaDecodeParams& p, cudaStream_t stream);
+cudaError_t k2_configure();
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxCtas = 4096;
+
+struct DeviceInfo {
+    std::once_flag once;
+    int status = MLA_E_ARCH;
+    int sm_count = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int device_info(int* sm_count) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MLA_E_LAUNCH;
+    DeviceInfo& d = g_dev[dev];
+    std::call_once(d.once, [&]() {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
+        if (prop.major != 10) { d.status = MLA_E_ARCH; return; }
+        if (k2_configure() != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
+        d.sm_count = prop.multiProcessorCount;
+        d.status = MLA_OK;
+    });
+    if (d.status == MLA_OK && sm_count) *sm_count = d.sm_count;
+    return d.status;
+}
+
+int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+    std::call_once(g_encode_once, []() {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    *fn = g_encode;
+    return g_encode ? MLA_OK : MLA_E_DRIVER;
+}
+
+// 2-D bf16 tensor map: inner dim 576 columns (row pitch 1152 B), outer `rows`,
+// box 64 columns x box_rows rows, 128-byte swizzle.
+int make_tmap_rows576(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn;
+    if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
+    cuuint64_t dims[2] = {(cuuint64_t)kRow, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)kRow * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
+}
+
+bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }
+
+int resolve_ctas(const MlaDecodeParams* p, int* ctas) {
+    if (p->num_ctas < 0 || p->num_ctas > kMaxCtas) return MLA_E_LIMIT;
+    if (p->num_ctas > 0) { *ctas = p->num_ctas; return MLA_OK; }
+    int sms = 0;
+    const int st = device_info(&sms);
+    if (st != MLA_OK) return st;
+    *ctas = sms;
+    return MLA_OK;
+}
+
+int check_header(const MlaDecodeParams* p) {
+    if (!p || p->struct_size != sizeof(MlaDecodeParams) || p->abi_version != MLA_ABI_VERSION)
+        return MLA_E_INVALID_ARG;
+    if (p->heads != MLA_HEADS || p->qk_nope != MLA_QK_NOPE || p->qk_rope != MLA_QK_ROPE ||
+        p->v_head != MLA_V_HEAD || p->kv_lora != MLA_KV_LORA || p->page_size != MLA_PAGE_SIZE)
+        return MLA_E_UNSUPPORTED_DIMS;
+    if (p->batch <= 0) return MLA_E_INVALID_ARG;
+    if (p->batch > MLA_MAX_BATCH) return MLA_E_LIMIT;
+    return MLA_OK;
+}
+
+// Full validation for the launch paths; fills `out` with num_ctas resolved.
+int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
+    int st = check_header(p);
+    if (st != MLA_OK) return st;
+    if (!p->q || !p->kv_a || !p->kv_a_norm_w || !p->kv_b || !p->rope_cos || !p->rope_sin || !p->block_table ||
+        !p->seq_lens || !p->kv_cache || !p->out || !p->workspace)
+        return MLA_E_INVALID_ARG;
+    if (p->max_blocks <= 0 || p->n_pages <= 0 || p->max_pos <= 0) return MLA_E_INVALID_ARG;
+    if ((int64_t)p->n_pages * MLA_PAGE_SIZE > INT32_MAX || (int64_t)p->batch * p->max_blocks > INT32_MAX)
+        return MLA_E_LIMIT;
+    if (p->q_stride < MLA_HEADS * (MLA_QK_NOPE + MLA_QK_ROPE) || p->kv_a_stride < MLA_ROW ||
+        p->out_stride < MLA_HEADS * MLA_V_HEAD)
+        return MLA_E_INVALID_ARG;
+    if (!(p->softmax_scale > 0.f) || !(p->rms_eps >= 0.f)) return MLA_E_INVALID_ARG;
+    if (!aligned(p->kv_cache, 16) || !aligned(p->kv_b, 16) || !aligned(p->workspace, 256) ||
+        !aligned(p->q, 2) || !aligned(p->kv_a, 2) || !aligned(p->out, 2) || !aligned(p->kv_a_norm_w, 2) ||
+        !aligned(p->rope_cos, 4) || !aligned(p->rope_sin, 4))
+        return MLA_E_MISALIGNED;
+    int sms = 0;
+    st = device_info(&sms);
+    if (st != MLA_OK) return st;
+    *out = *p;
+    st = resolve_ctas(p, &out->num_ctas);
+    if (st != MLA_OK) return st;
+    const WsLayout ws = ws_layout(p->batch, out->num_ctas);
+    if (p->workspace_bytes < ws.total) return MLA_E_WORKSPACE;
+    return MLA_OK;
+}
+
+int run_attention(const MlaDecodeParams& q, cudaStream_t s) {
+    const float scale_log2 = (float)((double)q.softmax_scale * 1.4426950408889634);
+    if (q.flags & MLA_FLAG_CHECK_KERNEL) {
+        return launch_attention_check(q, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    }
+    CUtensorMap tkv, tq;
+    int st = make_tmap_rows576(&tkv, q.kv_cache, (uint64_t)q.n_pages * MLA_PAGE_SIZE, 64);
+    if (st != MLA_OK) return st;
+    const WsLayout ws = ws_layout(q.batch, q.num_ctas);
+    st = make_tmap_rows576(&tq, reinterpret_cast<const char*>(q.workspace) + ws.qa, (uint64_t)q.batch * kQRows,
+                           kQRows);
+    if (st != MLA_OK) return st;
+    return launch_attention_tc(q, tkv, tq, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+}  // namespace
+}  // namespace mla
+
+using namespace mla;
+
+extern "C" {
+
+int mla_abi_version(void) { return MLA_ABI_VERSION; }
+
+const char* mla_status_string(int status) {
+    switch (status) {
+        case MLA_OK: return "MLA_OK";
+        case MLA_E_INVALID_ARG: return "MLA_E_INVALID_ARG";
+        case MLA_E_UNSUPPORTED_DIMS: return "MLA_E_UNSUPPORTED_DIMS";
+        case MLA_E_MISALIGNED: return "MLA_E_MISALIGNED";
+        case MLA_E_WORKSPACE: return "MLA_E_WORKSPACE";
+        case MLA_E_ARCH: return "MLA_E_ARCH";
+        case MLA_E_LAUNCH: return "MLA_E_LAUNCH";
+        case MLA_E_DRIVER: return "MLA_E_DRIVER";
+        case MLA_E_LIMIT: return "MLA_E_LIMIT";
+        default: return "MLA_E_UNKNOWN";
+    }
+}
+
+const char* mla_device_error_string(int code) {
+    switch (code) {
+        case MLA_DEV_OK: return "ok";
+        case MLA_DEV_BAD_PAGE: return "block_table entry outside [0, n_pages)";
+        case MLA_DEV_BAD_POSITION: return "seq_lens entry outside the rope table or block table";
+        case MLA_DEV_TIMEOUT: return "on-chip pipeline wait timed out";
+        default: return "unknown device error";
+    }
+}
+
+void mla_params_init(MlaDecodeParams* p) {
+    if (!p) return;
+    *p = MlaDecodeParams{};
+    p->struct_size = sizeof(MlaDecodeParams);
+    p->abi_version = MLA_ABI_VERSION;
+    p->heads = MLA_HEADS;
+    p->qk_nope = MLA_QK_NOPE;
+    p->qk_rope = MLA_QK_ROPE;
+    p->v_head = MLA_V_HEAD;
+    p->kv_lora = MLA_KV_LORA;
+    p->page_size = MLA_PAGE_SIZE;
+    p->rms_eps = 1e-6f;
+}
+
+int mla_workspace_size(const MlaDecodeParams* p, uint64_t* bytes) {
+    if (!bytes) return MLA_E_INVALID_ARG;
+    int st = check_header(p);
+    if (st != MLA_OK) return st;
+    int ctas = 0;
+    st = resolve_ctas(p, &ctas);
+    if (st != MLA_OK) return st;
+    *bytes = ws_layout(p->batch, ctas).total;
+    return MLA_OK;
+}
+
+int mla_plan_info(const MlaDecodeParams* p, int32_t* num_ctas, int32_t* num_slots) {
+    int st = check_header(p);
+    if (st != MLA_OK) return st;
+    int ctas = 0;
+    st = resolve_ctas(p, &ctas);
+    if (st != MLA_OK) return st;
+    if (num_ctas) *num_ctas = ctas;
+    if (num_slots) *num_slots = ws_layout(p->batch, ctas).slots;
+    return MLA_OK;
+}
+
+int mla_launches_per_step(void) { return 3; }
+
+int mla_prologue(const MlaDecodeParams* p, void* stream) {
+    MlaDecodeParams q;
+    int st = prepare(p, &q);
+    if (st != MLA_OK) return st;
+    return launch_prologue(q, (cudaStream_t)stream) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+int mla_attention(const MlaDecodeParams* p, void* stream) {
+    MlaDecodeParams q;
+    int st = prepare(p, &q);
+    if (st != MLA_OK) return st;
+    return run_attention(q, (cudaStream_t)stream);
+}
+
+int mla_merge_uv(const MlaDecodeParams* p, void* stream) {
+    MlaDecodeParams q;
+    int st = prepare(p, &q);
+    if (st != MLA_OK) return st;
+    return launch_merge_uv(q, (cudaStream_t)stream) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+int mla_decode_step(const MlaDecodeParams* p, void* stream) {
+    MlaDecodeParams q;
+    int st = prepare(p, &q);
+    if (st != MLA_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (launch_prologue(q, s) != cudaSuccess) return MLA_E_LAUNCH;
+    st = run_attention(q, s);
+    if (st != MLA_OK) return st;
+    return launch_merge_uv(q, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+}  // extern "C"

@@ -1,0 +1,114 @@
+"""ctypes binding of libmla_decode.so, the C ABI declared in include/mla_decode.h.
+
+The library is the product: there is no Python or CPU implementation behind this
+module. If the shared library is missing, loading fails loudly with the build command.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libmla_decode.so"
+
+ABI_VERSION = 1
+HEADS, QK_NOPE, QK_ROPE, V_HEAD, KV_LORA, PAGE_SIZE = 16, 128, 64, 128, 512, 64
+ROW = KV_LORA + QK_ROPE
+MAX_BATCH = 65536
+
+FLAG_CHECK_KERNEL = 0x2
+
+STATUS = {
+    0: "MLA_OK", -1: "MLA_E_INVALID_ARG", -2: "MLA_E_UNSUPPORTED_DIMS", -3: "MLA_E_MISALIGNED",
+    -4: "MLA_E_WORKSPACE", -5: "MLA_E_ARCH", -6: "MLA_E_LAUNCH", -7: "MLA_E_DRIVER", -8: "MLA_E_LIMIT",
+}
+DEV_ERRORS = {0: "ok", 1: "MLA_DEV_BAD_PAGE", 2: "MLA_DEV_BAD_POSITION", 3: "MLA_DEV_TIMEOUT"}
+
+EXPORTED = (
+    "mla_abi_version", "mla_status_string", "mla_device_error_string", "mla_params_init",
+    "mla_workspace_size", "mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv",
+    "mla_plan_info", "mla_launches_per_step",
+)
+
+
+class MlaError(RuntimeError):
+    """A nonzero mla_status from the C ABI, or a device error word."""
+
+    def __init__(self, code: int, what: str):
+        self.code = code
+        super().__init__(f"{what}: {STATUS.get(code, DEV_ERRORS.get(code, code))} ({code})")
+
+
+class MlaDecodeParams(ctypes.Structure):
+    """Field-for-field mirror of `MlaDecodeParams` in include/mla_decode.h."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("abi_version", ctypes.c_uint32),
+        ("heads", ctypes.c_int32), ("qk_nope", ctypes.c_int32), ("qk_rope", ctypes.c_int32),
+        ("v_head", ctypes.c_int32), ("kv_lora", ctypes.c_int32), ("page_size", ctypes.c_int32),
+        ("softmax_scale", ctypes.c_float), ("rms_eps", ctypes.c_float),
+        ("batch", ctypes.c_int32), ("max_blocks", ctypes.c_int32), ("n_pages", ctypes.c_int32),
+        ("max_pos", ctypes.c_int32),
+        ("q", ctypes.c_void_p), ("q_stride", ctypes.c_int64),
+        ("kv_a", ctypes.c_void_p), ("kv_a_stride", ctypes.c_int64),
+        ("kv_a_norm_w", ctypes.c_void_p), ("kv_b", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p), ("seq_lens", ctypes.c_void_p),
+        ("kv_cache", ctypes.c_void_p),
+        ("out", ctypes.c_void_p), ("out_stride", ctypes.c_int64),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+        ("error_word", ctypes.c_void_p),
+        ("num_ctas", ctypes.c_int32), ("flags", ctypes.c_int32),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library(path: Path | str | None = None) -> ctypes.CDLL:
+    """Load libmla_decode.so (once) and declare the prototypes."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"{p} is missing: build it with `python fleet-mi300x_b200/build.py` "
+                "(nvcc, sm_100a). There is no fallback implementation.")
+        lib = ctypes.CDLL(str(p))
+        P = ctypes.POINTER(MlaDecodeParams)
+        lib.mla_abi_version.restype = ctypes.c_int
+        lib.mla_status_string.restype = ctypes.c_char_p
+        lib.mla_status_string.argtypes = [ctypes.c_int]
+        lib.mla_device_error_string.restype = ctypes.c_char_p
+        lib.mla_device_error_string.argtypes = [ctypes.c_int]
+        lib.mla_params_init.restype = None
+        lib.mla_params_init.argtypes = [P]
+        lib.mla_workspace_size.restype = ctypes.c_int
+        lib.mla_workspace_size.argtypes = [P, ctypes.POINTER(ctypes.c_uint64)]
+        lib.mla_plan_info.restype = ctypes.c_int
+        lib.mla_plan_info.argtypes = [P, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]
+        lib.mla_launches_per_step.restype = ctypes.c_int
+        for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv"):
+            f = getattr(lib, fn)
+            f.restype = ctypes.c_int
+            f.argtypes = [P, ctypes.c_void_p]
+        if lib.mla_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"{p}: ABI version {lib.mla_abi_version()} != {ABI_VERSION}")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        raise MlaError(code, what)
+
+
+def new_params() -> MlaDecodeParams:
+    p = MlaDecodeParams()
+    load_library().mla_params_init(ctypes.byref(p))
+    return p

@@ -1,0 +1,164 @@
+/*
+ * mla_decode.h — C ABI of the B200 (sm_100a) absorbed-MLA decode-attention path.
+ *
+ * This library is a drop-in for the attention task of the reference's
+ * task-by-task decode: reference_decode.py:attention_absorbed
+ * (src/host/reference_decode.py:210-256), restricted to the slice between the
+ * input RMSNorm (:222) and o_proj (:256). Inputs are the q / kv_a projections
+ * of the post-RMSNorm hidden state (:225-231); the output is the
+ * head-concatenated, bf16-rounded attention result R(out) before o_proj (:256).
+ *
+ * On the device the reference runs this slice as three task kinds inside its
+ * persistent kernel (src/kernels/fleet_kernel.hip:647-654 TASK_Q_ABSORB,
+ * :745-798 TASK_ATTENTION, :694-701 TASK_MERGE_UV), launched through
+ * `extern "C" hipError_t fleet_launch_step(...)` (fleet_kernel.hip:1068-1078).
+ * Here the same work is three stream-ordered kernels behind plain C entry
+ * points: pointers, sizes and a caller-provided workspace; no allocation, no
+ * torch types, no global mutable state except a per-device attribute cache.
+ *
+ * Layouts (all device memory, row-major):
+ *   q            bf16 [batch][q_stride]      head h: [192h, 192h+128) q_nope, [192h+128, 192h+192) q_pe
+ *   kv_a         bf16 [batch][kv_a_stride]   [0,512) c_new (raw), [512,576) k_pe_new (raw)
+ *   kv_a_norm_w  bf16 [512]                  kv_a_layernorm.weight
+ *   kv_b         bf16 [16*256][512]          kv_b_proj.weight: head h rows [256h,256h+128) = W_UK,
+ *                                            [256h+128, 256h+256) = W_UV (reference_decode.py:242-248)
+ *   rope_cos/sin f32  [max_pos][64]          YaRN tables (reference_decode.py:102-117)
+ *   kv_cache     bf16 [n_pages][64][576]     paged latent cache: row = c_kv(512) | k_pe(64)
+ *   block_table  i32  [batch][max_blocks]    page ids of each request's logical pages
+ *   seq_lens     i32  [batch]                rows cached before this step = position of the new token
+ *   out          bf16 [batch][out_stride]    R(out): head h at [128h, 128h+128)
+ *
+ * One call appends each request's new row at position seq_lens[b] (the
+ * reference's in-place `cache[pos] = ...`, reference_decode.py:236-237) and
+ * attends over rows 0..seq_lens[b] inclusive. It does not advance seq_lens;
+ * the caller does, exactly as the reference's caller advances `pos`.
+ */
+#ifndef MLA_DECODE_H_
+#define MLA_DECODE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLA_ABI_VERSION 1
+
+/* Fixed model dimensions. The reference's launcher refuses any other shape
+ * (src/host/fleet_launch.hip:573-577: kv_lora != 512 or qk_rope != 64);
+ * these kernels refuse the same way, with MLA_E_UNSUPPORTED_DIMS. */
+#define MLA_HEADS 16
+#define MLA_QK_NOPE 128
+#define MLA_QK_ROPE 64
+#define MLA_V_HEAD 128
+#define MLA_KV_LORA 512
+#define MLA_PAGE_SIZE 64
+#define MLA_ROW (MLA_KV_LORA + MLA_QK_ROPE)
+
+/* Host-side status codes (return values). The reference's launcher dies with
+ * a message on bad shapes (fleet_launch.hip:573-577) and returns hipError_t
+ * from the launch (fleet_kernel.hip:1068-1078); here every entry point
+ * returns one of these instead of exiting. */
+typedef enum {
+    MLA_OK = 0,
+    MLA_E_INVALID_ARG = -1,      /* null pointer, bad struct size/version, batch <= 0 */
+    MLA_E_UNSUPPORTED_DIMS = -2, /* dims other than 16/128/64/128/512, page size != 64 */
+    MLA_E_MISALIGNED = -3,       /* a pointer or stride breaks the 16-byte rule of TMA/vector loads */
+    MLA_E_WORKSPACE = -4,        /* workspace missing or smaller than mla_workspace_size() */
+    MLA_E_ARCH = -5,             /* current device is not sm_100 */
+    MLA_E_LAUNCH = -6,           /* a CUDA launch/attribute call failed */
+    MLA_E_DRIVER = -7,           /* cuTensorMapEncodeTiled unavailable or failed */
+    MLA_E_LIMIT = -8             /* a size exceeds a documented limit (batch, pages, positions) */
+} mla_status;
+
+/* Device-side error codes, written to *error_word (first error wins, by
+ * atomicCAS). The reference decodes its abort word the same way
+ * (fleet_runtime.h:194-198, describe_abort in fleet_launch.hip:284-311). */
+#define MLA_DEV_OK 0
+#define MLA_DEV_BAD_PAGE 1      /* block_table entry outside [0, n_pages) */
+#define MLA_DEV_BAD_POSITION 2  /* seq_lens[b] >= max_pos or >= max_blocks * 64, or < 0 */
+#define MLA_DEV_TIMEOUT 3       /* a bounded on-chip wait gave up (pipeline stall) */
+
+/* Flags. */
+#define MLA_FLAG_CHECK_KERNEL 0x2 /* run the CUDA-core split-KV kernel instead of the tensor-core one
+                                     (same plan and partial layout, fp32 probabilities; it exists to
+                                     cross-check the tensor-core kernel, not as a fallback) */
+
+typedef struct MlaDecodeParams {
+    uint32_t struct_size; /* sizeof(MlaDecodeParams) */
+    uint32_t abi_version; /* MLA_ABI_VERSION */
+
+    /* dims: must equal the MLA_* constants above */
+    int32_t heads, qk_nope, qk_rope, v_head, kv_lora, page_size;
+    float softmax_scale; /* q_head_dim^-0.5 * mscale^2 (reference_decode.py:197-203) */
+    float rms_eps;       /* kv_a_layernorm eps (1e-6) */
+
+    int32_t batch;      /* requests in this call, 1..MLA_MAX_BATCH */
+    int32_t max_blocks; /* row stride of block_table */
+    int32_t n_pages;    /* pages in kv_cache */
+    int32_t max_pos;    /* rows of rope_cos / rope_sin */
+
+    const void* q;        int64_t q_stride;    /* elements between rows */
+    const void* kv_a;     int64_t kv_a_stride; /* elements between rows */
+    const void* kv_a_norm_w;
+    const void* kv_b;
+    const float* rope_cos;
+    const float* rope_sin;
+    const int32_t* block_table;
+    const int32_t* seq_lens;
+    void* kv_cache;
+    void* out;            int64_t out_stride;  /* elements between rows */
+
+    void* workspace;          /* device scratch, >= mla_workspace_size() bytes, 256-byte aligned */
+    uint64_t workspace_bytes;
+    int32_t* error_word;      /* optional device int32 (0 = no error); may be NULL */
+    int32_t num_ctas;         /* CTAs of the split-KV kernel; 0 = one per SM */
+    int32_t flags;            /* MLA_FLAG_* */
+} MlaDecodeParams;
+
+#define MLA_MAX_BATCH 65536
+
+/* ABI version of the loaded library (MLA_ABI_VERSION). */
+int mla_abi_version(void);
+
+/* Human-readable name of an mla_status / device error code. */
+const char* mla_status_string(int status);
+const char* mla_device_error_string(int code);
+
+/* Fill a params struct with the fixed dims, scale 0 and no pointers. */
+void mla_params_init(MlaDecodeParams* p);
+
+/* Bytes of workspace a call with these params needs (depends on batch and
+ * num_ctas only). Replaces the reference's host-side buffer plan
+ * (fleet_types.h:75-81 Activations.q_absorbed/attn_partial; dev_alloc in
+ * fleet_launch.hip:223-237): the caller allocates, the library never does. */
+int mla_workspace_size(const MlaDecodeParams* p, uint64_t* bytes);
+
+/* Whole attention task: K1 (kv_post + q RoPE + W_UK absorb + split plan),
+ * K2 (split-KV attention) and K3 (LSE merge + W_UV), stream-ordered on
+ * `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Replaces TASK_Q_ABSORB + TASK_ATTENTION + TASK_MERGE_UV as run by
+ * fleet_launch_step (fleet_kernel.hip:647-654, :745-798, :694-701, :1068-1078). */
+int mla_decode_step(const MlaDecodeParams* p, void* stream);
+
+/* The three stages one by one (same params; each expects the previous one's
+ * workspace contents). K1 = kv_post (attention.h:62-90) + q_absorb
+ * (attention.h:171-216); K2 = attention_chunk (attention.h:230-351);
+ * K3 = merge_and_uv (attention.h:358-411). */
+int mla_prologue(const MlaDecodeParams* p, void* stream);
+int mla_attention(const MlaDecodeParams* p, void* stream);
+int mla_merge_uv(const MlaDecodeParams* p, void* stream);
+
+/* Split plan as used by the last K2/K3 of these params, for inspection:
+ * number of CTAs that get work and number of partial slots. Host only. */
+int mla_plan_info(const MlaDecodeParams* p, int32_t* num_ctas, int32_t* num_slots);
+
+/* Number of kernel launches one mla_decode_step makes (for launch accounting). */
+int mla_launches_per_step(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLA_DECODE_H_ */

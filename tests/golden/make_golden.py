@@ -1,0 +1,148 @@
+"""Generate tests/golden/*.npz from the reference's own NumPy implementation.
+
+Run in the build container, where the reference tree is mounted read-only:
+
+    python tests/golden/make_golden.py --reference <path to cklxx/fleet-mi300x>
+
+It imports src/host/reference_decode.py from the reference and runs its
+`attention_absorbed` (src/host/reference_decode.py:210-256) on seeded inputs drawn
+by fleet-mi300x_b200/workloads.py. o_proj is set to the identity and the input
+RMSNorm weight to ones, so the function returns R(out), the head-concatenated bf16
+output before o_proj that the B200 path produces; the post-RMSNorm input it saw is
+recorded as x_n. Large inputs (weights, cache rows) are not stored: the fixture keeps
+their seeds and SHA-256 digests, and the tests regenerate and verify them.
+Nothing on the GPU box reads the reference tree; only this script does.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import importlib
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+fleet = importlib.import_module("fleet-mi300x_b200")
+workloads = importlib.import_module("fleet-mi300x_b200.workloads")
+
+OUT = Path(__file__).resolve().parent
+
+
+def sha(t) -> str:
+    if isinstance(t, torch.Tensor):
+        t = t.contiguous().view(torch.uint8).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+    return hashlib.sha256(np.ascontiguousarray(t).tobytes()).hexdigest()
+
+
+def f32(t: torch.Tensor) -> np.ndarray:
+    return t.float().numpy()
+
+
+def dsv2_case(ref, name: str, T: int, steps: int, w_seed: int, c_seed: int, x_seed: int) -> dict:
+    cfg = ref.ModelConfig(hidden=2048, heads=16, kv_lora_rank=512, qk_nope=128, qk_rope=64, v_head=128,
+                          moe_inter=1408, n_routed=64, top_k=6, bf16=True)
+    max_pos = T + steps + 8
+    cos, sin = ref.yarn_cos_sin(64, max_pos, cfg.rope_theta, cfg.rope_factor, cfg.rope_original_max,
+                                cfg.beta_fast, cfg.beta_slow, cfg.mscale, cfg.mscale_all_dim)
+    lw = workloads.make_layer_weights(w_seed, norm="uniform")
+    rows = workloads.make_cache_rows(c_seed, T, torch.from_numpy(cos), torch.from_numpy(sin), normed=True)
+    x_raw = workloads.make_hidden(x_seed, steps)  # bf16 N(0,1) rows, normalised once more by the reference
+    w = ref.LayerWeights(
+        input_layernorm=np.ones(2048, np.float32), q_proj=f32(lw.q_proj),
+        kv_a_proj_with_mqa=f32(lw.kv_a_proj_with_mqa), kv_a_layernorm=f32(lw.kv_a_layernorm),
+        kv_b_proj=f32(lw.kv_b_proj), o_proj=np.eye(2048, dtype=np.float32),
+        post_attention_layernorm=np.ones(2048, np.float32))
+    cache = np.zeros((max_pos, 576), np.float32)
+    cache[:T] = f32(rows)
+    xs, qs, kvas, outs, new_rows = [], [], [], [], []
+    for s in range(steps):
+        pos = T + s
+        x = f32(x_raw[s])
+        x_n = ref.rms_norm(x, w.input_layernorm, cfg.rms_eps, cfg.bf16)
+        # the reference's own q / kv_a expressions (reference_decode.py:225, 229)
+        q = cfg.r(w.q_proj @ x_n)
+        kv_a = cfg.r(w.kv_a_proj_with_mqa @ x_n)
+        out = ref.attention_absorbed(cfg, w, x, cache, pos, cos, sin)
+        xs.append(x_n); qs.append(q); kvas.append(kv_a); outs.append(out); new_rows.append(cache[pos].copy())
+    return {
+        f"{name}/T": np.int64(T), f"{name}/steps": np.int64(steps),
+        f"{name}/seeds": np.array([w_seed, c_seed, x_seed], np.int64),
+        f"{name}/x_n": np.stack(xs), f"{name}/q": np.stack(qs), f"{name}/kv_a": np.stack(kvas),
+        f"{name}/out": np.stack(outs), f"{name}/new_rows": np.stack(new_rows),
+        f"{name}/sha_weights": np.array(sha(lw.q_proj) + sha(lw.kv_a_proj_with_mqa) + sha(lw.kv_a_layernorm)
+                                        + sha(lw.kv_b_proj)),
+        f"{name}/sha_rows": np.array(sha(rows)),
+    }
+
+
+def tiny_case(ref) -> dict:
+    """The reference's tiny HF-comparison config (tests/test_reference_vs_hf.py:67-102):
+    hidden 64, 4 heads, kv_lora 16, nope 16, rope 8, v 16, YaRN orig 32; 12 tokens walked
+    through an initially empty cache, bf16 rounding points on."""
+    cfg = ref.ModelConfig(hidden=64, heads=4, kv_lora_rank=16, qk_nope=16, qk_rope=8, v_head=16,
+                          moe_inter=32, n_routed=8, top_k=2, rope_original_max=32, bf16=True)
+    g = torch.Generator().manual_seed(21)
+    def rnd(*shape, std=0.05):
+        return (torch.randn(*shape, generator=g) * std).to(torch.bfloat16).float().numpy()
+    w = ref.LayerWeights(
+        input_layernorm=np.ones(64, np.float32), q_proj=rnd(4 * 24, 64), kv_a_proj_with_mqa=rnd(24, 64),
+        kv_a_layernorm=(torch.rand(16, generator=g) * 0.4 + 0.8).to(torch.bfloat16).float().numpy(),
+        kv_b_proj=rnd(4 * 32, 16), o_proj=np.eye(64, dtype=np.float32),
+        post_attention_layernorm=np.ones(64, np.float32))
+    S = 12
+    x = (torch.randn(S, 64, generator=g) * 0.5).to(torch.bfloat16).float().numpy()
+    cos, sin = ref.yarn_cos_sin(8, S, cfg.rope_theta, cfg.rope_factor, cfg.rope_original_max,
+                                cfg.beta_fast, cfg.beta_slow, cfg.mscale, cfg.mscale_all_dim)
+    cache = np.zeros((S, 24), np.float32)
+    xs, outs = [], []
+    for t in range(S):
+        xs.append(ref.rms_norm(x[t], w.input_layernorm, cfg.rms_eps, True))
+        outs.append(ref.attention_absorbed(cfg, w, x[t], cache, t, cos, sin))
+    return {"tiny/x_n": np.stack(xs), "tiny/out": np.stack(outs), "tiny/cache": cache,
+            "tiny/q_proj": w.q_proj, "tiny/kv_a": w.kv_a_proj_with_mqa, "tiny/kv_a_ln": w.kv_a_layernorm,
+            "tiny/kv_b": w.kv_b_proj}
+
+
+def known_answers(ref) -> dict:
+    cfg = ref.ModelConfig(hidden=2048, heads=16, kv_lora_rank=512, qk_nope=128, qk_rope=64, v_head=128,
+                          moe_inter=1408, n_routed=64, top_k=6)
+    positions = np.array([0, 1, 5, 100, 1023, 4095, 32768, 131072], np.int64)
+    cos, sin = ref.yarn_cos_sin(64, int(positions.max()) + 1, cfg.rope_theta, cfg.rope_factor,
+                                cfg.rope_original_max, cfg.beta_fast, cfg.beta_slow, cfg.mscale,
+                                cfg.mscale_all_dim)
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4, 64, generator=g).numpy()
+    roped = ref.apply_rope(x, cos[5][None, :], sin[5][None, :])
+    vals = (torch.randn(4096, generator=g) * 3).numpy().astype(np.float32)
+    return {
+        "ka/softmax_scale": np.float64(cfg.softmax_scale),
+        "ka/mscale": np.float64(ref.yarn_get_mscale(40.0, 0.707)),
+        "ka/rope_positions": positions, "ka/cos": cos[positions], "ka/sin": sin[positions],
+        "ka/rope_x": x, "ka/rope_out": roped,
+        "ka/bf16_in": vals, "ka/bf16_out": ref.bf16_round(vals),
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference", help="path of the cklxx/fleet-mi300x tree")
+    a = ap.parse_args()
+    sys.path.insert(0, str(Path(a.reference) / "src" / "host"))
+    ref = importlib.import_module("reference_decode")
+    data = {}
+    data.update(known_answers(ref))
+    data.update(tiny_case(ref))
+    data.update(dsv2_case(ref, "t37", T=37, steps=2, w_seed=11, c_seed=12, x_seed=13))
+    data.update(dsv2_case(ref, "config1", T=1024, steps=1, w_seed=1, c_seed=2, x_seed=3))
+    data.update(dsv2_case(ref, "walk", T=126, steps=4, w_seed=21, c_seed=22, x_seed=23))
+    np.savez_compressed(OUT / "golden_mla.npz", **data)
+    print(f"wrote {OUT / 'golden_mla.npz'} ({len(data)} arrays)")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
