@@ -21,6 +21,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libmla_decode.so"
+TRACE_LIB = PKG / "libmla_decode_trace.so"  # -DMLA_TRACE: per-tile clock stamps of the attention kernel
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -36,42 +37,46 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
-def stale() -> bool:
-    if not LIB.exists():
+def stale(lib: Path = LIB) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     deps = sources() + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h")) + [Path(__file__)]
     return any(p.stat().st_mtime > t for p in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not stale():
-        return LIB
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
+    lib = TRACE_LIB if trace else LIB
+    if not force and not stale(lib):
+        return lib
     cmd = [
         nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
         "-Xcompiler", "-fPIC", "-shared",
         f"-I{INCLUDE}", f"-I{CSRC}",
-        "-o", str(LIB) + ".tmp",
+        "-o", str(lib) + ".tmp",
         *[str(s) for s in sources()],
     ]
+    if trace:
+        cmd.insert(1, "-DMLA_TRACE")
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         sys.stderr.write(proc.stdout + proc.stderr)
-        raise RuntimeError(f"nvcc failed ({proc.returncode}) building {LIB.name}")
+        raise RuntimeError(f"nvcc failed ({proc.returncode}) building {lib.name}")
     if verbose:
         sys.stdout.write(proc.stdout + proc.stderr)
-    os.replace(str(LIB) + ".tmp", LIB)
-    return LIB
+    os.replace(str(lib) + ".tmp", lib)
+    return lib
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="build libmla_decode_trace.so with -DMLA_TRACE")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose, trace=a.trace))
     return 0
 
 

@@ -19,6 +19,7 @@ cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tma
 cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream);
 cudaError_t launch_merge_uv(const MlaDecodeParams& p, cudaStream_t stream);
 cudaError_t k2_configure();
+cudaError_t k3_configure();
 
 namespace {
 
@@ -43,7 +44,7 @@ int device_info(int* sm_count) {
         cudaDeviceProp prop;
         if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
         if (prop.major != 10) { d.status = MLA_E_ARCH; return; }
-        if (k2_configure() != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
+        if (k2_configure() != cudaSuccess || k3_configure() != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
         d.sm_count = prop.multiProcessorCount;
         d.status = MLA_OK;
     });
@@ -64,17 +65,21 @@ int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* fn) {
     return g_encode ? MLA_OK : MLA_E_DRIVER;
 }
 
-// 2-D bf16 tensor map: inner dim 576 columns (row pitch 1152 B), outer `rows`,
-// box 64 columns x box_rows rows, 128-byte swizzle.
-int make_tmap_rows576(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows) {
+// bf16 tensor maps over 576-wide rows (1152 B pitch) that land in shared
+// memory as 9 column blocks of [rows x 64] with the 128-byte swizzle:
+// dims {64 columns, rows (pitch 1152 B), 9 blocks (pitch 128 B)[, pages]}.
+// The page map (rank 4) serves one whole 64-row page per request; the
+// query map (rank 3) one request's 16 absorbed-query rows.
+int make_tmap_blocks(CUtensorMap* m, const void* base, uint64_t rows_or_pages, bool paged) {
     PFN_cuTensorMapEncodeTiled_v12000 fn;
     if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
-    cuuint64_t dims[2] = {(cuuint64_t)kRow, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)kRow * 2};
-    cuuint32_t box[2] = {64, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const cuuint32_t rank = paged ? 4 : 3;
+    cuuint64_t dims[4] = {64, paged ? (cuuint64_t)kPage : (cuuint64_t)rows_or_pages, 9, (cuuint64_t)rows_or_pages};
+    cuuint64_t strides[3] = {(cuuint64_t)kRow * 2, 128, (cuuint64_t)kPage * kRow * 2};
+    cuuint32_t box[4] = {64, paged ? (cuuint32_t)kPage : (cuuint32_t)kQRows, 9, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
 }
@@ -117,7 +122,7 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         return MLA_E_INVALID_ARG;
     if (!(p->softmax_scale > 0.f) || !(p->rms_eps >= 0.f)) return MLA_E_INVALID_ARG;
     if (!aligned(p->kv_cache, 16) || !aligned(p->kv_b, 16) || !aligned(p->workspace, 256) ||
-        !aligned(p->q, 2) || !aligned(p->kv_a, 2) || !aligned(p->out, 2) || !aligned(p->kv_a_norm_w, 2) ||
+        !aligned(p->q, 4) || (p->q_stride & 1) || !aligned(p->kv_a, 2) || !aligned(p->out, 2) || !aligned(p->kv_a_norm_w, 2) ||
         !aligned(p->rope_cos, 4) || !aligned(p->rope_sin, 4))
         return MLA_E_MISALIGNED;
     int sms = 0;
@@ -137,11 +142,10 @@ int run_attention(const MlaDecodeParams& q, cudaStream_t s) {
         return launch_attention_check(q, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
     }
     CUtensorMap tkv, tq;
-    int st = make_tmap_rows576(&tkv, q.kv_cache, (uint64_t)q.n_pages * MLA_PAGE_SIZE, 64);
+    int st = make_tmap_blocks(&tkv, q.kv_cache, (uint64_t)q.n_pages, true);
     if (st != MLA_OK) return st;
     const WsLayout ws = ws_layout(q.batch, q.num_ctas);
-    st = make_tmap_rows576(&tq, reinterpret_cast<const char*>(q.workspace) + ws.qa, (uint64_t)q.batch * kQRows,
-                           kQRows);
+    st = make_tmap_blocks(&tq, reinterpret_cast<const char*>(q.workspace) + ws.qa, (uint64_t)q.batch * kQRows, false);
     if (st != MLA_OK) return st;
     return launch_attention_tc(q, tkv, tq, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
@@ -251,3 +255,4 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream) {
 }
 
 }  // extern "C"
+

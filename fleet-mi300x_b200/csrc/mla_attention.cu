@@ -35,24 +35,31 @@
 namespace mla {
 
 constexpr int kK2Threads = 192;
-constexpr int kNPair = 10;                   // ring of 16 KB slots: 64 tokens x 128 latent columns
-constexpr int kNKpe = 3;                     // ring of 8 KB slots: 64 tokens x 64 rope columns
-constexpr int kPairBytes = 16384;
-constexpr int kSubBytes = 8192;              // one 64x64 bf16 swizzled box
+constexpr int kNTile = 2;                    // ring of whole-page tiles (one TMA request each)
+constexpr int kChunkBytes = 8192;            // one [64 tokens x 64 columns] bf16 swizzled block
+constexpr int kTileBytes = 9 * kChunkBytes;  // a page: 9 column blocks (8 of c_kv, 1 of k_pe)
 constexpr int kQChunkBytes = kQRows * 128;   // 16 rows x 128 B
 constexpr int kQBytes = 9 * kQChunkBytes;    // 18 KB
+constexpr int kNQ = 2;                       // absorbed-query buffers (one per segment in flight)
 constexpr int kPBytes = kHeads * 128;        // 16 heads x 64 tokens bf16
-constexpr int kTmemCols = 128;               // S: 2 x 16 cols, O: 4 x 16 cols
-constexpr int kTmemS = 0;
-constexpr int kTmemO = 32;
+// TMEM columns: S (scores) double-buffered, each buffer 4 partial sums x 16
+// heads (independent accumulation chains, summed by the softmax); O: 4 latent
+// blocks x 16 heads.
+constexpr int kSParts = 4;
+constexpr int kTmemCols = 256;
+constexpr int kTmemS = 0;                     // + 64 * buffer + 16 * part
+constexpr int kTmemO = 2 * kSParts * 16;      // 128
+
+#ifdef MLA_TRACE
+__device__ long long g_mla_trace[kTraceCtas * kTraceTiles * kTraceEvents];
+#endif
 
 constexpr uint32_t kIdescQK = idesc_bf16_f32(64, 16, 0, 0);   // A = C tile (K-major), B = Qa (K-major)
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 16, 1, 0);  // A = C tile (MN-major), B = P (K-major)
 
 struct K2Smem {
-    uint64_t pair_full[kNPair], pair_empty[kNPair];
-    uint64_t kpe_full[kNKpe], kpe_empty[kNKpe];
-    uint64_t q_full, q_empty;
+    uint64_t tile_full[kNTile], tile_empty[kNTile];
+    uint64_t q_full[kNQ], q_empty[kNQ];
     uint64_t s_full[2], p_full[2], pv_done[2];
     uint64_t o_empty, teardown;
     uint32_t tmem_base;
@@ -61,12 +68,12 @@ struct K2Smem {
     float lred[4][16];
 };
 
-constexpr int kOffPair = 0;
-constexpr int kOffKpe = kOffPair + kNPair * kPairBytes;
-constexpr int kOffQ = kOffKpe + kNKpe * kSubBytes;
-constexpr int kOffP = kOffQ + kQBytes;
+constexpr int kOffTile = 0;
+constexpr int kOffQ = kOffTile + kNTile * kTileBytes;
+constexpr int kOffP = kOffQ + kNQ * kQBytes;
 constexpr int kOffMisc = kOffP + 2 * kPBytes;
 constexpr int kK2SmemBytes = kOffMisc + (int)sizeof(K2Smem) + 1024;  // + alignment slack
+static_assert(kK2SmemBytes <= 232448, "K2 shared memory exceeds 227 KB");
 
 // Walks the tiles [u_begin, u_end) of one CTA in order, tracking the request
 // and the segment (run of tiles of one request). All roles walk it alike.
@@ -154,8 +161,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     K2Smem& S = *reinterpret_cast<K2Smem*>(smem + kOffMisc);
-    uint8_t* pair_s = smem + kOffPair;
-    uint8_t* kpe_s = smem + kOffKpe;
+    uint8_t* tile_s = smem + kOffTile;
     uint8_t* q_s = smem + kOffQ;
     uint8_t* p_s = smem + kOffP;
 
@@ -174,9 +180,8 @@ __global__ void __launch_bounds__(kK2Threads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kNPair; ++i) { mbar_init(&S.pair_full[i], 1); mbar_init(&S.pair_empty[i], 1); }
-        for (int i = 0; i < kNKpe; ++i) { mbar_init(&S.kpe_full[i], 1); mbar_init(&S.kpe_empty[i], 1); }
-        mbar_init(&S.q_full, 1); mbar_init(&S.q_empty, 1);
+        for (int i = 0; i < kNTile; ++i) { mbar_init(&S.tile_full[i], 1); mbar_init(&S.tile_empty[i], 1); }
+        for (int i = 0; i < kNQ; ++i) { mbar_init(&S.q_full[i], 1); mbar_init(&S.q_empty[i], 1); }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&S.s_full[i], 1); mbar_init(&S.p_full[i], 128); mbar_init(&S.pv_done[i], 1);
         }
@@ -197,118 +202,134 @@ __global__ void __launch_bounds__(kK2Threads, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
+        // One TMA request per 64-token page (4-D box {64, 64, 9, 1}: 72 KB,
+        // landing as 9 swizzled [64 x 64] column blocks), and one per
+        // segment for the absorbed query (3-D box {64, 16, 9}: 18 KB).
         if (lane == 0) {
-            uint32_t pair_fill = 0, kpe_fill = 0;
+            uint32_t t = 0;
             int q_fill = 0;
             bool ok = true;
-            for (; cur.valid() && ok; cur.next()) {
+            for (; cur.valid() && ok; cur.next(), ++t) {
+                MLA_STAMP((int)t, 0);
                 if (cur.first()) {
-                    if (q_fill > 0 && !(ok = mbar_wait(&S.q_empty, (q_fill - 1) & 1, abort, p.error_word))) break;
-                    mbar_arrive_expect_tx(&S.q_full, kQBytes);
-                    for (int ch = 0; ch < 9; ++ch)
-                        tma_load_2d(q_s + ch * kQChunkBytes, &tmap_q, &S.q_full, 64 * ch, cur.b * kQRows,
-                                    kCacheEvictLast);
+                    const int qs = q_fill % kNQ, n = q_fill / kNQ;
+                    if (n > 0 && !(ok = mbar_wait(&S.q_empty[qs], (n - 1) & 1, abort, p.error_word))) break;
+                    mbar_arrive_expect_tx(&S.q_full[qs], kQBytes);
+                    tma_load_3d(q_s + qs * kQBytes, &tmap_q, &S.q_full[qs], 0, cur.b * kQRows, 0, kCacheEvictLast);
                     ++q_fill;
                 }
                 int page = p.block_table[(int64_t)cur.b * p.max_blocks + cur.page_index()];
                 if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
-                const int row = page * kPage;
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t slot = pair_fill % kNPair, n = pair_fill / kNPair;
-                    if (n > 0 && !(ok = mbar_wait(&S.pair_empty[slot], (n - 1) & 1, abort, p.error_word))) break;
-                    mbar_arrive_expect_tx(&S.pair_full[slot], kPairBytes);
-                    uint8_t* dst = pair_s + slot * kPairBytes;
-                    tma_load_2d(dst, &tmap_kv, &S.pair_full[slot], 128 * j, row, kCacheEvictFirst);
-                    tma_load_2d(dst + kSubBytes, &tmap_kv, &S.pair_full[slot], 128 * j + 64, row, kCacheEvictFirst);
-                    ++pair_fill;
-                }
-                if (!ok) break;
-                {
-                    const uint32_t slot = kpe_fill % kNKpe, n = kpe_fill / kNKpe;
-                    if (n > 0 && !(ok = mbar_wait(&S.kpe_empty[slot], (n - 1) & 1, abort, p.error_word))) break;
-                    mbar_arrive_expect_tx(&S.kpe_full[slot], kSubBytes);
-                    tma_load_2d(kpe_s + slot * kSubBytes, &tmap_kv, &S.kpe_full[slot], kLora, row, kCacheEvictFirst);
-                    ++kpe_fill;
-                }
+                const uint32_t slot = t % kNTile, n = t / kNTile;
+                if (n > 0 && !(ok = mbar_wait(&S.tile_empty[slot], (n - 1) & 1, abort, p.error_word))) break;
+                mbar_arrive_expect_tx(&S.tile_full[slot], kTileBytes);
+                tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.tile_full[slot], 0, 0, 0, page, kCacheEvictFirst);
+                MLA_STAMP((int)t, 1);
             }
             // Drain: every issued copy must land before the CTA's shared memory is released.
-            for (uint32_t s = 0; s < kNPair; ++s) {
-                const uint32_t fills = pair_fill / kNPair + (s < pair_fill % kNPair ? 1u : 0u);
-                if (fills) mbar_drain(&S.pair_full[s], (fills - 1) & 1, p.error_word);
+            for (uint32_t sl = 0; sl < kNTile; ++sl) {
+                const uint32_t fills = t / kNTile + (sl < t % kNTile ? 1u : 0u);
+                if (fills) mbar_drain(&S.tile_full[sl], (fills - 1) & 1, p.error_word);
             }
-            for (uint32_t s = 0; s < kNKpe; ++s) {
-                const uint32_t fills = kpe_fill / kNKpe + (s < kpe_fill % kNKpe ? 1u : 0u);
-                if (fills) mbar_drain(&S.kpe_full[s], (fills - 1) & 1, p.error_word);
+            for (int qs = 0; qs < kNQ; ++qs) {
+                const int fills = q_fill / kNQ + (qs < q_fill % kNQ ? 1 : 0);
+                if (fills) mbar_drain(&S.q_full[qs], (fills - 1) & 1, p.error_word);
             }
-            if (q_fill) mbar_drain(&S.q_full, (q_fill - 1) & 1, p.error_word);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // Event-driven: polls (non-blocking) for the next output MMA (P of the
+        // oldest tile ready) and the next score MMA (its page landed), output
+        // first. S is double-buffered, so the score MMA of tile j may run
+        // ahead of the output MMA of tile j-2 only.
         if (lane == 0) {
-            const uint32_t q_addr = smem_u32(q_s), p_addr = smem_u32(p_s);
-            const uint32_t pair_addr = smem_u32(pair_s), kpe_addr = smem_u32(kpe_s);
-            bool ok = true;
-            int i = 0;
-            bool prev_first = false;  // segment flags of tile i-1 (for its PV)
-            int prev_seg = 0;
-            auto do_pv = [&](int t, bool first, int seg) -> bool {
-                if (!mbar_wait(&S.p_full[t & 1], (t >> 1) & 1, abort, p.error_word)) return false;
+            const uint32_t q_addr = smem_u32(q_s), p_addr = smem_u32(p_s), tile_addr = smem_u32(tile_s);
+            // Descriptors differ only in the start-address field: build the
+            // constant high part once and add (address >> 4).
+            const uint64_t dK = smem_desc_sw128(0, 16, 1024);          // K-major, 8-row groups 1024 B apart
+            const uint64_t dMN = smem_desc_sw128(0, kChunkBytes, 1024);  // MN-major, 64-column blocks 8 KB apart
+            const int n_tiles = (int)(u_end - u_begin);
+            struct TileInfo { bool first, last; int seg; };
+            TileInfo info[4];
+            int qk_j = 0, pv_next = 0;
+
+            auto pv_step = [&]() -> bool {
+                if (!mbar_test_wait(&S.p_full[pv_next & 1], (pv_next >> 1) & 1)) return false;
+                const TileInfo ti = info[pv_next & 3];
+                if (ti.first && ti.seg > 0 && !mbar_test_wait(&S.o_empty, (ti.seg - 1) & 1)) return false;
                 tc_fence_after();
-                if (first && seg > 0) {
-                    if (!mbar_wait(&S.o_empty, (seg - 1) & 1, abort, p.error_word)) return false;
-                    tc_fence_after();
-                }
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t slot = (uint32_t)(4 * t + j) % kNPair;
-                    const uint32_t a0 = pair_addr + slot * kPairBytes;
+                const int t = pv_next;
+                MLA_STAMP(t, 4);
+                const uint32_t a0 = tile_addr + (uint32_t)(t % kNTile) * kTileBytes;
+                const uint32_t b0 = p_addr + (t & 1) * kPBytes;
+                // k-step-major: consecutive MMAs feed the 4 independent output
+                // blocks, so no MMA waits on the one just issued.
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        const uint64_t ad = smem_desc_sw128(a0 + ks * 2048, kSubBytes, 1024);
-                        const uint64_t bd = smem_desc_sw128(p_addr + (t & 1) * kPBytes + ks * 32, 16, 1024);
-                        tc_mma_f16(tmem + kTmemO + 16 * j, ad, bd, kIdescPV, (first && ks == 0) ? 0u : 1u);
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint64_t bd = dK + ((b0 + ks * 32) >> 4);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t ad = dMN + ((a0 + j * 2 * kChunkBytes + ks * 2048) >> 4);
+                        tc_mma_f16(tmem + kTmemO + 16 * j, ad, bd, kIdescPV, (ti.first && ks == 0) ? 0u : 1u);
                     }
-                    tc_commit(&S.pair_empty[slot]);
                 }
+                tc_commit(&S.tile_empty[t % kNTile]);
                 tc_commit(&S.pv_done[t & 1]);
+                MLA_STAMP(t, 5);
+                ++pv_next;
                 return true;
             };
-            for (; cur.valid(); cur.next(), ++i) {
-                if (cur.first()) {
-                    if (!(ok = mbar_wait(&S.q_full, cur.seg & 1, abort, p.error_word))) break;
-                    tc_fence_after();
-                }
-                const uint32_t d_s = tmem + kTmemS + 16 * (i & 1);
-                for (int ch = 0; ch < 9 && ok; ++ch) {
-                    uint32_t a_addr;
-                    if (ch < 8) {
-                        const uint32_t fill = (uint32_t)(4 * i + ch / 2), slot = fill % kNPair;
-                        if ((ch & 1) == 0) {
-                            if (!(ok = mbar_wait(&S.pair_full[slot], (fill / kNPair) & 1, abort, p.error_word))) break;
-                            tc_fence_after();
-                        }
-                        a_addr = pair_addr + slot * kPairBytes + (ch & 1) * kSubBytes;
-                    } else {
-                        const uint32_t slot = (uint32_t)i % kNKpe;
-                        if (!(ok = mbar_wait(&S.kpe_full[slot], ((uint32_t)i / kNKpe) & 1, abort, p.error_word))) break;
-                        tc_fence_after();
-                        a_addr = kpe_addr + slot * kSubBytes;
-                    }
+
+            auto qk_step = [&]() -> bool {
+                const bool first = cur.first();
+                const int qs = cur.seg % kNQ;
+                if (first && !mbar_test_wait(&S.q_full[qs], (cur.seg / kNQ) & 1)) return false;
+                const uint32_t slot = (uint32_t)qk_j % kNTile;
+                if (!mbar_test_wait(&S.tile_full[slot], ((uint32_t)qk_j / kNTile) & 1)) return false;
+                tc_fence_after();
+                MLA_STAMP(qk_j, 2);
+                info[qk_j & 3] = TileInfo{first, cur.last(), cur.seg};
+                const uint32_t a0 = tile_addr + slot * kTileBytes;
+                const uint32_t b0 = q_addr + qs * kQBytes;
+                // Sub-step kk of every 64-column block accumulates into its own
+                // partial S_kk: 4 independent chains of 9 MMAs, interleaved.
+                const uint32_t d_s = tmem + kTmemS + 64 * (qk_j & 1);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-                        const uint64_t bd = smem_desc_sw128(q_addr + ch * kQChunkBytes + kk * 32, 16, 1024);
-                        tc_mma_f16(d_s, ad, bd, kIdescQK, (ch | kk) ? 1u : 0u);
+                for (int ch = 0; ch < 9; ++ch) {
+#pragma unroll
+                    for (int kk = 0; kk < kSParts; ++kk) {
+                        const uint64_t ad = dK + ((a0 + ch * kChunkBytes + kk * 32) >> 4);
+                        const uint64_t bd = dK + ((b0 + ch * kQChunkBytes + kk * 32) >> 4);
+                        tc_mma_f16(d_s + 16 * kk, ad, bd, kIdescQK, ch ? 1u : 0u);
                     }
                 }
-                if (!ok) break;
-                tc_commit(&S.s_full[i & 1]);
-                tc_commit(&S.kpe_empty[(uint32_t)i % kNKpe]);
-                if (cur.last()) tc_commit(&S.q_empty);
-                if (i > 0 && !(ok = do_pv(i - 1, prev_first, prev_seg))) break;
-                prev_first = cur.first();
-                prev_seg = cur.seg;
+                tc_commit(&S.s_full[qk_j & 1]);
+                if (cur.last()) tc_commit(&S.q_empty[qs]);
+                MLA_STAMP(qk_j, 3);
+                ++qk_j;
+                cur.next();
+                return true;
+            };
+
+            uint32_t idle = 0;
+            uint64_t idle_t0 = 0;
+            while (pv_next < n_tiles) {
+                bool prog = false;
+                if (pv_next < qk_j) prog = pv_step();
+                if (!prog && qk_j < n_tiles && qk_j < pv_next + 2) prog = qk_step();
+                if (prog) { idle = 0; continue; }
+                if ((++idle & 63) == 0) {
+                    if (*abort) break;
+                    const uint64_t now = globaltimer_ns();
+                    if (idle == 64) {
+                        idle_t0 = now;
+                    } else if (now - idle_t0 > kWaitLimitNs) {
+                        record_error(p.error_word, MLA_DEV_TIMEOUT);
+                        *abort = 1;
+                        break;
+                    }
+                }
             }
-            if (ok && i > 0) do_pv(i - 1, prev_first, prev_seg);
             // Drain all issued MMAs before TMEM is freed.
             tc_commit(&S.teardown);
             mbar_drain(&S.teardown, 0, p.error_word);
@@ -332,31 +353,47 @@ __global__ void __launch_bounds__(kK2Threads, 1)
             if (!mbar_wait(&S.s_full[i & 1], (i >> 1) & 1, abort, p.error_word)) break;
             tc_fence_after();
             __syncwarp();
+            if (wg_tid == 0) MLA_STAMP(i, 6);
             float s[16];
-            tmem_ld16(tmem_lane_addr(tmem, sp, kTmemS + 16 * (i & 1)), s);
-            tmem_wait_ld();
+            {
+                float s1[16], s2[16], s3[16];
+                const uint32_t ta = tmem_lane_addr(tmem, sp, kTmemS + 64 * (i & 1));
+                tmem_ld16(ta, s);
+                tmem_ld16(ta + 16, s1);
+                tmem_ld16(ta + 32, s2);
+                tmem_ld16(ta + 48, s3);
+                tmem_wait_ld();
+#pragma unroll
+                for (int h = 0; h < 16; ++h) s[h] = (s[h] + s1[h]) + (s2[h] + s3[h]);
+            }
             const bool ok_tok = lane < 16 && tok < valid;
 #pragma unroll
             for (int h = 0; h < 16; ++h) s[h] = ok_tok ? s[h] * scale_log2 : -INFINITY;
 
-            const float wmax = warp_reduce16_transposed<true>(s, lane);
-            if (lane < 16) S.red[i & 1][sp][lane] = wmax;
-            named_bar_sync(1, 128);
-            float mt[16];
+            // Running max per head (log2 domain). First tile of a segment: the
+            // exact tile max. Later tiles: lazy rescale; the running max is
+            // kept unless some score exceeds it by more than 8 (exps stay
+            // <= 256), which all 128 threads decide in one barrier-reduction.
+            bool exchange = first;
+            if (!first) {
+                bool exceed = false;
 #pragma unroll
-            for (int h = 0; h < 16; ++h)
-                mt[h] = fmaxf(fmaxf(S.red[i & 1][0][h], S.red[i & 1][1][h]), fmaxf(S.red[i & 1][2][h], S.red[i & 1][3][h]));
-
-            if (first) {
+                for (int h = 0; h < 16; ++h) exceed |= s[h] > m_run[h] + 8.f;
+                exchange = bar_red_or(1, 128, exceed);
+            }
+            if (exchange) {
+                const float wmax = warp_reduce16_transposed<true>(s, lane);
+                if (lane < 16) S.red[i & 1][sp][lane] = wmax;
+                named_bar_sync(1, 128);
+                float mt[16];
 #pragma unroll
-                for (int h = 0; h < 16; ++h) m_run[h] = mt[h];
-            } else {
-                // Lazy rescale: keep the running max unless a head's tile max
-                // exceeds it by more than 2^8; exps stay <= 256 in between.
-                bool need = false;
+                for (int h = 0; h < 16; ++h)
+                    mt[h] = fmaxf(fmaxf(S.red[i & 1][0][h], S.red[i & 1][1][h]),
+                                  fmaxf(S.red[i & 1][2][h], S.red[i & 1][3][h]));
+                if (first) {
 #pragma unroll
-                for (int h = 0; h < 16; ++h) need |= mt[h] > m_run[h] + 8.f;
-                if (need) {
+                    for (int h = 0; h < 16; ++h) m_run[h] = mt[h];
+                } else {
                     float f[16];
 #pragma unroll
                     for (int h = 0; h < 16; ++h) {
@@ -402,25 +439,21 @@ __global__ void __launch_bounds__(kK2Threads, 1)
                 // Rows past the sequence end are masked in P; zero them in the
                 // C tile too so that 0 * (stale or non-finite bits) cannot
                 // reach the output MMA.
-                bool okw = true;
-                for (int j = 0; j < 4 && okw; ++j) {
-                    const uint32_t fill = (uint32_t)(4 * i + j);
-                    okw = mbar_wait(&S.pair_full[fill % kNPair], (fill / kNPair) & 1, abort, p.error_word);
-                }
-                if (!okw) break;
+                const uint32_t slot = (uint32_t)i % kNTile;
+                if (!mbar_wait(&S.tile_full[slot], ((uint32_t)i / kNTile) & 1, abort, p.error_word)) break;
                 const int nrows = kPage - valid;
-                const int per_sub = nrows * 8;
-                for (int idx = wg_tid; idx < 8 * per_sub; idx += 128) {
-                    const int sub = idx / per_sub, rem = idx % per_sub;
+                const int per_chunk = nrows * 8;
+                uint8_t* base = tile_s + slot * kTileBytes;
+                for (int idx = wg_tid; idx < 8 * per_chunk; idx += 128) {
+                    const int ch = idx / per_chunk, rem = idx % per_chunk;
                     const int r = valid + rem / 8, q16 = rem % 8;
-                    const uint32_t slot = (uint32_t)(4 * i + sub / 2) % kNPair;
-                    uint8_t* dst = pair_s + slot * kPairBytes + (sub & 1) * kSubBytes + r * 128 + q16 * 16;
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(base + ch * kChunkBytes + r * 128 + q16 * 16) = make_uint4(0, 0, 0, 0);
                 }
             }
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&S.p_full[i & 1]);
+            if (wg_tid == 0) MLA_STAMP(i, 7);
 
             if (last) {
                 if (!mbar_wait(&S.pv_done[i & 1], (i >> 1) & 1, abort, p.error_word)) break;
@@ -585,3 +618,18 @@ cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, c
 }
 
 }  // namespace mla
+
+#ifdef MLA_TRACE
+// Trace build only (not part of include/mla_decode.h): copy the attention
+// kernel's per-tile stamps [160 CTAs][96 tiles][8 events] (SM clocks) to `host`
+// and clear them.
+extern "C" int mla_trace_read(long long* host, uint64_t n) {
+    using namespace mla;
+    const uint64_t total = (uint64_t)kTraceCtas * kTraceTiles * kTraceEvents;
+    if (!host || n < total) return MLA_E_INVALID_ARG;
+    if (cudaMemcpyFromSymbol(host, g_mla_trace, total * sizeof(long long)) != cudaSuccess) return MLA_E_LAUNCH;
+    static long long zeros[kTraceCtas * kTraceTiles * kTraceEvents];
+    if (cudaMemcpyToSymbol(g_mla_trace, zeros, sizeof(zeros)) != cudaSuccess) return MLA_E_LAUNCH;
+    return MLA_OK;
+}
+#endif

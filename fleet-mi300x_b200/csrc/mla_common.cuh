@@ -105,6 +105,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe of one phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -142,6 +155,20 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also ORs a predicate over the participating threads.
+__device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 // ---------------------------------------------------------------------------
 // TMA: 2-D tiled load global -> shared, completion on an mbarrier. Never
 // with .multicast::cluster.
@@ -155,6 +182,24 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
         " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(cache_hint)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y, int z,
+                                            uint64_t cache_hint) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(cache_hint)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y, int z,
+                                            int w, uint64_t cache_hint) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(cache_hint)
         : "memory");
 }
 
@@ -265,5 +310,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+
+// ---------------------------------------------------------------------------
+// Optional per-tile trace stamps (SM clock), compiled in only with -DMLA_TRACE:
+// the role timeline of the attention kernel, read back by mla_trace_read().
+// ---------------------------------------------------------------------------
+#ifdef MLA_TRACE
+constexpr int kTraceCtas = 160, kTraceTiles = 96, kTraceEvents = 8;
+// g_mla_trace is defined in mla_attention.cu, the only translation unit that stamps.
+#define MLA_STAMP(tile, ev)                                                                          \
+    do {                                                                                             \
+        if (blockIdx.x < ::mla::kTraceCtas && (tile) < ::mla::kTraceTiles)                           \
+            ::mla::g_mla_trace[((int)blockIdx.x * ::mla::kTraceTiles + (tile)) * ::mla::kTraceEvents + \
+                               (ev)] = clock64();                                                    \
+    } while (0)
+#else
+#define MLA_STAMP(tile, ev) \
+    do {                    \
+    } while (0)
+#endif
 
 }  // namespace mla

@@ -10,18 +10,31 @@
 //    score contraction;
 //  * the split plan: prefix sum of 64-token tiles per request, consumed by K2/K3.
 //
-// Grid: x = request block of kReqBlock requests (plus one planner CTA),
-//       y = head, z = 128-column block of the 512-wide latent.
+// One 1-D grid with three kinds of CTA:
+//   [0, n_absorb)            absorb: (request block of 16, head, 128-column block)
+//   [n_absorb, +n_rowwarps)  per-request work, one warp per request
+//   last                     planner
 #include "mla_common.cuh"
 
 namespace mla {
 
 constexpr int kReqBlock = 16;   // requests per absorb CTA: W_UK tile reuse across requests
-constexpr int kColBlock = 128;  // latent columns per CTA
+constexpr int kColBlock = 128;  // latent columns per absorb CTA
 constexpr int kK1Threads = 128;
+constexpr int kReqPerRowCta = kK1Threads / 32;
 
-// DeepseekV2 RoPE on 64 values held as x[0..64): interleave-transpose, then
-// rotate_half (reference_decode.py:120-134). out[j] for j < 32 and out[32+j]:
+struct K1Grid {
+    int n_rb, n_absorb, n_row, total;
+    __host__ __device__ explicit K1Grid(int batch) {
+        n_rb = (batch + kReqBlock - 1) / kReqBlock;
+        n_absorb = n_rb * kHeads * (kLora / kColBlock);
+        n_row = (batch + kReqPerRowCta - 1) / kReqPerRowCta;
+        total = n_absorb + n_row + 1;
+    }
+};
+
+// DeepseekV2 RoPE on 64 values x[0..64): interleave-transpose, then rotate_half
+// (reference_decode.py:120-134). For pair j < 32:
 //   out[j]    = x[2j]*cos[j]       - x[2j+1]*sin[j]
 //   out[32+j] = x[2j+1]*cos[32+j]  + x[2j]*sin[32+j]
 // Products and the sum are rounded separately, as NumPy evaluates
@@ -32,14 +45,8 @@ __device__ __forceinline__ void rope_pair(float x_even, float x_odd, const float
     hi = __fadd_rn(__fmul_rn(x_odd, cs[32 + j]), __fmul_rn(x_even, sn[32 + j]));
 }
 
-__device__ __forceinline__ float block_sum_128(float v, float* red) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    return (red[0] + red[1]) + (red[2] + red[3]);  // fixed order
+__device__ __forceinline__ bool position_ok(const MlaDecodeParams& p, int pos) {
+    return pos >= 0 && pos < p.max_pos && pos < p.max_blocks * kPage;
 }
 
 // Prefix sum of tiles per request (one CTA). Invalid positions are recorded
@@ -54,11 +61,8 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum) {
         int n = 0;
         if (b < p.batch) {
             const int pos = p.seq_lens[b];
-            if (pos < 0 || pos >= p.max_pos || pos >= p.max_blocks * kPage) {
-                record_error(p.error_word, MLA_DEV_BAD_POSITION);
-            } else {
-                n = (pos + 1 + kPage - 1) / kPage;
-            }
+            if (!position_ok(p, pos)) record_error(p.error_word, MLA_DEV_BAD_POSITION);
+            else n = (pos + 1 + kPage - 1) / kPage;
         }
         int incl = n;
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -79,33 +83,103 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum) {
     if (threadIdx.x == 0) cum[p.batch] = carry;
 }
 
+// One warp: kv_post + cache append + q_pe RoPE of request b.
+__device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b, int lane) {
+    const int pos = p.seq_lens[b];
+    if (!position_ok(p, pos)) return;  // recorded by the planner
+    const float* cs = p.rope_cos + (int64_t)pos * kRope;
+    const float* sn = p.rope_sin + (int64_t)pos * kRope;
+    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q) + (int64_t)b * p.q_stride;
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride;
+    const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w);
+
+    // q_pe of all 16 heads: lane j rotates pair j
+    __nv_bfloat16* qrow = qa + (int64_t)b * kQRows * kRow;
+#pragma unroll 4
+    for (int h = 0; h < kHeads; ++h) {
+        const __nv_bfloat162 x = reinterpret_cast<const __nv_bfloat162*>(q + h * kQHead + kNope)[lane];
+        float lo, hi;
+        rope_pair(__low2float(x), __high2float(x), cs, sn, lane, lo, hi);
+        qrow[h * kRow + kLora + lane] = __float2bfloat16_rn(lo);
+        qrow[h * kRow + kLora + 32 + lane] = __float2bfloat16_rn(hi);
+    }
+
+    // kv_post (reference_decode.py:60-65): var = mean(x^2); y = x * (1 / sqrt(var + eps));
+    // row = bf16(bf16(y) * weight). Lane owns c[16*lane, 16*lane+16).
+    float x[16];
+    {
+        const uint4* s4 = reinterpret_cast<const uint4*>(src) + 2 * lane;
+        uint4 v[2];
+        if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+            v[0] = s4[0]; v[1] = s4[1];
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { x[2 * k] = __low2float(h2[k]); x[2 * k + 1] = __high2float(h2[k]); }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) x[k] = __bfloat162float(src[16 * lane + k]);
+        }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) ss = __fadd_rn(ss, __fmul_rn(x[k], x[k]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float var = __fdiv_rn(ss, (float)kLora);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.rms_eps)));
+    __align__(16) __nv_bfloat16 outc[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const float y = bf16_round(__fmul_rn(x[k], inv));
+        outc[k] = __float2bfloat16_rn(__fmul_rn(y, __bfloat162float(gam[16 * lane + k])));
+    }
+    float lo, hi;
+    rope_pair(__bfloat162float(src[kLora + 2 * lane]), __bfloat162float(src[kLora + 2 * lane + 1]), cs, sn, lane,
+              lo, hi);
+    const int page = p.block_table[(int64_t)b * p.max_blocks + pos / kPage];
+    if (page < 0 || page >= p.n_pages) {
+        if (lane == 0) record_error(p.error_word, MLA_DEV_BAD_PAGE);
+        return;
+    }
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.kv_cache) + ((int64_t)page * kPage + pos % kPage) * kRow;
+    reinterpret_cast<uint4*>(dst)[2 * lane] = reinterpret_cast<const uint4*>(outc)[0];
+    reinterpret_cast<uint4*>(dst)[2 * lane + 1] = reinterpret_cast<const uint4*>(outc)[1];
+    dst[kLora + lane] = __float2bfloat16_rn(lo);
+    dst[kLora + 32 + lane] = __float2bfloat16_rn(hi);
+}
+
 __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p) {
     const WsLayout ws = ws_layout(p.batch, p.num_ctas);
     char* wsb = reinterpret_cast<char*>(p.workspace);
-    const int n_rb = (p.batch + kReqBlock - 1) / kReqBlock;
+    __nv_bfloat16* qa = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
+    const K1Grid g(p.batch);
+    const int cta = blockIdx.x;
 
-    if (blockIdx.x == n_rb) {  // planner CTA
-        if (blockIdx.y == 0 && blockIdx.z == 0) plan_scan(p, reinterpret_cast<int32_t*>(wsb + ws.tiles_cum));
+    if (cta == g.total - 1) {
+        plan_scan(p, reinterpret_cast<int32_t*>(wsb + ws.tiles_cum));
+        return;
+    }
+    if (cta >= g.n_absorb) {
+        const int b = (cta - g.n_absorb) * kReqPerRowCta + (threadIdx.x >> 5);
+        if (b < p.batch) request_rows(p, qa, b, threadIdx.x & 31);
         return;
     }
 
-    __shared__ __align__(16) __nv_bfloat16 w_s[kNope][kColBlock];  // W_UK[h][:, cols], 32 KB
-    __shared__ __align__(16) float q_s[kNope][kReqBlock];          // q_nope, transposed, 8 KB
-    __shared__ float red[4];
-    __shared__ float row_s[kRow];
-
-    const int h = blockIdx.y, cb = blockIdx.z;
-    const int b0 = blockIdx.x * kReqBlock;
+    // ---- absorb CTA: q_c[b][h][cols] = q_nope[b][h] @ W_UK[h][:, cols] for 16 requests ----
+    __shared__ __align__(16) __nv_bfloat16 w_s[kNope][kColBlock];  // 32 KB
+    __shared__ __align__(16) float q_s[kNope][kReqBlock];          // 8 KB, transposed
+    const int cb = cta % (kLora / kColBlock);
+    const int h = (cta / (kLora / kColBlock)) % kHeads;
+    const int rb = cta / (kLora / kColBlock) / kHeads;
+    const int b0 = rb * kReqBlock;
     const int nreq = min(kReqBlock, p.batch - b0);
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);
     const __nv_bfloat16* kvb = reinterpret_cast<const __nv_bfloat16*>(p.kv_b);
-    __nv_bfloat16* qa = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
-
-    // ---- stage W_UK[h][0:128, cb*128 : cb*128+128] (kv_b rows 256h + d) ----
     {
         const uint4* src = reinterpret_cast<const uint4*>(kvb);
         uint4* dst = reinterpret_cast<uint4*>(&w_s[0][0]);
-        constexpr int kVecPerRow = kColBlock / 8;  // 16
+        constexpr int kVecPerRow = kColBlock / 8;
+#pragma unroll 4
         for (int i = threadIdx.x; i < kNope * kVecPerRow; i += kK1Threads) {
             const int d = i / kVecPerRow, v = i % kVecPerRow;
             dst[i] = src[((int64_t)(h * kKvbHead + d) * kLora + cb * kColBlock) / 8 + v];
@@ -116,107 +190,31 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
         q_s[d][r] = r < nreq ? __bfloat162float(q[(int64_t)(b0 + r) * p.q_stride + h * kQHead + d]) : 0.f;
     }
     __syncthreads();
-
-    // ---- q_c[b][h][col] = sum_d q_nope[b][h][d] * W_UK[h][d][col], fp32 ----
-    {
-        const int col = threadIdx.x;
-        float acc[kReqBlock];
+    const int col = threadIdx.x;
+    float acc[kReqBlock];
 #pragma unroll
-        for (int r = 0; r < kReqBlock; ++r) acc[r] = 0.f;
+    for (int r = 0; r < kReqBlock; ++r) acc[r] = 0.f;
 #pragma unroll 4
-        for (int d = 0; d < kNope; ++d) {
-            const float w = __bfloat162float(w_s[d][col]);
-            const float4* q4 = reinterpret_cast<const float4*>(&q_s[d][0]);
+    for (int d = 0; d < kNope; ++d) {
+        const float w = __bfloat162float(w_s[d][col]);
+        const float4* q4 = reinterpret_cast<const float4*>(&q_s[d][0]);
 #pragma unroll
-            for (int r4 = 0; r4 < kReqBlock / 4; ++r4) {
-                const float4 qq = q4[r4];
-                acc[4 * r4 + 0] = fmaf(qq.x, w, acc[4 * r4 + 0]);
-                acc[4 * r4 + 1] = fmaf(qq.y, w, acc[4 * r4 + 1]);
-                acc[4 * r4 + 2] = fmaf(qq.z, w, acc[4 * r4 + 2]);
-                acc[4 * r4 + 3] = fmaf(qq.w, w, acc[4 * r4 + 3]);
-            }
+        for (int r4 = 0; r4 < kReqBlock / 4; ++r4) {
+            const float4 qq = q4[r4];
+            acc[4 * r4 + 0] = fmaf(qq.x, w, acc[4 * r4 + 0]);
+            acc[4 * r4 + 1] = fmaf(qq.y, w, acc[4 * r4 + 1]);
+            acc[4 * r4 + 2] = fmaf(qq.z, w, acc[4 * r4 + 2]);
+            acc[4 * r4 + 3] = fmaf(qq.w, w, acc[4 * r4 + 3]);
         }
+    }
 #pragma unroll
-        for (int r = 0; r < kReqBlock; ++r) {
-            if (r < nreq) {
-                qa[((int64_t)(b0 + r) * kQRows + h) * kRow + cb * kColBlock + col] = __float2bfloat16_rn(acc[r]);
-            }
-        }
-    }
-
-    if (cb != 0) return;
-
-    // ---- q_pe RoPE for head h (cb == 0 CTAs) ----
-    for (int r = 0; r < nreq; ++r) {
-        const int b = b0 + r;
-        const int pos = p.seq_lens[b];
-        if (pos < 0 || pos >= p.max_pos) continue;  // recorded by the planner
-        const float* cs = p.rope_cos + (int64_t)pos * kRope;
-        const float* sn = p.rope_sin + (int64_t)pos * kRope;
-        if (threadIdx.x < 32) {
-            const int j = threadIdx.x;
-            const __nv_bfloat16* qp = q + (int64_t)b * p.q_stride + h * kQHead + kNope;
-            float lo, hi;
-            rope_pair(__bfloat162float(qp[2 * j]), __bfloat162float(qp[2 * j + 1]), cs, sn, j, lo, hi);
-            __nv_bfloat16* dst = qa + ((int64_t)b * kQRows + h) * kRow + kLora;
-            dst[j] = __float2bfloat16_rn(lo);
-            dst[32 + j] = __float2bfloat16_rn(hi);
-        }
-    }
-
-    if (h != 0) return;
-
-    // ---- kv_post for the block's requests (h == 0, cb == 0) ----
-    const __nv_bfloat16* kva = reinterpret_cast<const __nv_bfloat16*>(p.kv_a);
-    const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w);
-    __nv_bfloat16* cache = reinterpret_cast<__nv_bfloat16*>(p.kv_cache);
-    for (int r = 0; r < nreq; ++r) {
-        const int b = b0 + r;
-        const int pos = p.seq_lens[b];
-        const bool pos_ok = pos >= 0 && pos < p.max_pos && pos < p.max_blocks * kPage;
-        const __nv_bfloat16* src = kva + (int64_t)b * p.kv_a_stride;
-        float ss = 0.f;
-        for (int i = threadIdx.x; i < kLora; i += kK1Threads) {
-            const float v = __bfloat162float(src[i]);
-            ss = fmaf(v, v, ss);
-        }
-        const float sumsq = block_sum_128(ss, red);
-        // reference_decode.py:60-65: var = mean(x^2); y = x * (1 / sqrt(var + eps));
-        // bf16(y) * weight, rounded to bf16 again.
-        const float var = __fdiv_rn(sumsq, (float)kLora);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.rms_eps)));
-        for (int i = threadIdx.x; i < kLora; i += kK1Threads) {
-            const float y = bf16_round(__fmul_rn(__bfloat162float(src[i]), inv));
-            row_s[i] = bf16_round(__fmul_rn(y, __bfloat162float(gam[i])));
-        }
-        if (pos_ok && threadIdx.x < 32) {
-            const int j = threadIdx.x;
-            const float* cs = p.rope_cos + (int64_t)pos * kRope;
-            const float* sn = p.rope_sin + (int64_t)pos * kRope;
-            float lo, hi;
-            rope_pair(__bfloat162float(src[kLora + 2 * j]), __bfloat162float(src[kLora + 2 * j + 1]), cs, sn, j,
-                      lo, hi);
-            row_s[kLora + j] = lo;
-            row_s[kLora + 32 + j] = hi;
-        }
-        __syncthreads();
-        if (pos_ok) {
-            const int page = p.block_table[(int64_t)b * p.max_blocks + pos / kPage];
-            if (page < 0 || page >= p.n_pages) {
-                if (threadIdx.x == 0) record_error(p.error_word, MLA_DEV_BAD_PAGE);
-            } else {
-                __nv_bfloat16* dst = cache + ((int64_t)page * kPage + pos % kPage) * kRow;
-                for (int i = threadIdx.x; i < kRow; i += kK1Threads) dst[i] = __float2bfloat16_rn(row_s[i]);
-            }
-        }
-        __syncthreads();
-    }
+    for (int r = 0; r < kReqBlock; ++r)
+        if (r < nreq) qa[((int64_t)(b0 + r) * kQRows + h) * kRow + cb * kColBlock + col] = __float2bfloat16_rn(acc[r]);
 }
 
 cudaError_t launch_prologue(const MlaDecodeParams& p, cudaStream_t stream) {
-    const int n_rb = (p.batch + kReqBlock - 1) / kReqBlock;
-    dim3 grid(n_rb + 1, kHeads, kLora / kColBlock);
-    k1_prologue<<<grid, kK1Threads, 0, stream>>>(p);
+    const K1Grid g(p.batch);
+    k1_prologue<<<g.total, kK1Threads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -6,6 +6,7 @@ module. If the shared library is missing, loading fails loudly with the build co
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -73,7 +74,7 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
     with _lock:
         if _lib is not None and path is None:
             return _lib
-        p = Path(path) if path else LIB_PATH
+        p = Path(path) if path else Path(os.environ.get("MLA_DECODE_LIB", LIB_PATH))
         if not p.exists():
             raise RuntimeError(
                 f"{p} is missing: build it with `python fleet-mi300x_b200/build.py` "
