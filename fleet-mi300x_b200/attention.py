@@ -59,7 +59,7 @@ class MlaDecodeAttention:
     """
 
     def __init__(self, cfg: ModelConfig, w: LayerWeights, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
-                 *, num_ctas: int = 0, check_kernel: bool = False):
+                 *, num_ctas: int = 0, check_kernel: bool = False, kernel: str = "mma"):
         cfg.check_supported()
         self.cfg = cfg
         self.lib = native.load_library()
@@ -74,7 +74,9 @@ class MlaDecodeAttention:
         self.cos = rope_cos.contiguous().float()
         self.sin = rope_sin.contiguous().float()
         self.num_ctas = int(num_ctas)
-        self.flags = native.FLAG_CHECK_KERNEL if check_kernel else 0
+        if kernel not in ("mma", "tcgen05"):
+            raise ValueError("kernel must be 'mma' (m16n8k16, default) or 'tcgen05'")
+        self.flags = native.FLAG_CHECK_KERNEL if check_kernel else (native.FLAG_TCGEN05 if kernel == "tcgen05" else 0)
         self.error_word = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ws: torch.Tensor | None = None
 

@@ -18,7 +18,10 @@ cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tma
                                 float scale_log2, cudaStream_t stream);
 cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream);
 cudaError_t launch_merge_uv(const MlaDecodeParams& p, cudaStream_t stream);
+cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
+                                 cudaStream_t stream);
 cudaError_t k2_configure();
+cudaError_t k2_mma_configure();
 cudaError_t k3_configure();
 
 namespace {
@@ -44,7 +47,10 @@ int device_info(int* sm_count) {
         cudaDeviceProp prop;
         if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
         if (prop.major != 10) { d.status = MLA_E_ARCH; return; }
-        if (k2_configure() != cudaSuccess || k3_configure() != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
+        if (k2_configure() != cudaSuccess || k2_mma_configure() != cudaSuccess || k3_configure() != cudaSuccess) {
+            d.status = MLA_E_LAUNCH;
+            return;
+        }
         d.sm_count = prop.multiProcessorCount;
         d.status = MLA_OK;
     });
@@ -144,6 +150,8 @@ int run_attention(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap tkv, tq;
     int st = make_tmap_blocks(&tkv, q.kv_cache, (uint64_t)q.n_pages, true);
     if (st != MLA_OK) return st;
+    if (!(q.flags & MLA_FLAG_TCGEN05))
+        return launch_attention_mma(q, tkv, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
     const WsLayout ws = ws_layout(q.batch, q.num_ctas);
     st = make_tmap_blocks(&tq, reinterpret_cast<const char*>(q.workspace) + ws.qa, (uint64_t)q.batch * kQRows, false);
     if (st != MLA_OK) return st;

@@ -19,6 +19,7 @@ ROW = KV_LORA + QK_ROPE
 MAX_BATCH = 65536
 
 FLAG_CHECK_KERNEL = 0x2
+FLAG_TCGEN05 = 0x4
 
 STATUS = {
     0: "MLA_OK", -1: "MLA_E_INVALID_ARG", -2: "MLA_E_UNSUPPORTED_DIMS", -3: "MLA_E_MISALIGNED",

@@ -83,7 +83,10 @@ typedef enum {
 /* Flags. */
 #define MLA_FLAG_CHECK_KERNEL 0x2 /* run the CUDA-core split-KV kernel instead of the tensor-core one
                                      (same plan and partial layout, fp32 probabilities; it exists to
-                                     cross-check the tensor-core kernel, not as a fallback) */
+                                     cross-check the tensor-core kernels, not as a fallback) */
+#define MLA_FLAG_TCGEN05 0x4      /* run the split-KV kernel that keeps scores and the output in tensor
+                                     memory (tcgen05.mma, tokens on M, heads on N) instead of the default
+                                     m16n8k16 kernel (heads on M); same plan and partial layout */
 
 typedef struct MlaDecodeParams {
     uint32_t struct_size; /* sizeof(MlaDecodeParams) */

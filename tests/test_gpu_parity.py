@@ -38,12 +38,16 @@ def golden_runner(case, dev, **kw):
     return fleet.MlaDecodeAttention(cfg, to_dev(case.lw, dev), cos, sin, **kw), cache
 
 
+KERNELS = [dict(kernel="mma"), dict(kernel="tcgen05"), dict(check_kernel=True)]
+KERNEL_IDS = ["mma", "tcgen05", "check"]
+
+
 @pytest.mark.parametrize("name", ["t37", "config1", "walk"])
-@pytest.mark.parametrize("check_kernel", [False, True])
-def test_golden_from_reference_qkv(golden, cuda_device, name, check_kernel):
+@pytest.mark.parametrize("kw", KERNELS, ids=KERNEL_IDS)
+def test_golden_from_reference_qkv(golden, cuda_device, name, kw):
     """Kernels fed the reference's own q / kv_a reproduce its R(out) and appended row."""
     case = GoldenCase(golden, name)
-    runner, cache = golden_runner(case, cuda_device, check_kernel=check_kernel)
+    runner, cache = golden_runner(case, cuda_device, **kw)
     for s in range(case.steps):
         q = torch.from_numpy(case.q[s]).to(BF)[None].to(cuda_device)
         kv_a = torch.from_numpy(case.kv_a[s]).to(BF)[None].to(cuda_device)
@@ -98,10 +102,10 @@ def oracle_paged(bt, pages_np, d, requests=None, fast=False):
                                   fast=fast, requests=requests)
 
 
-def run_gpu(d, dev, num_ctas=0, check_kernel=False):
+def run_gpu(d, dev, num_ctas=0, check_kernel=False, kernel="mma"):
     runner = fleet.MlaDecodeAttention(fleet.ModelConfig(), to_dev(d["lw"], dev), torch.from_numpy(d["cos"]).to(dev),
                                       torch.from_numpy(d["sin"]).to(dev), num_ctas=num_ctas,
-                                      check_kernel=check_kernel)
+                                      check_kernel=check_kernel, kernel=kernel)
     q = torch.from_numpy(d["q"]).to(BF).to(dev)
     kv_a = torch.from_numpy(d["kv_a"]).to(BF).to(dev)
     out = runner.attend(q, kv_a, d["cache"])
@@ -112,39 +116,43 @@ def run_gpu(d, dev, num_ctas=0, check_kernel=False):
 EDGE_LENGTHS = [0, 1, 62, 63, 64, 65, 127, 128, 129, 200, 1000, 1023, 4095]
 
 
+@pytest.mark.parametrize("kernel", ["mma", "tcgen05"])
 @pytest.mark.parametrize("num_ctas", [0, 1, 3, 7, 64, 500])
-def test_ragged_paged_batch(cuda_device, num_ctas):
+def test_ragged_paged_batch(cuda_device, num_ctas, kernel):
     """Edge lengths around page boundaries (0 cached rows = only the new token), a
     permuted block table, and split plans from 1 CTA to more CTAs than tiles."""
     d = ragged_batch(cuda_device, EDGE_LENGTHS)
     pages_np = d["cache"].pages.float().cpu().numpy()
     bt = d["cache"].block_table.cpu().numpy()
     want, rows = oracle_paged(bt, pages_np, d)
-    got = run_gpu(d, cuda_device, num_ctas=num_ctas)
+    got = run_gpu(d, cuda_device, num_ctas=num_ctas, kernel=kernel)
     for b in range(len(EDGE_LENGTHS)):
-        assert_close(got[b], want[b], f"request {b} (T={EDGE_LENGTHS[b]}, ctas={num_ctas})")
+        assert_close(got[b], want[b], f"request {b} (T={EDGE_LENGTHS[b]}, ctas={num_ctas}, {kernel})")
     gpu_pages = d["cache"].pages.float().cpu().numpy()
     for b, n in enumerate(EDGE_LENGTHS):
         r = gpu_pages[bt[b][n // 64], n % 64]
         np.testing.assert_allclose(r, rows[b], rtol=1e-2, atol=1e-6)
 
 
-def test_tensor_core_vs_check_kernel_bitwise_plan(cuda_device):
+def test_tensor_core_kernels_vs_check_kernel(cuda_device):
     d = ragged_batch(cuda_device, EDGE_LENGTHS)
     a = run_gpu(d, cuda_device, num_ctas=5)
+    t = run_gpu(d, cuda_device, num_ctas=5, kernel="tcgen05")
     b = run_gpu(d, cuda_device, num_ctas=5, check_kernel=True)
     for i in range(len(EDGE_LENGTHS)):
-        assert_close(a[i], b[i], f"tc vs check, request {i}")
+        assert_close(a[i], b[i], f"mma vs check, request {i}")
+        assert_close(t[i], b[i], f"tcgen05 vs check, request {i}")
 
 
-def test_deterministic_and_page_permutation_invariant(cuda_device):
+@pytest.mark.parametrize("kernel", ["mma", "tcgen05"])
+def test_deterministic_and_page_permutation_invariant(cuda_device, kernel):
     lengths = [300, 5000, 77, 2048]
     d1 = ragged_batch(cuda_device, lengths, permute=True)
-    o1 = run_gpu(d1, cuda_device, num_ctas=9)
-    o1b = run_gpu(d1, cuda_device, num_ctas=9)
+    o1 = run_gpu(d1, cuda_device, num_ctas=9, kernel=kernel)
+    o1b = run_gpu(d1, cuda_device, num_ctas=9, kernel=kernel)
     np.testing.assert_array_equal(o1, o1b)  # same plan, same bits (no atomics, fixed merge order)
     d2 = ragged_batch(cuda_device, lengths, permute=False)
-    o2 = run_gpu(d2, cuda_device, num_ctas=9)
+    o2 = run_gpu(d2, cuda_device, num_ctas=9, kernel=kernel)
     np.testing.assert_array_equal(o1, o2)   # physical page placement does not matter
 
 
@@ -213,9 +221,11 @@ def test_full_size_config_subset(cuda_device, cfg_name, subset):
              kv_a=np.stack(kvs), lengths=lengths)
     pages_before = cache.pages.float().cpu().numpy()
     tc = run_gpu(d, cuda_device)
+    t5 = run_gpu(d, cuda_device, kernel="tcgen05")
     ck = run_gpu(d, cuda_device, check_kernel=True)
     for b in range(len(lengths)):
-        assert_close(tc[b], ck[b], f"{cfg_name} request {b}: tc vs check")
+        assert_close(tc[b], ck[b], f"{cfg_name} request {b}: mma vs check")
+        assert_close(t5[b], ck[b], f"{cfg_name} request {b}: tcgen05 vs check")
     want, _ = oracle_paged(cache.block_table.cpu().numpy(), pages_before, d, requests=subset, fast=True)
     for b in subset:
         assert_close(tc[b], want[b], f"{cfg_name} request {b} vs oracle")
