@@ -13,11 +13,12 @@
 #include "mla_common.cuh"
 
 namespace mla {
-cudaError_t launch_prologue(const MlaDecodeParams& p, cudaStream_t stream);
+cudaError_t launch_prologue(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream);
 cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, const CUtensorMap& tmap_q,
                                 float scale_log2, cudaStream_t stream);
 cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream);
-cudaError_t launch_merge_uv(const MlaDecodeParams& p, cudaStream_t stream);
+cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream);
+cudaError_t k1_configure();
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
                                  cudaStream_t stream);
 cudaError_t k2_configure();
@@ -47,7 +48,8 @@ int device_info(int* sm_count) {
         cudaDeviceProp prop;
         if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
         if (prop.major != 10) { d.status = MLA_E_ARCH; return; }
-        if (k2_configure() != cudaSuccess || k2_mma_configure() != cudaSuccess || k3_configure() != cudaSuccess) {
+        if (k1_configure() != cudaSuccess || k2_configure() != cudaSuccess || k2_mma_configure() != cudaSuccess ||
+            k3_configure() != cudaSuccess) {
             d.status = MLA_E_LAUNCH;
             return;
         }
@@ -90,6 +92,36 @@ int make_tmap_blocks(CUtensorMap* m, const void* base, uint64_t rows_or_pages, b
     return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
 }
 
+// kv_b (16*256 rows x 512 bf16) as 128-row blocks of W_UK / W_UV: dims {64
+// columns, 4096 rows (1024 B), 8 column blocks (128 B)}, box {64, 128, 8} =
+// one 128 KB request landing as [8][128 rows][128 B] with the 128-byte swizzle.
+int make_tmap_kvb(CUtensorMap* m, const void* kv_b) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn;
+    if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
+    cuuint64_t dims[3] = {64, (cuuint64_t)kHeads * kKvbHead, 8};
+    cuuint64_t strides[2] = {(cuuint64_t)kLora * 2, 128};
+    cuuint32_t box[3] = {64, 128, 8};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(kv_b), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
+}
+
+int run_prologue(const MlaDecodeParams& q, cudaStream_t s) {
+    CUtensorMap t;
+    const int st = make_tmap_kvb(&t, q.kv_b);
+    if (st != MLA_OK) return st;
+    return launch_prologue(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+int run_merge(const MlaDecodeParams& q, cudaStream_t s) {
+    CUtensorMap t;
+    const int st = make_tmap_kvb(&t, q.kv_b);
+    if (st != MLA_OK) return st;
+    return launch_merge_uv(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
 bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }
 
 int resolve_ctas(const MlaDecodeParams* p, int* ctas) {
@@ -128,7 +160,7 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         return MLA_E_INVALID_ARG;
     if (!(p->softmax_scale > 0.f) || !(p->rms_eps >= 0.f)) return MLA_E_INVALID_ARG;
     if (!aligned(p->kv_cache, 16) || !aligned(p->kv_b, 16) || !aligned(p->workspace, 256) ||
-        !aligned(p->q, 4) || (p->q_stride & 1) || !aligned(p->kv_a, 2) || !aligned(p->out, 2) || !aligned(p->kv_a_norm_w, 2) ||
+        !aligned(p->q, 4) || (p->q_stride & 1) || (p->out_stride & 1) || !aligned(p->kv_a, 2) || !aligned(p->out, 4) || !aligned(p->kv_a_norm_w, 2) ||
         !aligned(p->rope_cos, 4) || !aligned(p->rope_sin, 4))
         return MLA_E_MISALIGNED;
     int sms = 0;
@@ -234,7 +266,7 @@ int mla_prologue(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;
     int st = prepare(p, &q);
     if (st != MLA_OK) return st;
-    return launch_prologue(q, (cudaStream_t)stream) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    return run_prologue(q, (cudaStream_t)stream);
 }
 
 int mla_attention(const MlaDecodeParams* p, void* stream) {
@@ -248,7 +280,7 @@ int mla_merge_uv(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;
     int st = prepare(p, &q);
     if (st != MLA_OK) return st;
-    return launch_merge_uv(q, (cudaStream_t)stream) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    return run_merge(q, (cudaStream_t)stream);
 }
 
 int mla_decode_step(const MlaDecodeParams* p, void* stream) {
@@ -256,10 +288,11 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream) {
     int st = prepare(p, &q);
     if (st != MLA_OK) return st;
     cudaStream_t s = (cudaStream_t)stream;
-    if (launch_prologue(q, s) != cudaSuccess) return MLA_E_LAUNCH;
+    st = run_prologue(q, s);
+    if (st != MLA_OK) return st;
     st = run_attention(q, s);
     if (st != MLA_OK) return st;
-    return launch_merge_uv(q, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    return run_merge(q, s);
 }
 
 }  // extern "C"

@@ -30,6 +30,7 @@
 
 #include "mla_common.cuh"
 #include "mla_tiles.cuh"
+#include "mla_mma.cuh"
 
 namespace mla {
 
@@ -40,7 +41,8 @@ constexpr int kWarps = 4;                    // compute warps
 constexpr int kNTile = 2;                    // whole-page ring
 constexpr int kChunkBytes = 8192;
 constexpr int kTileBytes = 9 * kChunkBytes;
-constexpr int kSPitch = 68;                  // floats per head row of a partial-score block
+constexpr int kSPitch = 72;                  // floats per head row of a partial-score block (64-bit
+                                             // accesses by a half-warp then hit 32 distinct banks)
 constexpr int kSPartBytes = kWarps * kHeads * kSPitch * 4;   // 17,408
 constexpr int kPBytes = kHeads * 128;        // [16 heads][64 tokens] bf16, 128-byte swizzled rows
 
@@ -57,31 +59,6 @@ constexpr int kOffP = kOffS + kSPartBytes;
 constexpr int kOffMisc = kOffP + 2 * kPBytes;
 constexpr int kSmemBytes = kOffMisc + (int)sizeof(Smem) + 1024;
 static_assert(kSmemBytes <= 232448, "K2 (mma) shared memory exceeds 227 KB");
-
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t*>(&v);
-}
 
 // Zero the bf16 halves of a B fragment register whose token index is >= valid.
 __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok_lo, int valid) {
@@ -156,11 +133,13 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         uint32_t qf[9][4];                     // Q fragments, k-steps [9w, 9w+9)
         float o[16][4];                        // O_w: 16 latent tiles of 8
         float m_run[2], l_run[2];              // heads g, g+8
+        int rows_b = 0;                        // rows attended by the current request (seq_lens[b] + 1)
         int i = 0;
         bool ok = true;
         for (; cur.valid(); cur.next(), ++i) {
             const bool first = cur.first(), last = cur.last();
-            const int valid = cur.tokens();
+            if (first) rows_b = p.seq_lens[cur.b] + 1;
+            const int valid = min(kPage, rows_b - cur.page_index() * kPage);
             if (first) {
                 const __nv_bfloat16* qrow = qa + (int64_t)cur.b * kQRows * kRow + 144 * w + 2 * t4;
 #pragma unroll

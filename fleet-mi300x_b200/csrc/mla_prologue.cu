@@ -5,29 +5,36 @@
 //    bf16 row appended to the request's page (reference_decode.py:231-237,
 //    src/kernels/attention.h:62-90);
 //  * q_pe RoPE, bf16-rounded (reference_decode.py:235);
-//  * q-absorb q_c[h] = q_nope[h] @ W_UK[h] in fp32 (reference_decode.py:250,
-//    attention.h:171-216), stored bf16 as the B operand of the tensor-core
-//    score contraction;
+//  * q-absorb q_c[h] = q_nope[h] @ W_UK[h] with fp32 accumulation
+//    (reference_decode.py:250, attention.h:171-216): per head an m16n8k16 GEMM
+//    [16 requests x 128] x [128 x 512] with W_UK[h] staged by one 128 KB TMA
+//    box; q_nope and W_UK are bf16 already, so the products are exact; q_c is
+//    stored bf16 as an operand of the attention kernel's score contraction;
 //  * the split plan: prefix sum of 64-token tiles per request, consumed by K2/K3.
 //
 // One 1-D grid with three kinds of CTA:
-//   [0, n_absorb)            absorb: (request block of 16, head, 128-column block)
+//   [0, n_absorb)            absorb: (head, request block of 16)
 //   [n_absorb, +n_rowwarps)  per-request work, one warp per request
 //   last                     planner
+#include <cuda.h>
+
 #include "mla_common.cuh"
+#include "mla_mma.cuh"
 
 namespace mla {
 
-constexpr int kReqBlock = 16;   // requests per absorb CTA: W_UK tile reuse across requests
-constexpr int kColBlock = 128;  // latent columns per absorb CTA
+constexpr int kReqBlock = 16;   // requests per absorb CTA (M of the MMA)
 constexpr int kK1Threads = 128;
 constexpr int kReqPerRowCta = kK1Threads / 32;
+constexpr int kWukBytes = kNope * kLora * 2;          // 131072: [8 column blocks][128 rows][128 B], swizzled
+constexpr int kQnBytes = kReqBlock * kNope * 2;       // 4096: [16 requests][128] bf16, 256-byte rows, swizzled
+constexpr int kK1SmemBytes = kWukBytes + kQnBytes + 64 + 1024;
 
 struct K1Grid {
     int n_rb, n_absorb, n_row, total;
     __host__ __device__ explicit K1Grid(int batch) {
         n_rb = (batch + kReqBlock - 1) / kReqBlock;
-        n_absorb = n_rb * kHeads * (kLora / kColBlock);
+        n_absorb = n_rb * kHeads;
         n_row = (batch + kReqPerRowCta - 1) / kReqPerRowCta;
         total = n_absorb + n_row + 1;
     }
@@ -148,7 +155,8 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
     dst[kLora + 32 + lane] = __float2bfloat16_rn(hi);
 }
 
-__global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p) {
+__global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p,
+                                                            const __grid_constant__ CUtensorMap tmap_kvb) {
     const WsLayout ws = ws_layout(p.batch, p.num_ctas);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     __nv_bfloat16* qa = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
@@ -165,56 +173,79 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
         return;
     }
 
-    // ---- absorb CTA: q_c[b][h][cols] = q_nope[b][h] @ W_UK[h][:, cols] for 16 requests ----
-    __shared__ __align__(16) __nv_bfloat16 w_s[kNope][kColBlock];  // 32 KB
-    __shared__ __align__(16) float q_s[kNope][kReqBlock];          // 8 KB, transposed
-    const int cb = cta % (kLora / kColBlock);
-    const int h = (cta / (kLora / kColBlock)) % kHeads;
-    const int rb = cta / (kLora / kColBlock) / kHeads;
+    // ---- absorb CTA: q_c[b][h][:] = q_nope[b][h] @ W_UK[h] for 16 requests ----
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* w_s = smem;
+    uint8_t* q_s = smem + kWukBytes;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(q_s + kQnBytes);
+    const int h = cta % kHeads, rb = cta / kHeads;
     const int b0 = rb * kReqBlock;
     const int nreq = min(kReqBlock, p.batch - b0);
-    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);
-    const __nv_bfloat16* kvb = reinterpret_cast<const __nv_bfloat16*>(p.kv_b);
-    {
-        const uint4* src = reinterpret_cast<const uint4*>(kvb);
-        uint4* dst = reinterpret_cast<uint4*>(&w_s[0][0]);
-        constexpr int kVecPerRow = kColBlock / 8;
-#pragma unroll 4
-        for (int i = threadIdx.x; i < kNope * kVecPerRow; i += kK1Threads) {
-            const int d = i / kVecPerRow, v = i % kVecPerRow;
-            dst[i] = src[((int64_t)(h * kKvbHead + d) * kLora + cb * kColBlock) / 8 + v];
-        }
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(bar, kWukBytes);
+        tma_load_3d(w_s, &tmap_kvb, bar, 0, h * kKvbHead, 0, kCacheEvictLast);
     }
-    for (int i = threadIdx.x; i < kNope * kReqBlock; i += kK1Threads) {
-        const int r = i / kNope, d = i % kNope;
-        q_s[d][r] = r < nreq ? __bfloat162float(q[(int64_t)(b0 + r) * p.q_stride + h * kQHead + d]) : 0.f;
+    // q_nope [16][128] -> shared, 256-byte rows with 16-byte units XOR (row & 7)
+    const uint32_t qb = smem_u32(q_s);
+    {
+        const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);
+        for (int i = threadIdx.x; i < kReqBlock * (kNope / 2); i += kK1Threads) {
+            const int r = i / (kNope / 2), c2 = 2 * (i % (kNope / 2));
+            uint32_t v = 0u;
+            if (r < nreq) v = *reinterpret_cast<const uint32_t*>(q + (int64_t)(b0 + r) * p.q_stride + h * kQHead + c2);
+            *reinterpret_cast<uint32_t*>(q_s + r * 256 + ((((c2 >> 3) ^ (r & 7))) << 4) + (c2 & 7) * 2) = v;
+        }
     }
     __syncthreads();
-    const int col = threadIdx.x;
-    float acc[kReqBlock];
+    {
+        int dummy = 0;
+        if (!mbar_wait(bar, 0, &dummy, p.error_word)) return;
+    }
+    // D[16 requests][512] = A[16][128 d] x W_UK[h][128 d][512]; warp w owns columns [128w, 128w+128)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;
+    const uint32_t wb = smem_u32(w_s);
+    float acc[16][4];
 #pragma unroll
-    for (int r = 0; r < kReqBlock; ++r) acc[r] = 0.f;
-#pragma unroll 4
-    for (int d = 0; d < kNope; ++d) {
-        const float w = __bfloat162float(w_s[d][col]);
-        const float4* q4 = reinterpret_cast<const float4*>(&q_s[d][0]);
+    for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
 #pragma unroll
-        for (int r4 = 0; r4 < kReqBlock / 4; ++r4) {
-            const float4 qq = q4[r4];
-            acc[4 * r4 + 0] = fmaf(qq.x, w, acc[4 * r4 + 0]);
-            acc[4 * r4 + 1] = fmaf(qq.y, w, acc[4 * r4 + 1]);
-            acc[4 * r4 + 2] = fmaf(qq.z, w, acc[4 * r4 + 2]);
-            acc[4 * r4 + 3] = fmaf(qq.w, w, acc[4 * r4 + 3]);
+    for (int ks = 0; ks < kNope / 16; ++ks) {
+        uint32_t a[4];
+        {
+            const int row = (m8 & 1) * 8 + r8, col = 16 * ks + (m8 >> 1) * 8;
+            ldsm_x4(qb + row * 256 + ((((col >> 3) ^ (row & 7))) << 4), a[0], a[1], a[2], a[3]);
+        }
+        const int d = 16 * ks + (m8 & 1) * 8 + r8;
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {  // latent tiles 2np, 2np+1 of this warp
+            const int l = 128 * warp + 16 * np + (m8 >> 1) * 8;
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4_t(wb + (l >> 6) * (kNope * 128) + d * 128 + ((((l & 63) >> 3) ^ r8) << 4), b00, b01, b10, b11);
+            mma16816(acc[2 * np], a, b00, b01);
+            mma16816(acc[2 * np + 1], a, b10, b11);
         }
     }
 #pragma unroll
-    for (int r = 0; r < kReqBlock; ++r)
-        if (r < nreq) qa[((int64_t)(b0 + r) * kQRows + h) * kRow + cb * kColBlock + col] = __float2bfloat16_rn(acc[r]);
+    for (int n = 0; n < 16; ++n) {
+        const int l = 128 * warp + 8 * n + 2 * t4;
+        if (gq < nreq)
+            *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + gq) * kQRows + h) * kRow + l) = pack_bf16(acc[n][0], acc[n][1]);
+        if (gq + 8 < nreq)
+            *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + gq + 8) * kQRows + h) * kRow + l) =
+                pack_bf16(acc[n][2], acc[n][3]);
+    }
 }
 
-cudaError_t launch_prologue(const MlaDecodeParams& p, cudaStream_t stream) {
+cudaError_t k1_configure() {
+    return cudaFuncSetAttribute(k1_prologue, cudaFuncAttributeMaxDynamicSharedMemorySize, kK1SmemBytes);
+}
+
+cudaError_t launch_prologue(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream) {
     const K1Grid g(p.batch);
-    k1_prologue<<<g.total, kK1Threads, 0, stream>>>(p);
+    k1_prologue<<<g.total, kK1Threads, kK1SmemBytes, stream>>>(p, tmap_kvb);
     return cudaGetLastError();
 }
 
