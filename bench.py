@@ -76,7 +76,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
             time.sleep(0.3)
@@ -276,11 +276,6 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     out_host = torch.empty(B, 2048, dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty_like(x_n)
 
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        fleet.attention_absorbed(runner.cfg, runner.w, x_dev, cache, runner=runner)
-        out_host.copy_(out, non_blocking=True)
-
     def e2e_step_real():
         x_dev.copy_(x_host, non_blocking=True)
         o = runner(x_dev, cache, out)
@@ -324,7 +319,7 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         "attn_tokens_per_s_27_layers": round(world * B / (27 * us * 1e-6), 1),
         "stages_us": {"prologue": round(k1_ms * 1e3, 2), "attention": round(k2_ms * 1e3, 2),
                       "merge_uv": round(k3_ms * 1e3, 2)},
-        "roofline": {"bound": "hbm", "kernel": "k2_attention_tc", "achieved": round(k2_gbs, 1), "peak": peak,
+        "roofline": {"bound": "hbm", "kernel": "k2_attention_mma", "achieved": round(k2_gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(k2_gbs / peak, 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": kv_b, "peak_source": peak_src},
         "cpu_baseline": cpu,
@@ -340,7 +335,7 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="config5a", choices=sorted(workloads.WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
