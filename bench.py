@@ -227,6 +227,10 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
+    if args.workload == "config5b" and world > 1:
+        run_sequence_sharded(args, rank, world, local_rank, dev, dist)
+        return
+
     wl, lengths, runner, cache, x_n, q, kv_a = build_workload(args.workload, dev, rank)
     B = len(lengths)
     out = torch.empty(B, 2048, dtype=torch.bfloat16, device=dev)
@@ -327,6 +331,75 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                 "h2d_bytes_per_step": int(x_n.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2),
                 "path": "attention_absorbed-style call: pinned x_n H2D, cuBLAS q|kv_a, K1-K3, R(out) D2H"},
         "gpu_launches": native.load_library().mla_launches_per_step() * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torch.device, dist) -> None:
+    """Config 5b across `world` GPUs: one 131,072-token sequence split by page-aligned KV
+    ranges; per step K1+K2+K3 on each range, one NCCL all-gather of the 8.4 KB partials
+    and the fixed-order combine (distributed.py). Total work is fixed: strong scaling."""
+    dmod = importlib.import_module("fleet-mi300x_b200.distributed")
+    wl = workloads.WORKLOADS["config5b"]
+    T = wl.seq_lens()[0]
+    cfg = fleet.ModelConfig()
+    lw = workloads.make_layer_weights(wl.seed)
+    w = fleet.LayerWeights(*(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm,
+                                                   lw.kv_b_proj)))
+    cos, sin = fleet.device_rope_tables(cfg, T + 8, dev)
+    a, b = dmod.sequence_shards(T, world)[rank]
+    last = rank == world - 1
+    cache = fleet.PagedLatentCache.for_lengths([b - a], extra_tokens=1 if last else 0, permute=True, zero=False,
+                                               generator=torch.Generator().manual_seed(wl.seed + rank), device=dev)
+    workloads.fill_pool_random(cache.pages, wl.seed + 1000 * rank)
+    runner = fleet.MlaDecodeAttention(cfg, w, cos, sin)
+    x_n = workloads.make_hidden(wl.seed + 1, 1).to(dev)
+    q, kv_a = (t.contiguous() for t in runner.project(x_n))
+    pos = torch.tensor([T], dtype=torch.int32, device=dev)
+    local = torch.empty(1, 16, native.SHARD_STRIDE, dtype=torch.float32, device=dev)
+    parts = torch.empty(world, 1, 16, native.SHARD_STRIDE, dtype=torch.float32, device=dev)
+    out = torch.empty(1, 2048, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        runner.attend(q, kv_a, cache, rope_pos=pos, shard_out=local, new_row=last)
+        dist.all_gather_into_tensor(parts, local)
+        fleet.combine_shards(parts, out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    runner.check_errors()
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms = time_loop(step, args.steps, stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    runner.check_errors()
+    kv_b = workloads.kv_bytes([T])
+    peak, _ = measured_peak()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = kv_b / (ms_max * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents, N(0,0.02) weights)",
+        "config": {"workload": "config5b", "batch": 1, "context": T, "page_size": 64,
+                   "parallelism": f"sequence-sharded x{world}: page-aligned KV ranges, NCCL all-gather of "
+                                  f"{16 * native.SHARD_STRIDE * 4} B partials per GPU, fixed-order combine",
+                   "kv_bytes_per_step": kv_b, "kv_bytes_per_gpu": kv_b // world,
+                   "l2": "per-GPU range %.0f MB" % (kv_b / world / 1e6)},
+        "us_per_layer_step": round(ms_max * 1e3, 3),
+        "kv_frac_of_hbm_peak_per_gpu": round(value / world / peak, 4),
+        "gpu_launches": (native.load_library().mla_launches_per_step() + 1) * args.steps,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

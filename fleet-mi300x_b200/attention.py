@@ -50,6 +50,12 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def _row_stride(t: torch.Tensor) -> int:
+    """Elements between rows of a [B, n] tensor. For B = 1 torch may report any
+    stride for the batch dimension (0 for a broadcast view), so use the row length."""
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1]
+
+
 class MlaDecodeAttention:
     """One layer's attention task over a PagedLatentCache.
 
@@ -82,7 +88,8 @@ class MlaDecodeAttention:
 
     # ------------------------------------------------------------------ params
     def params(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
-               out: torch.Tensor) -> native.MlaDecodeParams:
+               out: torch.Tensor | None, *, rope_pos: torch.Tensor | None = None,
+               shard_out: torch.Tensor | None = None, new_row: bool = True) -> native.MlaDecodeParams:
         B = q.shape[0]
         p = native.new_params()
         p.softmax_scale = self.cfg.softmax_scale
@@ -91,18 +98,21 @@ class MlaDecodeAttention:
         p.max_blocks = cache.max_blocks
         p.n_pages = cache.n_pages
         p.max_pos = self.cos.shape[0]
-        p.q, p.q_stride = _ptr(q), q.stride(0)
-        p.kv_a, p.kv_a_stride = _ptr(kv_a), kv_a.stride(0)
+        p.q, p.q_stride = _ptr(q), _row_stride(q)
+        p.kv_a, p.kv_a_stride = _ptr(kv_a), _row_stride(kv_a)
         p.kv_a_norm_w = _ptr(self.norm_w)
         p.kv_b = _ptr(self.kv_b)
         p.rope_cos, p.rope_sin = _ptr(self.cos), _ptr(self.sin)
         p.block_table = _ptr(cache.block_table)
         p.seq_lens = _ptr(cache.seq_lens)
         p.kv_cache = _ptr(cache.pages)
-        p.out, p.out_stride = _ptr(out), out.stride(0)
+        p.out = _ptr(out)
+        p.out_stride = _row_stride(out) if out is not None else self.cfg.heads * self.cfg.v_head
         p.error_word = _ptr(self.error_word)
         p.num_ctas = self.num_ctas
-        p.flags = self.flags
+        p.flags = self.flags | (0 if new_row else native.FLAG_NO_NEW_ROW)
+        p.rope_pos = _ptr(rope_pos)
+        p.shard_out = _ptr(shard_out)
         need = ctypes.c_uint64()
         native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
         if self._ws is None or self._ws.numel() < need.value:
@@ -116,24 +126,37 @@ class MlaDecodeAttention:
             raise TypeError("q and kv_a must be bf16")
         if q.shape[0] != cache.batch or kv_a.shape[0] != cache.batch:
             raise ValueError(f"batch {q.shape[0]} does not match the cache's {cache.batch} requests")
+        if q.dim() != 2 or kv_a.dim() != 2 or q.shape[1] != self.cfg.heads * self.cfg.q_head_dim or \
+                kv_a.shape[1] != self.cfg.kv_lora_rank + self.cfg.qk_rope:
+            raise ValueError(f"q must be [B, 3072] and kv_a [B, 576], got {tuple(q.shape)} and {tuple(kv_a.shape)}")
         if q.stride(-1) != 1 or kv_a.stride(-1) != 1:
             raise ValueError("q and kv_a rows must be contiguous")
 
     # ------------------------------------------------------------------ calls
     def attend(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
-               out: torch.Tensor | None = None, stage: str = "all") -> torch.Tensor:
+               out: torch.Tensor | None = None, stage: str = "all", *, rope_pos: torch.Tensor | None = None,
+               shard_out: torch.Tensor | None = None, new_row: bool = True) -> torch.Tensor:
         """K1+K2+K3 from q [B, 3072] and kv_a [B, 576] (bf16 views allowed).
-        Appends each request's row at seq_lens[b]; does not advance seq_lens."""
+        Appends each request's row at seq_lens[b]; does not advance seq_lens.
+
+        Sequence-sharded use: `rope_pos` gives the new token's global position,
+        `new_row=False` marks a shard that does not own the new token, and
+        `shard_out` (f32 [B, 16, 132]) receives this shard's partial instead of
+        R(out); combine the gathered partials with `combine_shards`."""
         self._check_inputs(q, kv_a, cache)
-        if out is None:
+        if shard_out is not None:
+            if shard_out.dtype != torch.float32 or tuple(shard_out.shape) != (q.shape[0], 16, native.SHARD_STRIDE):
+                raise ValueError(f"shard_out must be f32 [{q.shape[0]}, 16, {native.SHARD_STRIDE}]")
+            out = None
+        elif out is None:
             out = torch.empty(q.shape[0], self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16,
                               device=self.device)
-        p = self.params(q, kv_a, cache, out)
+        p = self.params(q, kv_a, cache, out, rope_pos=rope_pos, shard_out=shard_out, new_row=new_row)
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         fn = {"all": self.lib.mla_decode_step, "prologue": self.lib.mla_prologue,
               "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv}[stage]
-        native.check(fn(ctypes.byref(p), stream), f"mla {stage}")
-        return out
+        native.check(fn(ctypes.byref(p), stream), f"mla {stage}", p)
+        return out if shard_out is None else shard_out
 
     def project(self, x_n: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """q = R(W_q x_n), kv_a = R(W_kv_a x_n) as views of one bf16 GEMM output."""
@@ -161,6 +184,22 @@ class MlaDecodeAttention:
         need = ctypes.c_uint64()
         native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
         return int(need.value)
+
+
+def combine_shards(parts: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fixed-order LSE combine of gathered shard partials f32 [n_shards, B, 16, 132]
+    (sequence order) into R(out) bf16 [B, 2048] (libmla_decode.so: mla_combine_shards)."""
+    if parts.dtype != torch.float32 or parts.dim() != 4 or parts.shape[2:] != (16, native.SHARD_STRIDE):
+        raise ValueError("parts must be f32 [n_shards, B, 16, 132]")
+    parts = parts.contiguous()
+    n, B = parts.shape[0], parts.shape[1]
+    if out is None:
+        out = torch.empty(B, 2048, dtype=torch.bfloat16, device=parts.device)
+    lib = native.load_library()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(parts.device).cuda_stream)
+    native.check(lib.mla_combine_shards(parts.data_ptr(), n, B, out.data_ptr(), _row_stride(out), stream),
+                 "mla_combine_shards")
+    return out
 
 
 def attention_absorbed(cfg: ModelConfig, w: LayerWeights, x_n: torch.Tensor, cache: PagedLatentCache,

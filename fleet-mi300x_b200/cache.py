@@ -49,8 +49,8 @@ class PagedLatentCache:
         `permute` (the fragmented layout of a long-running server)."""
         lengths = [int(x) for x in lengths]
         need = [(n + extra_tokens + PAGE_SIZE - 1) // PAGE_SIZE for n in lengths]
-        total = sum(need) + spare_pages
-        max_blocks = max(need)
+        total = max(1, sum(need) + spare_pages)
+        max_blocks = max(1, max(need))
         cache = cls(total, len(lengths), max_blocks, device=device, zero=zero)
         order = (torch.randperm(total, generator=generator) if permute else torch.arange(total))
         order = order.to(torch.int32)

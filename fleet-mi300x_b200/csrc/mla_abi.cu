@@ -19,6 +19,8 @@ cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tma
 cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream);
 cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream);
 cudaError_t k1_configure();
+cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,
+                                  cudaStream_t stream);
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
                                  cudaStream_t stream);
 cudaError_t k2_configure();
@@ -150,8 +152,9 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
     int st = check_header(p);
     if (st != MLA_OK) return st;
     if (!p->q || !p->kv_a || !p->kv_a_norm_w || !p->kv_b || !p->rope_cos || !p->rope_sin || !p->block_table ||
-        !p->seq_lens || !p->kv_cache || !p->out || !p->workspace)
+        !p->seq_lens || !p->kv_cache || (!p->out && !p->shard_out) || !p->workspace)
         return MLA_E_INVALID_ARG;
+    if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW)) return MLA_E_INVALID_ARG;
     if (p->max_blocks <= 0 || p->n_pages <= 0 || p->max_pos <= 0) return MLA_E_INVALID_ARG;
     if ((int64_t)p->n_pages * MLA_PAGE_SIZE > INT32_MAX || (int64_t)p->batch * p->max_blocks > INT32_MAX)
         return MLA_E_LIMIT;
@@ -161,7 +164,8 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
     if (!(p->softmax_scale > 0.f) || !(p->rms_eps >= 0.f)) return MLA_E_INVALID_ARG;
     if (!aligned(p->kv_cache, 16) || !aligned(p->kv_b, 16) || !aligned(p->workspace, 256) ||
         !aligned(p->q, 4) || (p->q_stride & 1) || (p->out_stride & 1) || !aligned(p->kv_a, 2) || !aligned(p->out, 4) || !aligned(p->kv_a_norm_w, 2) ||
-        !aligned(p->rope_cos, 4) || !aligned(p->rope_sin, 4))
+        !aligned(p->rope_cos, 4) || !aligned(p->rope_sin, 4) || !aligned(p->rope_pos, 4) ||
+        !aligned(p->shard_out, 16))
         return MLA_E_MISALIGNED;
     int sms = 0;
     st = device_info(&sms);
@@ -261,6 +265,19 @@ int mla_plan_info(const MlaDecodeParams* p, int32_t* num_ctas, int32_t* num_slot
 }
 
 int mla_launches_per_step(void) { return 3; }
+
+int mla_combine_shards(const float* parts, int32_t n_shards, int32_t batch, void* out, int64_t out_stride,
+                       void* stream) {
+    if (!parts || !out || n_shards <= 0 || batch <= 0 || out_stride < MLA_HEADS * MLA_V_HEAD || (out_stride & 1))
+        return MLA_E_INVALID_ARG;
+    if (n_shards > 4096 || batch > MLA_MAX_BATCH) return MLA_E_LIMIT;
+    if (!aligned(parts, 16) || !aligned(out, 4)) return MLA_E_MISALIGNED;
+    const int st = device_info(nullptr);
+    if (st != MLA_OK) return st;
+    return launch_combine_shards(parts, n_shards, batch, out, out_stride, (cudaStream_t)stream) == cudaSuccess
+               ? MLA_OK
+               : MLA_E_LAUNCH;
+}
 
 int mla_prologue(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;

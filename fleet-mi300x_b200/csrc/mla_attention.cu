@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
     volatile int* abort = &S.abort;
 
     TileCursor cur;
-    cur.init(cum, p.seq_lens, p.batch, u_begin, u_end);
+    cur.init(cum, p.seq_lens, p.batch, u_begin, u_end, new_row_count(p));
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(kCkThreads)
     const int c = blockIdx.x;
     if (c >= G) return;
     TileCursor cur;
-    cur.init(cum, p.seq_lens, p.batch, plan_begin(c, U, G), plan_begin(c + 1, U, G));
+    cur.init(cum, p.seq_lens, p.batch, plan_begin(c, U, G), plan_begin(c + 1, U, G), new_row_count(p));
 
     const int h = threadIdx.x >> 4, part = threadIdx.x & 15;  // head, 32-column slice of the latent
     float acc[32];

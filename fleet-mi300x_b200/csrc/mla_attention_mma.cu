@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     volatile int* abort = &S.abort;
 
     TileCursor cur;
-    cur.init(cum, p.seq_lens, p.batch, u_begin, u_end);
+    cur.init(cum, p.seq_lens, p.batch, u_begin, u_end, new_row_count(p));
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         bool ok = true;
         for (; cur.valid(); cur.next(), ++i) {
             const bool first = cur.first(), last = cur.last();
-            if (first) rows_b = p.seq_lens[cur.b] + 1;
+            if (first) rows_b = p.seq_lens[cur.b] + new_row_count(p);
             const int valid = min(kPage, rows_b - cur.page_index() * kPage);
             if (first) {
                 const __nv_bfloat16* qrow = qa + (int64_t)cur.b * kQRows * kRow + 144 * w + 2 * t4;

@@ -63,6 +63,19 @@ __host__ __device__ inline int plan_cta_of(int64_t u, int64_t U, int G) {
 }
 
 // ---------------------------------------------------------------------------
+// Per-request positions. The new token's row is stored at local row seq_lens[b]
+// and attended unless MLA_FLAG_NO_NEW_ROW (a sequence shard that does not own
+// it); its RoPE position is rope_pos[b] when given (the global position of a
+// sequence-sharded step), else seq_lens[b].
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int new_row_count(const MlaDecodeParams& p) {
+    return (p.flags & MLA_FLAG_NO_NEW_ROW) ? 0 : 1;
+}
+__device__ __forceinline__ int rope_position(const MlaDecodeParams& p, int b) {
+    return p.rope_pos ? p.rope_pos[b] : p.seq_lens[b];
+}
+
+// ---------------------------------------------------------------------------
 // Error word: first error wins.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void record_error(int32_t* w, int code) {

@@ -26,8 +26,55 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kWBytes = kV * kLora * 2;          // 131072: [8 column blocks][128 rows][128 B], swizzled
 constexpr int kABytes = kReq * kLora * 2;        // 16384: [16 requests][512] bf16, 1024-byte rows, swizzled
-constexpr int kSmemBytes = kWBytes + 2 * kABytes + 64 + 1024;
+constexpr int kSmemBytes = kWBytes + 2 * kABytes + 64 + kWarps * kLora * 4 + 1024;
 }  // namespace k3
+
+// Partial slot s = (c + b) * heads + h: its (m, L) pair and the lane's four
+// float4 of acc (latent l = 4 lane + 128 k, k < 4).
+__device__ __forceinline__ void load_partial(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
+                                             int b, int h, int c, int lane, float2& ml, float4 (&a)[4]) {
+    const int64_t s = (int64_t)(c + b) * kHeads + h;
+    ml = *reinterpret_cast<const float2*>(part_ml + s * 2);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) a[k] = reinterpret_cast<const float4*>(part_acc + s * kLora)[lane + 32 * k];
+}
+
+// One step of the online LSE merge: running max m (log2 domain), rescaled sum of
+// exps L and unnormalised acc absorb the partial (ml.x = its max, ml.y = its sum).
+__device__ __forceinline__ void fold_partial(float2 ml, const float4 (&a)[4], float& m, float& L, float4 (&acc)[4]) {
+    const float mn = fmaxf(m, ml.x);
+    const float so = exp2f(m - mn), sc = exp2f(ml.x - mn);
+    L = L * so + sc * ml.y;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        acc[k].x = acc[k].x * so + sc * a[k].x;
+        acc[k].y = acc[k].y * so + sc * a[k].y;
+        acc[k].z = acc[k].z * so + sc * a[k].z;
+        acc[k].w = acc[k].w * so + sc * a[k].w;
+    }
+    m = mn;
+}
+
+// Fold of the partials c = first, first + stride, ... <= last of (request b,
+// head h), in order. Loads are issued four partials at a time.
+__device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
+                                               int b, int h, int first, int last, int stride, int lane, float& m,
+                                               float& L, float4 (&acc)[4]) {
+    m = -INFINITY;
+    L = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int cc = first; cc <= last; cc += 4 * stride) {
+        float2 ml[4];
+        float4 a[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (cc + j * stride <= last) load_partial(part_ml, part_acc, b, h, cc + j * stride, lane, ml[j], a[j]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (cc + j * stride <= last) fold_partial(ml[j], a[j], m, L, acc);
+    }
+}
 
 // Address of element (row, col) of a [rows][512] bf16 matrix stored as 1024-byte
 // rows whose 16-byte units are XOR-swizzled with (row & 7) (conflict-free ldmatrix).
@@ -66,71 +113,99 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     }
 
     // ---- merge: o_c[r][l] = sum_c w_c acc_c[l] / sum_c w_c l_c ----
-    // One pass over the partials in CTA order (running max, rescaled sums); the
-    // next partial's loads are issued before the current one is folded in.
-    // Warp w merges requests w and w+8; lane owns l = 4 lane + 128 k (k < 4).
+    // Every fold visits partials in CTA order; requests without tiles (invalid
+    // position) get a zero o_c.
     __shared__ int32_t cum_s[kReq + 1];
+    __shared__ float red_ml[kWarps][2];
     if (threadIdx.x <= kReq) cum_s[threadIdx.x] = cum[min(b0 + (int)threadIdx.x, p.batch)];
     __syncthreads();
     const uint32_t ahi = smem_u32(a_hi), alo = smem_u32(a_lo);
-    {
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    auto part_range = [&](int r, int& c0, int& c1) -> bool {
+        if (r >= nreq || cum_s[r + 1] <= cum_s[r]) return false;  // invalid position: no tiles
+        c0 = plan_cta_of(cum_s[r], U, G);
+        c1 = plan_cta_of(cum_s[r + 1] - 1, U, G);
+        return true;
+    };
+    // o_c -> bf16 hi/lo operands of request r; lane owns l = 4 lane + 128 k
+    auto store_oc = [&](int r, const float4 (&acc)[4], float inv_L) {
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-            const int r = warp + kWarps * rr;
-            const int b = b0 + r;
-            float4 acc[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-            float inv_L = 0.f;
-            if (r < nreq && cum_s[r + 1] > cum_s[r]) {  // a request with an invalid position has no tiles
-                const int c0 = plan_cta_of(cum_s[r], U, G), c1 = plan_cta_of(cum_s[r + 1] - 1, U, G);
-                int64_t sidx = (int64_t)(c0 + b) * kHeads + h;
-                float2 ml = *reinterpret_cast<const float2*>(part_ml + sidx * 2);
-                float4 cur[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) cur[k] = reinterpret_cast<const float4*>(part_acc + sidx * kLora)[lane + 32 * k];
-                float m = -INFINITY, L = 0.f;
-                for (int cc = c0; cc <= c1; ++cc) {
-                    float2 ml_n = ml;
-                    float4 nxt[4];
-                    if (cc < c1) {
-                        const int64_t sn = (int64_t)(cc + 1 + b) * kHeads + h;
-                        ml_n = *reinterpret_cast<const float2*>(part_ml + sn * 2);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) nxt[k] = reinterpret_cast<const float4*>(part_acc + sn * kLora)[lane + 32 * k];
-                    }
-                    const float mn = fmaxf(m, ml.x);
-                    const float so = exp2f(m - mn), sc = exp2f(ml.x - mn);
-                    L = L * so + sc * ml.y;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        acc[k].x = acc[k].x * so + sc * cur[k].x;
-                        acc[k].y = acc[k].y * so + sc * cur[k].y;
-                        acc[k].z = acc[k].z * so + sc * cur[k].z;
-                        acc[k].w = acc[k].w * so + sc * cur[k].w;
-                    }
-                    m = mn;
-                    if (cc < c1) {
-                        ml = ml_n;
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
-                    }
-                }
-                inv_L = 1.f / L;
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float o0 = acc[k].x * inv_L, o1 = acc[k].y * inv_L, o2 = acc[k].z * inv_L, o3 = acc[k].w * inv_L;
-                const float h0 = bf16_round(o0), h1 = bf16_round(o1), h2 = bf16_round(o2), h3 = bf16_round(o3);
-                const int col = 4 * lane + 128 * k;
-                uint2 vh, vl;
-                vh.x = pack_bf16(h0, h1); vh.y = pack_bf16(h2, h3);
-                vl.x = pack_bf16(o0 - h0, o1 - h1); vl.y = pack_bf16(o2 - h2, o3 - h3);
-                *reinterpret_cast<uint2*>(a_hi + (swz1024(ahi, r, col) - ahi)) = vh;
-                *reinterpret_cast<uint2*>(a_lo + (swz1024(alo, r, col) - alo)) = vl;
-            }
+        for (int k = 0; k < 4; ++k) {
+            const float o0 = acc[k].x * inv_L, o1 = acc[k].y * inv_L, o2 = acc[k].z * inv_L, o3 = acc[k].w * inv_L;
+            const float h0 = bf16_round(o0), h1 = bf16_round(o1), h2 = bf16_round(o2), h3 = bf16_round(o3);
+            const int col = 4 * lane + 128 * k;
+            uint2 vh, vl;
+            vh.x = pack_bf16(h0, h1); vh.y = pack_bf16(h2, h3);
+            vl.x = pack_bf16(o0 - h0, o1 - h1); vl.y = pack_bf16(o2 - h2, o3 - h3);
+            *reinterpret_cast<uint2*>(a_hi + (swz1024(ahi, r, col) - ahi)) = vh;
+            *reinterpret_cast<uint2*>(a_lo + (swz1024(alo, r, col) - alo)) = vl;
         }
+    };
+    auto store_ml = [&](int r, float m, float L) {
+        if (p.shard_out && r < nreq && lane == 0) {
+            float* so = p.shard_out + ((int64_t)(b0 + r) * kHeads + h) * MLA_SHARD_STRIDE;
+            so[kV] = m;
+            so[kV + 1] = L;
+        }
+    };
+
+    // Warps per request: the largest power of two <= 8 / nreq (8 for one request,
+    // 1 for 5 or more). A group of wpr warps folds request r's partials c0 + wi,
+    // c0 + wi + wpr, ... (wi = warp within the group), then the group's warp
+    // results are combined through shared memory in warp order.
+    for (int i = threadIdx.x; i < (kReq - nreq) * (kLora / 8); i += kThreads) {  // rows past nreq: zero operands
+        const int r = nreq + i / (kLora / 8), col = (i % (kLora / 8)) * 8;
+        *reinterpret_cast<uint4*>(a_hi + (swz1024(ahi, r, col) - ahi)) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(a_lo + (swz1024(alo, r, col) - alo)) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    const int wpr = nreq == 1 ? 8 : nreq == 2 ? 4 : nreq <= 4 ? 2 : 1;
+    const int groups = kWarps / wpr, gi = warp / wpr, wi = warp % wpr;
+    const int iters = (nreq + groups - 1) / groups;
+    float* red_acc = reinterpret_cast<float*>(bar + 2);  // [kWarps][512] f32, 16-B aligned after the barrier
+#pragma unroll 1
+    for (int it = 0; it < iters; ++it) {  // uniform trip count: the barriers below are CTA-wide
+        const int r = gi + it * groups;
+        int c0 = 0, c1 = -1;
+        float4 acc[4];
+        float m = -INFINITY, L = 0.f;
+        if (part_range(r, c0, c1) && c0 + wi <= c1)
+            merge_partials(part_ml, part_acc, b0 + r, h, c0 + wi, c1, wpr, lane, m, L, acc);
+        else
+            for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (wpr == 1) {
+            if (r < nreq) {
+                store_ml(r, m, L);
+                store_oc(r, acc, L > 0.f ? 1.f / L : 0.f);
+            }
+            continue;
+        }
+        if (lane == 0) { red_ml[warp][0] = m; red_ml[warp][1] = L; }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<float4*>(red_acc + warp * kLora + 4 * lane + 128 * k) = acc[k];
+        __syncthreads();
+        if (wi == 0 && r < nreq) {
+            const int w0 = warp;
+            float gm = -INFINITY;
+            for (int v = 0; v < wpr; ++v) gm = fmaxf(gm, red_ml[w0 + v][0]);
+            float Lt = 0.f;
+            float4 tot[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tot[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int v = 0; v < wpr; ++v) {
+                const float wv = red_ml[w0 + v][1] > 0.f ? exp2f(red_ml[w0 + v][0] - gm) : 0.f;
+                Lt = fmaf(wv, red_ml[w0 + v][1], Lt);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 x = *reinterpret_cast<const float4*>(red_acc + (w0 + v) * kLora + 4 * lane + 128 * k);
+                    tot[k].x = fmaf(wv, x.x, tot[k].x); tot[k].y = fmaf(wv, x.y, tot[k].y);
+                    tot[k].z = fmaf(wv, x.z, tot[k].z); tot[k].w = fmaf(wv, x.w, tot[k].w);
+                }
+            }
+            store_ml(r, gm, Lt);
+            store_oc(r, tot, Lt > 0.f ? 1.f / Lt : 0.f);
+        }
+        __syncthreads();
     }
     __syncthreads();
     {
@@ -139,7 +214,6 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     }
 
     // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l]; warp w owns v in [16w, 16w+16) ----
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;
     const uint32_t wb = smem_u32(w_s);
     float acc[2][4];
@@ -164,6 +238,19 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
             mma16816(acc[1], al, b10, b11);
         }
     }
+    if (p.shard_out) {  // sequence-sharded step: fp32 y = W_UV o_c / L of this shard
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            const int v = 16 * warp + 8 * n + 2 * t4;
+            if (g < nreq)
+                *reinterpret_cast<float2*>(p.shard_out + ((int64_t)(b0 + g) * kHeads + h) * MLA_SHARD_STRIDE + v) =
+                    make_float2(acc[n][0], acc[n][1]);
+            if (g + 8 < nreq)
+                *reinterpret_cast<float2*>(p.shard_out + ((int64_t)(b0 + g + 8) * kHeads + h) * MLA_SHARD_STRIDE + v) =
+                    make_float2(acc[n][2], acc[n][3]);
+        }
+        return;
+    }
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
         const int v = 16 * warp + 8 * n + 2 * t4;
@@ -174,6 +261,46 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
             *reinterpret_cast<uint32_t*>(out + (int64_t)(b0 + g + 8) * p.out_stride + h * kV + v) =
                 pack_bf16(acc[n][2], acc[n][3]);
     }
+}
+
+// Cross-shard combine of a sequence-sharded step (parts gathered from all GPUs):
+// out[b][128h + v] = bf16( sum_r w_r y_r[v] / sum_r w_r ), w_r = L_r 2^(m_r - max m),
+// shards folded in order. Block = request, thread = (head, 8 values of v).
+__global__ void __launch_bounds__(256) k4_combine_shards(const float* __restrict__ parts, int n_shards, int batch,
+                                                         __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+    const int b = blockIdx.x;
+    const int h = threadIdx.x >> 4, v0 = (threadIdx.x & 15) * 8;
+    const int64_t shard_stride = (int64_t)batch * kHeads * MLA_SHARD_STRIDE;
+    const float* base = parts + ((int64_t)b * kHeads + h) * MLA_SHARD_STRIDE;
+    float gm = -INFINITY;
+    for (int r = 0; r < n_shards; ++r) gm = fmaxf(gm, base[r * shard_stride + kV]);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float W = 0.f;
+    for (int r = 0; r < n_shards; ++r) {
+        const float* pr = base + r * shard_stride;
+        const float Lr = pr[kV + 1];
+        if (!(Lr > 0.f)) continue;  // an empty shard contributes nothing
+        const float w = Lr * exp2f(pr[kV] - gm);
+        W += w;
+        const float4 y0 = *reinterpret_cast<const float4*>(pr + v0);
+        const float4 y1 = *reinterpret_cast<const float4*>(pr + v0 + 4);
+        acc[0] = fmaf(w, y0.x, acc[0]); acc[1] = fmaf(w, y0.y, acc[1]);
+        acc[2] = fmaf(w, y0.z, acc[2]); acc[3] = fmaf(w, y0.w, acc[3]);
+        acc[4] = fmaf(w, y1.x, acc[4]); acc[5] = fmaf(w, y1.y, acc[5]);
+        acc[6] = fmaf(w, y1.z, acc[6]); acc[7] = fmaf(w, y1.w, acc[7]);
+    }
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+    __nv_bfloat16* o = out + (int64_t)b * out_stride + h * kV + v0;
+#pragma unroll
+    for (int k = 0; k < 8; k += 2)
+        *reinterpret_cast<uint32_t*>(o + k) = pack_bf16(acc[k] * inv, acc[k + 1] * inv);
+}
+
+cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,
+                                  cudaStream_t stream) {
+    k4_combine_shards<<<batch, 256, 0, stream>>>(parts, n_shards, batch, reinterpret_cast<__nv_bfloat16*>(out),
+                                                out_stride);
+    return cudaGetLastError();
 }
 
 cudaError_t k3_configure() {

@@ -52,8 +52,11 @@ __device__ __forceinline__ void rope_pair(float x_even, float x_odd, const float
     hi = __fadd_rn(__fmul_rn(x_odd, cs[32 + j]), __fmul_rn(x_even, sn[32 + j]));
 }
 
-__device__ __forceinline__ bool position_ok(const MlaDecodeParams& p, int pos) {
-    return pos >= 0 && pos < p.max_pos && pos < p.max_blocks * kPage;
+// Request b is valid if its RoPE position lies in the tables and its rows
+// (cached + the new one, if this call stores it) fit its block-table row.
+__device__ __forceinline__ bool request_ok(const MlaDecodeParams& p, int b) {
+    const int rows = p.seq_lens[b], rp = rope_position(p, b);
+    return rows >= 0 && rp >= 0 && rp < p.max_pos && rows + new_row_count(p) <= p.max_blocks * kPage;
 }
 
 // Prefix sum of tiles per request (one CTA). Invalid positions are recorded
@@ -67,9 +70,8 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum) {
         const int b = base + threadIdx.x;
         int n = 0;
         if (b < p.batch) {
-            const int pos = p.seq_lens[b];
-            if (!position_ok(p, pos)) record_error(p.error_word, MLA_DEV_BAD_POSITION);
-            else n = (pos + 1 + kPage - 1) / kPage;
+            if (!request_ok(p, b)) record_error(p.error_word, MLA_DEV_BAD_POSITION);
+            else n = (p.seq_lens[b] + new_row_count(p) + kPage - 1) / kPage;
         }
         int incl = n;
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -90,12 +92,14 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum) {
     if (threadIdx.x == 0) cum[p.batch] = carry;
 }
 
-// One warp: kv_post + cache append + q_pe RoPE of request b.
+// One warp: q_pe RoPE of request b, then (unless the call stores no row)
+// kv_post + the cache append at local row seq_lens[b].
 __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b, int lane) {
+    if (!request_ok(p, b)) return;  // recorded by the planner
     const int pos = p.seq_lens[b];
-    if (!position_ok(p, pos)) return;  // recorded by the planner
-    const float* cs = p.rope_cos + (int64_t)pos * kRope;
-    const float* sn = p.rope_sin + (int64_t)pos * kRope;
+    const int rp = rope_position(p, b);
+    const float* cs = p.rope_cos + (int64_t)rp * kRope;
+    const float* sn = p.rope_sin + (int64_t)rp * kRope;
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q) + (int64_t)b * p.q_stride;
     const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride;
     const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w);
@@ -110,6 +114,7 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
         qrow[h * kRow + kLora + lane] = __float2bfloat16_rn(lo);
         qrow[h * kRow + kLora + 32 + lane] = __float2bfloat16_rn(hi);
     }
+    if (!new_row_count(p)) return;
 
     // kv_post (reference_decode.py:60-65): var = mean(x^2); y = x * (1 / sqrt(var + eps));
     // row = bf16(bf16(y) * weight). Lane owns c[16*lane, 16*lane+16).

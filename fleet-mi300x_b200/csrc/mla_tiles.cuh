@@ -15,9 +15,10 @@ struct TileCursor {
     int b;
     int64_t cb0, cb1;  // cum[b], cum[b+1]
     int seg;
+    int extra;  // 1 if the new token's row is part of the attended rows
 
-    __device__ void init(const int32_t* cum_, const int32_t* sl, int B, int64_t ub, int64_t ue) {
-        cum = cum_; seq_lens = sl; batch = B; u = ub; u_begin = ub; u_end = ue; seg = 0;
+    __device__ void init(const int32_t* cum_, const int32_t* sl, int B, int64_t ub, int64_t ue, int extra_ = 1) {
+        cum = cum_; seq_lens = sl; batch = B; u = ub; u_begin = ub; u_end = ue; seg = 0; extra = extra_;
         // largest b with cum[b] <= u (upper_bound - 1); skips empty requests
         int lo = 0, hi = B;  // cum[B] > u
         while (hi - lo > 1) {
@@ -29,7 +30,7 @@ struct TileCursor {
     __device__ bool valid() const { return u < u_end; }
     __device__ int page_index() const { return (int)(u - cb0); }
     __device__ int tokens() const {  // valid tokens in this 64-token tile
-        const int L = seq_lens[b] + 1;
+        const int L = seq_lens[b] + extra;
         return min(kPage, L - page_index() * kPage);
     }
     __device__ bool first() const { return u == u_begin || u == cb0; }

@@ -13,13 +13,15 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libmla_decode.so"
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 HEADS, QK_NOPE, QK_ROPE, V_HEAD, KV_LORA, PAGE_SIZE = 16, 128, 64, 128, 512, 64
 ROW = KV_LORA + QK_ROPE
 MAX_BATCH = 65536
 
 FLAG_CHECK_KERNEL = 0x2
 FLAG_TCGEN05 = 0x4
+FLAG_NO_NEW_ROW = 0x8
+SHARD_STRIDE = 132
 
 STATUS = {
     0: "MLA_OK", -1: "MLA_E_INVALID_ARG", -2: "MLA_E_UNSUPPORTED_DIMS", -3: "MLA_E_MISALIGNED",
@@ -30,16 +32,20 @@ DEV_ERRORS = {0: "ok", 1: "MLA_DEV_BAD_PAGE", 2: "MLA_DEV_BAD_POSITION", 3: "MLA
 EXPORTED = (
     "mla_abi_version", "mla_status_string", "mla_device_error_string", "mla_params_init",
     "mla_workspace_size", "mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv",
-    "mla_plan_info", "mla_launches_per_step",
+    "mla_plan_info", "mla_launches_per_step", "mla_combine_shards",
 )
 
 
 class MlaError(RuntimeError):
     """A nonzero mla_status from the C ABI, or a device error word."""
 
-    def __init__(self, code: int, what: str):
+    def __init__(self, code: int, what: str, params: "MlaDecodeParams | None" = None):
         self.code = code
-        super().__init__(f"{what}: {STATUS.get(code, DEV_ERRORS.get(code, code))} ({code})")
+        msg = f"{what}: {STATUS.get(code, DEV_ERRORS.get(code, code))} ({code})"
+        if params is not None:
+            fields = ", ".join(f"{n}={getattr(params, n)}" for n, _ in params._fields_)
+            msg += f" [params: {fields}]"
+        super().__init__(msg)
 
 
 class MlaDecodeParams(ctypes.Structure):
@@ -62,6 +68,7 @@ class MlaDecodeParams(ctypes.Structure):
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
         ("error_word", ctypes.c_void_p),
         ("num_ctas", ctypes.c_int32), ("flags", ctypes.c_int32),
+        ("rope_pos", ctypes.c_void_p), ("shard_out", ctypes.c_void_p),
     ]
 
 
@@ -94,6 +101,9 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.mla_plan_info.restype = ctypes.c_int
         lib.mla_plan_info.argtypes = [P, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]
         lib.mla_launches_per_step.restype = ctypes.c_int
+        lib.mla_combine_shards.restype = ctypes.c_int
+        lib.mla_combine_shards.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                           ctypes.c_int64, ctypes.c_void_p]
         for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv"):
             f = getattr(lib, fn)
             f.restype = ctypes.c_int
@@ -105,9 +115,9 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         return lib
 
 
-def check(code: int, what: str) -> None:
+def check(code: int, what: str, params: "MlaDecodeParams | None" = None) -> None:
     if code != 0:
-        raise MlaError(code, what)
+        raise MlaError(code, what, params)
 
 
 def new_params() -> MlaDecodeParams:

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define MLA_ABI_VERSION 1
+#define MLA_ABI_VERSION 2
 
 /* Fixed model dimensions. The reference's launcher refuses any other shape
  * (src/host/fleet_launch.hip:573-577: kv_lora != 512 or qk_rope != 64);
@@ -87,6 +87,8 @@ typedef enum {
 #define MLA_FLAG_TCGEN05 0x4      /* run the split-KV kernel that keeps scores and the output in tensor
                                      memory (tcgen05.mma, tokens on M, heads on N) instead of the default
                                      m16n8k16 kernel (heads on M); same plan and partial layout */
+#define MLA_FLAG_NO_NEW_ROW 0x8   /* sequence-sharded decode, a shard that does not own the new token:
+                                     store no row and attend over cache rows 0..seq_lens[b]-1 only */
 
 typedef struct MlaDecodeParams {
     uint32_t struct_size; /* sizeof(MlaDecodeParams) */
@@ -118,7 +120,17 @@ typedef struct MlaDecodeParams {
     int32_t* error_word;      /* optional device int32 (0 = no error); may be NULL */
     int32_t num_ctas;         /* CTAs of the split-KV kernel; 0 = one per SM */
     int32_t flags;            /* MLA_FLAG_* */
+
+    /* Sequence-sharded decode (one long sequence split over GPUs by KV range). */
+    const int32_t* rope_pos;  /* optional [batch]: RoPE position of the new token (the global position);
+                                 NULL = seq_lens[b] */
+    float* shard_out;         /* optional: if set, K3 writes this shard's partial instead of `out`:
+                                 f32 [batch][16][MLA_SHARD_STRIDE] = y[128] (W_UV o_c / L, normalised
+                                 within the shard), m (log2-domain max), L (sum of exps), 2 unused;
+                                 16-byte aligned */
 } MlaDecodeParams;
+
+#define MLA_SHARD_STRIDE (MLA_V_HEAD + 4)
 
 #define MLA_MAX_BATCH 65536
 
@@ -159,6 +171,15 @@ int mla_plan_info(const MlaDecodeParams* p, int32_t* num_ctas, int32_t* num_slot
 
 /* Number of kernel launches one mla_decode_step makes (for launch accounting). */
 int mla_launches_per_step(void);
+
+/* Combine the shard partials of a sequence-sharded step after they were
+ * gathered from all GPUs: parts f32 [n_shards][batch][16][MLA_SHARD_STRIDE]
+ * (shard order = sequence order). out[b][128h + v] = bf16(sum_r w_r y_r[v] /
+ * sum_r w_r), w_r = L_r * 2^(m_r - max_r m_r), in shard order. The same LSE
+ * merge the reference runs over its KV chunks (src/kernels/attention.h:358-401),
+ * one level up; there the chunks never leave one GPU. */
+int mla_combine_shards(const float* parts, int32_t n_shards, int32_t batch, void* out, int64_t out_stride,
+                       void* stream);
 
 #ifdef __cplusplus
 }

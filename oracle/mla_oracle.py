@@ -252,3 +252,40 @@ def attention_task_paged(cfg: Config, w: Weights, q: np.ndarray, kv_a: np.ndarra
         out[b] = attend(cfg, w, q[b].reshape(cfg.heads, cfg.q_head_dim), rows, pos, cos, sin)
         new_rows[b] = row
     return out, new_rows
+
+
+# ------------------------------------------------------------------ sequence shards (multi-GPU protocol)
+
+def attend_rows_partial(cfg: Config, w: Weights, q: np.ndarray, rows: np.ndarray, pos: int, cos, sin):
+    """One shard's contribution for one token: rows [S, 576] of the shard (S may be 0).
+    Returns (y [H, Dv], m [H], L [H]) with m the log2-domain max of scaled scores,
+    L = sum 2^(s - m) and y = W_UV (sum 2^(s - m) c) / L: the per-chunk (m, l, acc) of
+    attention.h:230-351 with W_UV applied (it is linear), as exchanged between GPUs."""
+    H, Dk, Dv, L = cfg.heads, cfg.qk_nope, cfg.v_head, cfg.kv_lora_rank
+    if rows.shape[0] == 0:
+        return np.zeros((H, Dv), np.float32), np.full(H, -np.inf, np.float32), np.zeros(H, np.float32)
+    q_nope, q_pe = q[:, :Dk], q[:, Dk:]
+    q_pe = cfg.r(apply_rope(q_pe, cos[pos][None, :], sin[pos][None, :]))
+    kvb = w.kv_b_proj.reshape(H, Dk + Dv, L)
+    q_c = np.einsum("hd,hdl->hl", q_nope, kvb[:, :Dk])
+    qa = np.concatenate([q_c, q_pe], axis=1)
+    s2 = (rows @ qa.T).astype(np.float64) * cfg.softmax_scale * np.log2(np.e)   # [S, H]
+    m = s2.max(axis=0)
+    e = np.exp2(s2 - m)
+    Lsum = e.sum(axis=0)
+    o_c = (e.T @ rows[:, :L]) / Lsum[:, None]
+    y = np.einsum("hvl,hl->hv", kvb[:, Dk:], o_c)
+    return y.astype(np.float32), m.astype(np.float32), Lsum.astype(np.float32)
+
+
+def combine_partials(parts):
+    """Fixed-order LSE combine of per-shard (y, m, L) into R(out) [H*Dv] (shard order)."""
+    ms = np.stack([p[1] for p in parts]).astype(np.float64)       # [R, H]
+    gm = ms.max(axis=0)
+    acc = 0.0
+    W = 0.0
+    for y, m, Lr in parts:
+        w = np.where(Lr > 0, Lr * np.exp2(m.astype(np.float64) - gm), 0.0)
+        acc = acc + w[:, None] * y
+        W = W + w
+    return bf16_round((acc / W[:, None]).reshape(-1).astype(np.float32))

@@ -113,3 +113,12 @@ def test_no_cpu_path_without_cuda_tensors():
     cos, sin = fleet.rope_tables(cfg, 16)
     with pytest.raises(RuntimeError):
         fleet.MlaDecodeAttention(cfg, lw, torch.from_numpy(cos), torch.from_numpy(sin))
+
+
+def test_row_stride_of_single_row_views():
+    att = importlib.import_module("fleet-mi300x_b200.attention")
+    import numpy as np
+    v = torch.from_numpy(np.zeros(576, np.float32)[None])  # NumPy broadcast view: batch stride 0
+    assert v.stride(0) == 0 and att._row_stride(v) == 576
+    w = torch.zeros(4, 3648)[:, :3072]
+    assert att._row_stride(w) == 3648
