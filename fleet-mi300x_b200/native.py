@@ -22,6 +22,7 @@ FLAG_CHECK_KERNEL = 0x2
 FLAG_TCGEN05 = 0x4
 FLAG_NO_NEW_ROW = 0x8
 SHARD_STRIDE = 132
+STATIC_SCRATCH_BYTES = 32 << 20  # MLA_STATIC_SCRATCH_BYTES, the workspace of mla_decode_step_static
 
 STATUS = {
     0: "MLA_OK", -1: "MLA_E_INVALID_ARG", -2: "MLA_E_UNSUPPORTED_DIMS", -3: "MLA_E_MISALIGNED",
@@ -32,7 +33,7 @@ DEV_ERRORS = {0: "ok", 1: "MLA_DEV_BAD_PAGE", 2: "MLA_DEV_BAD_POSITION", 3: "MLA
 EXPORTED = (
     "mla_abi_version", "mla_status_string", "mla_device_error_string", "mla_params_init",
     "mla_workspace_size", "mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv",
-    "mla_plan_info", "mla_launches_per_step", "mla_combine_shards",
+    "mla_plan_info", "mla_launches_per_step", "mla_combine_shards", "mla_decode_step_static",
 )
 
 
@@ -104,7 +105,7 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.mla_combine_shards.restype = ctypes.c_int
         lib.mla_combine_shards.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                            ctypes.c_int64, ctypes.c_void_p]
-        for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv"):
+        for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv", "mla_decode_step_static"):
             f = getattr(lib, fn)
             f.restype = ctypes.c_int
             f.argtypes = [P, ctypes.c_void_p]

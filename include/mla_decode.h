@@ -181,6 +181,32 @@ int mla_launches_per_step(void);
 int mla_combine_shards(const float* parts, int32_t n_shards, int32_t batch, void* out, int64_t out_stride,
                        void* stream);
 
+/* Size of the workspace that mla_decode_step_static keeps inside the library, per
+ * device: 32 MiB, which holds mla_workspace_size() for up to 558 requests at 148
+ * CTAs (one per SM of a B200). */
+#define MLA_STATIC_SCRATCH_BYTES (32ull << 20)
+
+/* No counterpart in the reference: its launcher allocates every buffer itself
+ * before the token loop (fleet_launch.hip:223-237), so it never needed this.
+ *
+ * mla_decode_step with the workspace taken from a device array inside the library
+ * (MLA_STATIC_SCRATCH_BYTES per device) instead of from the caller. p->workspace
+ * and p->workspace_bytes are ignored; every other field means what it means for
+ * mla_decode_step, and the same kernels run. It calls no cudaMalloc, cudaFree or
+ * other allocating routine. It is for callers that cannot allocate device memory
+ * on the decode path: a server that sized its paged KV pool to all the HBM left
+ * after the weights has none left for a per-step workspace, and a C or FFI host
+ * without a caching allocator would otherwise pay a cudaMalloc/cudaFree (and the
+ * device-wide synchronisation of cudaFree) per decoded token whenever the batch grows.
+ *
+ * Returns MLA_E_LIMIT, before any launch, when mla_workspace_size(p) exceeds
+ * MLA_STATIC_SCRATCH_BYTES. Nothing in the scratch has to start at zero (each
+ * step writes everything it reads). The scratch is one per device and shared by
+ * every call on that device: calls that overlap on the GPU (on streams not
+ * ordered with one another, or from several host threads) race on it. Order
+ * them on one stream or with events. */
+int mla_decode_step_static(const MlaDecodeParams* p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
