@@ -236,6 +236,9 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     out = torch.empty(B, 2048, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
     step = lambda: runner.attend(q, kv_a, cache, out)
+    if args.sweep_splits:
+        run_split_sweep(args, runner, cache, q, kv_a, lengths, stream)
+        return
 
     # warm-up (also JIT-free: the library is prebuilt)
     for _ in range(max(3, args.warmup)):
@@ -405,6 +408,42 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
     print(json.dumps(line), flush=True)
 
 
+def run_split_sweep(args, runner, cache, q, kv_a, lengths, stream) -> None:
+    """Split-count sweep (one GPU): the whole step, K2 alone and the LSE merge + W_UV (K3)
+    alone at each CTA count of the split-KV plan. Every output is checked against the
+    default plan's (one CTA per SM) before it is timed. Prints one JSON line."""
+    kv_b = workloads.kv_bytes(lengths)
+    B = len(lengths)
+    lib = runner.lib
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    runner.num_ctas = 0
+    ref = runner.attend(q, kv_a, cache).float()
+    rows = []
+    for n in args.sweep_splits:
+        runner.num_ctas = n
+        out = torch.empty(B, 2048, dtype=torch.bfloat16, device=q.device)
+        for _ in range(max(3, args.warmup)):
+            runner.attend(q, kv_a, cache, out)
+        runner.check_errors()
+        rel = float(((out.float() - ref).abs().max() / ref.abs().max()).item())
+        if rel > 1e-2:
+            raise RuntimeError(f"split count {n}: output differs from the default plan's (max rel {rel:.3e})")
+        step_ms = time_loop(lambda: runner.attend(q, kv_a, cache, out), args.steps, stream)
+        p = runner.params(q, kv_a, cache, out)
+        k2_ms = time_loop(lambda: lib.mla_attention(ctypes.byref(p), sptr), args.steps, stream)
+        k3_ms = time_loop(lambda: lib.mla_merge_uv(ctypes.byref(p), sptr), args.steps, stream)
+        ctas, slots = ctypes.c_int32(), ctypes.c_int32()
+        native.check(lib.mla_plan_info(ctypes.byref(p), ctypes.byref(ctas), ctypes.byref(slots)), "plan_info")
+        # a request's tiles are cut at CTA boundaries: at most (ctas + B - 1) segments in all
+        rows.append({"num_ctas": ctas.value, "partials_per_request_max_avg": round((ctas.value + B - 1) / B, 2),
+                     "step_us": round(step_ms * 1e3, 2), "attention_us": round(k2_ms * 1e3, 2),
+                     "merge_uv_us": round(k3_ms * 1e3, 2), "kv_gbs": round(kv_b / (step_ms * 1e-3) / 1e9, 1),
+                     "max_rel_vs_default": rel})
+    runner.num_ctas = 0
+    print(json.dumps({"sweep": "split count", "workload": args.workload, "batch": B,
+                      "kv_bytes": kv_b, "rows": rows}), flush=True)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -414,6 +453,9 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep-splits", type=lambda v: [int(x) for x in v.split(",")], default=None,
+                    help="comma-separated CTA counts of the split plan, e.g. 1,2,4,8,16,32,64,148; "
+                         "prints a sweep line instead of the bench line (one GPU)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
