@@ -148,6 +148,41 @@ def time_loop(fn, steps: int, stream: torch.cuda.Stream) -> float:
     return start.elapsed_time(end) / steps
 
 
+L2_BYTES = 126e6
+
+
+class StepTimer:
+    """CUDA-event timing of repeated calls on the launching stream. When a step reads
+    less than 4x L2 of cache rows, 256 MB are written between timed calls (outside the
+    timed events, one event pair per call) so that no call finds the previous one's
+    rows in L2."""
+
+    def __init__(self, stream: torch.cuda.Stream, kv_bytes: int, device):
+        self.stream = stream
+        self.flush = (torch.empty(256 << 20, dtype=torch.uint8, device=device)
+                      if kv_bytes < 4 * L2_BYTES else None)
+        self.kv_bytes = kv_bytes
+
+    def __call__(self, fn, steps: int) -> float:
+        if self.flush is None:
+            return time_loop(fn, steps, self.stream)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda.synchronize()
+        for a, b in evs:
+            self.flush.zero_()
+            a.record(self.stream)
+            fn()
+            b.record(self.stream)
+        evs[-1][1].synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+    def describe(self) -> str:
+        if self.flush is None:
+            return "no flush: each step reads %.0f MB of cache rows, > 4x the 126 MB L2" % (self.kv_bytes / 1e6)
+        return ("L2 flushed: 256 MB written before every timed step, outside its CUDA events "
+                "(the step reads %.1f MB of cache rows)" % (self.kv_bytes / 1e6))
+
+
 def cpu_oracle_sample(name: str, budget_s: float, faithful: bool) -> dict:
     """Times the CPU oracle on a bounded sample of the workload's requests."""
     from oracle import mla_oracle as O
@@ -244,6 +279,21 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     for _ in range(max(3, args.warmup)):
         step()
     runner.check_errors()
+    kv_b = workloads.kv_bytes(lengths)
+    timer = StepTimer(stream, kv_b, dev)
+
+    # The product's step for a decode loop: K1-K3 captured once as a CUDA graph
+    # (DecodeGraph, PDL edges between the kernels) and replayed; it must reproduce
+    # the eager step bit for bit before it is timed.
+    out_g = torch.empty_like(out)
+    graph = fleet.DecodeGraph(runner, cache, inputs="qkv", q=q, kv_a=kv_a, out=out_g)
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    step()
+    torch.cuda.synchronize()
+    if not torch.equal(out_g, out):
+        raise RuntimeError("graph step output differs from the eager step")
+    runner.check_errors()
 
     # ---- timed region: K steps of the whole task, inputs resident
     clocks = ClockSampler(local_rank)
@@ -251,18 +301,18 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
-        ms = time_loop(step, args.steps, stream)
+        ms = timer(graph.replay, args.steps)
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
+        ms_eager = timer(step, args.steps)
     ms_max = ms
     if dist:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms, ms_eager], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+        ms_max, ms_eager = float(t[0].item()), float(t[1].item())
     runner.check_errors()
 
-    kv_b = workloads.kv_bytes(lengths)
     tot_b = workloads.total_bytes(lengths)
     value = world * kv_b / (ms_max * 1e-3) / 1e9
 
@@ -271,9 +321,9 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     sptr = ctypes.c_void_p(stream.cuda_stream)
     lib = runner.lib
     native.check(lib.mla_prologue(ctypes.byref(p), sptr), "prologue")
-    k1_ms = time_loop(lambda: lib.mla_prologue(ctypes.byref(p), sptr), max(5, args.steps), stream)
-    k2_ms = time_loop(lambda: lib.mla_attention(ctypes.byref(p), sptr), max(5, args.steps), stream)
-    k3_ms = time_loop(lambda: lib.mla_merge_uv(ctypes.byref(p), sptr), max(5, args.steps), stream)
+    k1_ms = timer(lambda: lib.mla_prologue(ctypes.byref(p), sptr), max(5, args.steps))
+    k2_ms = timer(lambda: lib.mla_attention(ctypes.byref(p), sptr), max(5, args.steps))
+    k3_ms = timer(lambda: lib.mla_merge_uv(ctypes.byref(p), sptr), max(5, args.steps))
     peak, peak_src = measured_peak()
     k2_gbs = kv_b / (k2_ms * 1e-3) / 1e9
     traffic = ncu_traffic(args.workload)
@@ -292,7 +342,7 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         e2e_step_real()
     if dist:
         dist.barrier()
-    e2e_ms = time_loop(e2e_step_real, args.steps, stream)
+    e2e_ms = timer(e2e_step_real, args.steps)
     if dist:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -318,10 +368,11 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                                                                             else [min(lengths), max(lengths)]),
                    "page_size": 64, "block_table": "permuted" if wl.permute else "contiguous",
                    "parallelism": f"by-request x{world}" if world > 1 else "single GPU",
-                   "kv_bytes_per_gpu_step": kv_b,
-                   "l2": "no flush: each step reads %.0f MB of cache rows, > 126 MB L2" % (kv_b / 1e6)
-                   if kv_b > 126e6 else "inputs smaller than L2; steps re-read from L2"},
+                   "kv_bytes_per_gpu_step": kv_b, "l2": timer.describe(),
+                   "step": "K1-K3 replayed as one CUDA graph (DecodeGraph); eager_ms_per_step is the same "
+                           "step launched through the C ABI call by call"},
         "us_per_layer_step": round(us, 3),
+        "eager_ms_per_step": round(ms_eager, 5),
         "kv_frac_of_hbm_peak": round(value / world / peak, 4),
         "attn_tokens_per_s_27_layers": round(world * B / (27 * us * 1e-6), 1),
         "stages_us": {"prologue": round(k1_ms * 1e3, 2), "attention": round(k2_ms * 1e3, 2),
@@ -373,18 +424,19 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
     for _ in range(max(3, args.warmup)):
         step()
     runner.check_errors()
+    kv_b = workloads.kv_bytes([T])
+    timer = StepTimer(stream, kv_b // world, dev)
     clocks = ClockSampler(local_rank)
     with clocks:
         dist.barrier()
         torch.cuda.synchronize()
-        ms = time_loop(step, args.steps, stream)
+        ms = timer(step, args.steps)
         torch.cuda.synchronize()
         dist.barrier()
     t = torch.tensor([ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     runner.check_errors()
-    kv_b = workloads.kv_bytes([T])
     peak, _ = measured_peak()
     dist.barrier()
     dist.destroy_process_group()
@@ -399,7 +451,7 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
                    "parallelism": f"sequence-sharded x{world}: page-aligned KV ranges, NCCL all-gather of "
                                   f"{16 * native.SHARD_STRIDE * 4} B partials per GPU, fixed-order combine",
                    "kv_bytes_per_step": kv_b, "kv_bytes_per_gpu": kv_b // world,
-                   "l2": "per-GPU range %.0f MB" % (kv_b / world / 1e6)},
+                   "l2": timer.describe()},
         "us_per_layer_step": round(ms_max * 1e3, 3),
         "kv_frac_of_hbm_peak_per_gpu": round(value / world / peak, 4),
         "gpu_launches": (native.load_library().mla_launches_per_step() + 1) * args.steps,
@@ -416,6 +468,7 @@ def run_split_sweep(args, runner, cache, q, kv_a, lengths, stream) -> None:
     B = len(lengths)
     lib = runner.lib
     sptr = ctypes.c_void_p(stream.cuda_stream)
+    timer = StepTimer(stream, kv_b, q.device)
     runner.num_ctas = 0
     ref = runner.attend(q, kv_a, cache).float()
     rows = []
@@ -428,10 +481,10 @@ def run_split_sweep(args, runner, cache, q, kv_a, lengths, stream) -> None:
         rel = float(((out.float() - ref).abs().max() / ref.abs().max()).item())
         if rel > 1e-2:
             raise RuntimeError(f"split count {n}: output differs from the default plan's (max rel {rel:.3e})")
-        step_ms = time_loop(lambda: runner.attend(q, kv_a, cache, out), args.steps, stream)
+        step_ms = timer(lambda: runner.attend(q, kv_a, cache, out), args.steps)
         p = runner.params(q, kv_a, cache, out)
-        k2_ms = time_loop(lambda: lib.mla_attention(ctypes.byref(p), sptr), args.steps, stream)
-        k3_ms = time_loop(lambda: lib.mla_merge_uv(ctypes.byref(p), sptr), args.steps, stream)
+        k2_ms = timer(lambda: lib.mla_attention(ctypes.byref(p), sptr), args.steps)
+        k3_ms = timer(lambda: lib.mla_merge_uv(ctypes.byref(p), sptr), args.steps)
         ctas, slots = ctypes.c_int32(), ctypes.c_int32()
         native.check(lib.mla_plan_info(ctypes.byref(p), ctypes.byref(ctas), ctypes.byref(slots)), "plan_info")
         # a request's tiles are cut at CTA boundaries: at most (ctas + B - 1) segments in all
@@ -440,7 +493,7 @@ def run_split_sweep(args, runner, cache, q, kv_a, lengths, stream) -> None:
                      "merge_uv_us": round(k3_ms * 1e3, 2), "kv_gbs": round(kv_b / (step_ms * 1e-3) / 1e9, 1),
                      "max_rel_vs_default": rel})
     runner.num_ctas = 0
-    print(json.dumps({"sweep": "split count", "workload": args.workload, "batch": B,
+    print(json.dumps({"sweep": "split count", "workload": args.workload, "batch": B, "l2": timer.describe(),
                       "kv_bytes": kv_b, "rows": rows}), flush=True)
 
 

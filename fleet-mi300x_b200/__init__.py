@@ -12,10 +12,11 @@ The directory name is not a Python identifier; import it with
 from .config import ModelConfig, rope_tables, yarn_cos_sin, yarn_get_mscale
 from .cache import PagedLatentCache
 from .attention import LayerWeights, MlaDecodeAttention, attention_absorbed, combine_shards, device_rope_tables
+from .graph import DecodeGraph
 from .native import MlaError, load_library
 
 __all__ = [
     "ModelConfig", "rope_tables", "yarn_cos_sin", "yarn_get_mscale", "PagedLatentCache",
     "LayerWeights", "MlaDecodeAttention", "attention_absorbed", "combine_shards", "device_rope_tables",
-    "MlaError", "load_library",
+    "DecodeGraph", "MlaError", "load_library",
 ]

@@ -8,7 +8,7 @@ head-concatenated bf16 output R(out) before o_proj (:256):
 
     q, kv_a      = R(W_q x_n), R(W_kv_a x_n)       cuBLAS bf16 GEMM (torch), one fused [W_q; W_kv_a]
     K1 prologue  kv_post + cache append + q_pe RoPE + q_c = q_nope W_UK      (libmla_decode.so)
-    K2 attention split-KV scores, online softmax, P c_kv on tcgen05         (libmla_decode.so)
+    K2 attention split-KV scores, online softmax, P c_kv (m16n8k16 MMAs)    (libmla_decode.so)
     K3 merge     fixed-order LSE merge + W_UV up-projection, bf16 out       (libmla_decode.so)
 
 Everything after the GEMM runs in the C-ABI library; there is no CPU path.
@@ -85,6 +85,8 @@ class MlaDecodeAttention:
         self.flags = native.FLAG_CHECK_KERNEL if check_kernel else (native.FLAG_TCGEN05 if kernel == "tcgen05" else 0)
         self.error_word = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ws: torch.Tensor | None = None
+        self._step_key: tuple | None = None   # attend(): params of the last call, reused for the same tensors
+        self._step_p: native.MlaDecodeParams | None = None
 
     # ------------------------------------------------------------------ params
     def params(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
@@ -151,7 +153,14 @@ class MlaDecodeAttention:
         elif out is None:
             out = torch.empty(q.shape[0], self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16,
                               device=self.device)
-        p = self.params(q, kv_a, cache, out, rope_pos=rope_pos, shard_out=shard_out, new_row=new_row)
+        key = (q.data_ptr(), _row_stride(q), kv_a.data_ptr(), _row_stride(kv_a), cache.pages.data_ptr(),
+               cache.block_table.data_ptr(), cache.seq_lens.data_ptr(), cache.n_pages, cache.max_blocks,
+               q.shape[0], _ptr(out), None if out is None else _row_stride(out), _ptr(rope_pos), _ptr(shard_out),
+               new_row, self.flags, self.num_ctas, self.cos.data_ptr(), self.cos.shape[0], self.kv_b.data_ptr())
+        p = self._step_p
+        if key != self._step_key or self._ws is None or p.workspace != self._ws.data_ptr():
+            p = self.params(q, kv_a, cache, out, rope_pos=rope_pos, shard_out=shard_out, new_row=new_row)
+            self._step_key, self._step_p = key, p
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         fn = {"all": self.lib.mla_decode_step, "prologue": self.lib.mla_prologue,
               "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv}[stage]

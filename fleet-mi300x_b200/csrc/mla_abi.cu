@@ -95,14 +95,15 @@ int make_tmap_blocks(CUtensorMap* m, const void* base, uint64_t rows_or_pages, b
 }
 
 // kv_b (16*256 rows x 512 bf16) as 128-row blocks of W_UK / W_UV: dims {64
-// columns, 4096 rows (1024 B), 8 column blocks (128 B)}, box {64, 128, 8} =
-// one 128 KB request landing as [8][128 rows][128 B] with the 128-byte swizzle.
-int make_tmap_kvb(CUtensorMap* m, const void* kv_b) {
+// columns, 4096 rows (1024 B), 8 column blocks (128 B)}, box {64, 128, blocks}
+// = one request of blocks x 16 KB landing as [blocks][128 rows][128 B] with the
+// 128-byte swizzle (8 blocks: a whole 128 x 512 head block; 2: a quarter of it).
+int make_tmap_kvb(CUtensorMap* m, const void* kv_b, int blocks) {
     PFN_cuTensorMapEncodeTiled_v12000 fn;
     if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
     cuuint64_t dims[3] = {64, (cuuint64_t)kHeads * kKvbHead, 8};
     cuuint64_t strides[2] = {(cuuint64_t)kLora * 2, 128};
-    cuuint32_t box[3] = {64, 128, 8};
+    cuuint32_t box[3] = {64, 128, (cuuint32_t)blocks};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(kv_b), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -112,14 +113,14 @@ int make_tmap_kvb(CUtensorMap* m, const void* kv_b) {
 
 int run_prologue(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap t;
-    const int st = make_tmap_kvb(&t, q.kv_b);
+    const int st = make_tmap_kvb(&t, q.kv_b, kK1WukBlocks);
     if (st != MLA_OK) return st;
     return launch_prologue(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 int run_merge(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap t;
-    const int st = make_tmap_kvb(&t, q.kv_b);
+    const int st = make_tmap_kvb(&t, q.kv_b, 8);
     if (st != MLA_OK) return st;
     return launch_merge_uv(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }

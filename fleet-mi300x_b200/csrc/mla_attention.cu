@@ -92,6 +92,8 @@ __global__ void __launch_bounds__(kK2Threads, 1)
     float* part_ml = reinterpret_cast<float*>(wsb + ws.part_ml);
     float* part_acc = reinterpret_cast<float*>(wsb + ws.part_acc);
 
+    pdl_trigger();
+    pdl_wait();  // the plan, absorbed queries and new rows come from K1
     const int64_t U = cum[p.batch];
     const int G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
     const int c = blockIdx.x;
@@ -171,7 +173,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
             const uint64_t dMN = smem_desc_sw128(0, kChunkBytes, 1024);  // MN-major, 64-column blocks 8 KB apart
             const int n_tiles = (int)(u_end - u_begin);
             struct TileInfo { bool first, last; int seg; };
-            TileInfo info[4];
+            TileInfo info[4] = {};  // entry t & 3 is written by the score step of tile t before P of t exists
             int qk_j = 0, pv_next = 0;
 
             auto pv_step = [&]() -> bool {
@@ -438,6 +440,8 @@ __global__ void __launch_bounds__(kCkThreads)
     float* part_acc = reinterpret_cast<float*>(wsb + ws.part_acc);
     const __nv_bfloat16* cache = reinterpret_cast<const __nv_bfloat16*>(p.kv_cache);
 
+    pdl_trigger();
+    pdl_wait();  // the plan, absorbed queries and new rows come from K1
     const int64_t U = cum[p.batch];
     const int G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
     const int c = blockIdx.x;
@@ -529,12 +533,16 @@ cudaError_t k2_configure() {
 
 cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, const CUtensorMap& tmap_q,
                                 float scale_log2, cudaStream_t stream) {
-    k2_attention_tc<<<p.num_ctas, kK2Threads, kK2SmemBytes, stream>>>(p, tmap_kv, tmap_q, scale_log2);
+    const cudaError_t e = launch_pdl(k2_attention_tc, dim3(p.num_ctas), dim3(kK2Threads), kK2SmemBytes, stream, p,
+                                     tmap_kv, tmap_q, scale_log2);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream) {
-    k2_attention_check<<<p.num_ctas, kCkThreads, kCkSmemBytes, stream>>>(p, scale_log2);
+    const cudaError_t e = launch_pdl(k2_attention_check, dim3(p.num_ctas), dim3(kCkThreads), kCkSmemBytes, stream, p,
+                                     scale_log2);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

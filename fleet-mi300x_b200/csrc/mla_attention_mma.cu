@@ -86,6 +86,8 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     float* part_ml = reinterpret_cast<float*>(wsb + ws.part_ml);
     float* part_acc = reinterpret_cast<float*>(wsb + ws.part_acc);
 
+    pdl_trigger();
+    pdl_wait();  // the plan, absorbed queries and new rows come from K1
     const int64_t U = cum[p.batch];
     const int G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
     const int c = blockIdx.x;
@@ -135,7 +137,6 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         float m_run[2], l_run[2];              // heads g, g+8
         int rows_b = 0;                        // rows attended by the current request (seq_lens[b] + 1)
         int i = 0;
-        bool ok = true;
         for (; cur.valid(); cur.next(), ++i) {
             const bool first = cur.first(), last = cur.last();
             if (first) rows_b = p.seq_lens[cur.b] + new_row_count(p);
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 l_run[0] = l_run[1] = 0.f;
             }
             const uint32_t slot = (uint32_t)i % kNTile;
-            if (!mbar_wait(&S.tile_full[slot], ((uint32_t)i / kNTile) & 1, abort, p.error_word)) { ok = false; break; }
+            if (!mbar_wait(&S.tile_full[slot], ((uint32_t)i / kNTile) & 1, abort, p.error_word)) break;
             const uint32_t tbase = tile_addr + slot * kTileBytes;
 
             // ---- partial scores over this warp's 144 columns, all 64 tokens ----
@@ -309,7 +310,6 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 // at least one more tile's barriers, which every warp passes after this read
             }
         }
-        (void)ok;
         (void)cw_tid;
     }
     __syncthreads();
@@ -323,7 +323,9 @@ cudaError_t k2_mma_configure() {
 
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
                                  cudaStream_t stream) {
-    k2_attention_mma<<<p.num_ctas, mmak::kThreads, mmak::kSmemBytes, stream>>>(p, tmap_kv, scale_log2);
+    const cudaError_t e = launch_pdl(k2_attention_mma, dim3(p.num_ctas), dim3(mmak::kThreads), mmak::kSmemBytes,
+                                     stream, p, tmap_kv, scale_log2);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -6,6 +6,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <utility>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -23,6 +24,8 @@ constexpr int kPage = MLA_PAGE_SIZE;       // 64
 constexpr int kQHead = kNope + kRope;      // 192: q row per head
 constexpr int kKvbHead = kNope + kV;       // 256: kv_b rows per head
 constexpr int kQRows = kHeads;             // rows of the absorbed query per request in the workspace
+constexpr int kK1LatQ = 128;               // latent columns of W_UK per prologue CTA (a quarter)
+constexpr int kK1WukBlocks = kK1LatQ / 64; // 64-column blocks of that slice (its TMA box)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ---------------------------------------------------------------------------
@@ -50,6 +53,32 @@ __host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas) {
     w.part_acc = off;  off = align256(off + uint64_t(w.slots) * kHeads * kLora * 4);
     w.total = off;
     return w;
+}
+
+// Programmatic dependent launch. A kernel launched with launch_pdl may start
+// while the kernel before it on the stream is still running; pdl_wait() returns
+// once that kernel has completed and its writes are visible, so it must come
+// before any read of data an earlier kernel writes and before any write an
+// earlier kernel may still read. pdl_trigger() lets the next PDL kernel launch
+// as soon as every CTA of this one has issued it. Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Split plan: the CTA grid shares the flattened list of tiles of all requests

@@ -102,15 +102,17 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     const int h = blockIdx.x;
     const int b0 = blockIdx.y * kReq;
     const int nreq = min(kReq, p.batch - b0);
-    const int64_t U = cum[p.batch];
-    const int G = (int)(U < 1 ? 1 : (U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas));
 
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0) {  // W_UV is a weight: no kernel writes it, so it may load before pdl_wait
         mbar_init(bar, 1);
         fence_mbar_init();
         mbar_arrive_expect_tx(bar, kWBytes);
         tma_load_3d(w_s, &tmap_kvb, bar, 0, h * kKvbHead + kNope, 0, kCacheEvictLast);
     }
+    pdl_trigger();
+    pdl_wait();  // partials from K2, plan from K1
+    const int64_t U = cum[p.batch];
+    const int G = (int)(U < 1 ? 1 : (U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas));
 
     // ---- merge: o_c[r][l] = sum_c w_c acc_c[l] / sum_c w_c l_c ----
     // Every fold visits partials in CTA order; requests without tiles (invalid
@@ -309,8 +311,7 @@ cudaError_t k3_configure() {
 
 cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream) {
     dim3 grid(kHeads, (p.batch + k3::kReq - 1) / k3::kReq);
-    k3_merge_uv<<<grid, k3::kThreads, k3::kSmemBytes, stream>>>(p, tmap_kvb);
-    return cudaGetLastError();
+    return launch_pdl(k3_merge_uv, grid, dim3(k3::kThreads), k3::kSmemBytes, stream, p, tmap_kvb);
 }
 
 }  // namespace mla

@@ -12,10 +12,12 @@
 //    stored bf16 as an operand of the attention kernel's score contraction;
 //  * the split plan: prefix sum of 64-token tiles per request, consumed by K2/K3.
 //
-// One 1-D grid with three kinds of CTA:
-//   [0, n_absorb)            absorb: (head, request block of 16)
-//   [n_absorb, +n_rowwarps)  per-request work, one warp per request
-//   last                     planner
+// One 1-D grid with two kinds of CTA:
+//   [0, n_absorb)  absorb: (request block of 64, head, quarter of the latent
+//                  columns). Warps 0-3 stage q_nope and run the MMAs against a
+//                  32 KB W_UK slice; warp 4 does the per-request work of one
+//                  request of the block (q_pe RoPE, kv_post, cache append).
+//   last           planner
 #include <cuda.h>
 
 #include "mla_common.cuh"
@@ -23,20 +25,21 @@
 
 namespace mla {
 
-constexpr int kReqBlock = 16;   // requests per absorb CTA (M of the MMA)
-constexpr int kK1Threads = 128;
-constexpr int kReqPerRowCta = kK1Threads / 32;
-constexpr int kWukBytes = kNope * kLora * 2;          // 131072: [8 column blocks][128 rows][128 B], swizzled
-constexpr int kQnBytes = kReqBlock * kNope * 2;       // 4096: [16 requests][128] bf16, 256-byte rows, swizzled
+constexpr int kReqBlock = 64;                         // requests per absorb CTA (4 m16 tiles)
+constexpr int kQuarters = kLora / kK1LatQ;            // 4
+constexpr int kK1MmaWarps = 4;
+constexpr int kK1Threads = (kK1MmaWarps + 1) * 32;    // + the per-request warp
+constexpr int kWukBytes = kNope * kK1LatQ * 2;        // 32768: [2 column blocks][128 d][128 B], swizzled
+constexpr int kQnBytes = kReqBlock * kNope * 2;       // 16384: [64 requests][128] bf16, 256-byte rows, swizzled
 constexpr int kK1SmemBytes = kWukBytes + kQnBytes + 64 + 1024;
+static_assert(kReqBlock == kHeads * kQuarters, "each absorb CTA of a block owns one request's row work");
 
 struct K1Grid {
-    int n_rb, n_absorb, n_row, total;
+    int n_rb, n_absorb, total;
     __host__ __device__ explicit K1Grid(int batch) {
         n_rb = (batch + kReqBlock - 1) / kReqBlock;
-        n_absorb = n_rb * kHeads;
-        n_row = (batch + kReqPerRowCta - 1) / kReqPerRowCta;
-        total = n_absorb + n_row + 1;
+        n_absorb = n_rb * kHeads * kQuarters;
+        total = n_absorb + 1;
     }
 };
 
@@ -104,13 +107,15 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
     const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride;
     const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w);
 
-    // q_pe of all 16 heads: lane j rotates pair j
+    // q_pe of all 16 heads: lane j rotates pair j (all 16 loads issued first)
     __nv_bfloat16* qrow = qa + (int64_t)b * kQRows * kRow;
-#pragma unroll 4
+    __nv_bfloat162 xq[kHeads];
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) xq[h] = reinterpret_cast<const __nv_bfloat162*>(q + h * kQHead + kNope)[lane];
+#pragma unroll
     for (int h = 0; h < kHeads; ++h) {
-        const __nv_bfloat162 x = reinterpret_cast<const __nv_bfloat162*>(q + h * kQHead + kNope)[lane];
         float lo, hi;
-        rope_pair(__low2float(x), __high2float(x), cs, sn, lane, lo, hi);
+        rope_pair(__low2float(xq[h]), __high2float(xq[h]), cs, sn, lane, lo, hi);
         qrow[h * kRow + kLora + lane] = __float2bfloat16_rn(lo);
         qrow[h * kRow + kLora + 32 + lane] = __float2bfloat16_rn(hi);
     }
@@ -139,15 +144,25 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float var = __fdiv_rn(ss, (float)kLora);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.rms_eps)));
+    __align__(16) __nv_bfloat16 gw[16];  // gamma[16 lane, 16 lane + 16)
+    if ((reinterpret_cast<uintptr_t>(gam) & 15) == 0) {
+        reinterpret_cast<uint4*>(gw)[0] = reinterpret_cast<const uint4*>(gam)[2 * lane];
+        reinterpret_cast<uint4*>(gw)[1] = reinterpret_cast<const uint4*>(gam)[2 * lane + 1];
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) gw[k] = gam[16 * lane + k];
+    }
     __align__(16) __nv_bfloat16 outc[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
         const float y = bf16_round(__fmul_rn(x[k], inv));
-        outc[k] = __float2bfloat16_rn(__fmul_rn(y, __bfloat162float(gam[16 * lane + k])));
+        outc[k] = __float2bfloat16_rn(__fmul_rn(y, __bfloat162float(gw[k])));
     }
     float lo, hi;
-    rope_pair(__bfloat162float(src[kLora + 2 * lane]), __bfloat162float(src[kLora + 2 * lane + 1]), cs, sn, lane,
-              lo, hi);
+    {
+        const __nv_bfloat16* kp = src + kLora + 2 * lane;
+        rope_pair(__bfloat162float(kp[0]), __bfloat162float(kp[1]), cs, sn, lane, lo, hi);
+    }
     const int page = p.block_table[(int64_t)b * p.max_blocks + pos / kPage];
     if (page < 0 || page >= p.n_pages) {
         if (lane == 0) record_error(p.error_word, MLA_DEV_BAD_PAGE);
@@ -161,86 +176,122 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
 }
 
 __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p,
-                                                            const __grid_constant__ CUtensorMap tmap_kvb) {
+                                                            const __grid_constant__ CUtensorMap tmap_wuk) {
     const WsLayout ws = ws_layout(p.batch, p.num_ctas);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     __nv_bfloat16* qa = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
     const K1Grid g(p.batch);
     const int cta = blockIdx.x;
+    pdl_wait();     // q, kv_a and the cache come from earlier work on the stream
+    pdl_trigger();  // K2 may become resident now; it waits for this grid before reading its output
 
     if (cta == g.total - 1) {
         plan_scan(p, reinterpret_cast<int32_t*>(wsb + ws.tiles_cum));
         return;
     }
-    if (cta >= g.n_absorb) {
-        const int b = (cta - g.n_absorb) * kReqPerRowCta + (threadIdx.x >> 5);
-        if (b < p.batch) request_rows(p, qa, b, threadIdx.x & 31);
-        return;
-    }
 
-    // ---- absorb CTA: q_c[b][h][:] = q_nope[b][h] @ W_UK[h] for 16 requests ----
+    // ---- absorb CTA: q_c[b][h][128j + l] = q_nope[b][h] @ W_UK[h][:, 128j + l] ----
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* w_s = smem;
     uint8_t* q_s = smem + kWukBytes;
     uint64_t* bar = reinterpret_cast<uint64_t*>(q_s + kQnBytes);
-    const int h = cta % kHeads, rb = cta / kHeads;
+    const int rb = cta / (kHeads * kQuarters), c_in = cta % (kHeads * kQuarters);
+    const int h = c_in / kQuarters, j = c_in % kQuarters;
     const int b0 = rb * kReqBlock;
     const int nreq = min(kReqBlock, p.batch - b0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
         mbar_arrive_expect_tx(bar, kWukBytes);
-        tma_load_3d(w_s, &tmap_kvb, bar, 0, h * kKvbHead, 0, kCacheEvictLast);
+        tma_load_3d(w_s, &tmap_wuk, bar, 0, h * kKvbHead, kK1WukBlocks * j, kCacheEvictLast);
     }
-    // q_nope [16][128] -> shared, 256-byte rows with 16-byte units XOR (row & 7)
-    const uint32_t qb = smem_u32(q_s);
+    if (warp == kK1MmaWarps) {  // the per-request work of request b0 + c_in; joins no barrier
+        if (c_in < nreq) request_rows(p, qa, b0 + c_in, lane);
+        return;
+    }
+    // q_nope [64][128] -> shared, 256-byte rows with 16-byte units XOR (row & 7)
     {
         const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);
-        for (int i = threadIdx.x; i < kReqBlock * (kNope / 2); i += kK1Threads) {
-            const int r = i / (kNope / 2), c2 = 2 * (i % (kNope / 2));
-            uint32_t v = 0u;
-            if (r < nreq) v = *reinterpret_cast<const uint32_t*>(q + (int64_t)(b0 + r) * p.q_stride + h * kQHead + c2);
-            *reinterpret_cast<uint32_t*>(q_s + r * 256 + ((((c2 >> 3) ^ (r & 7))) << 4) + (c2 & 7) * 2) = v;
+        constexpr int kUnits = kReqBlock * (kNope / 8);  // 16-byte units
+        constexpr int kPer = kUnits / (kK1MmaWarps * 32);
+        const bool vec = (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (p.q_stride & 7) == 0;
+        uint4 v[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = threadIdx.x + k * kK1MmaWarps * 32;
+            const int r = i >> 4, u = i & 15;
+            const __nv_bfloat16* src = q + (int64_t)(b0 + r) * p.q_stride + h * kQHead + u * 8;
+            v[k] = make_uint4(0u, 0u, 0u, 0u);
+            if (r < nreq) {
+                if (vec) {
+                    v[k] = *reinterpret_cast<const uint4*>(src);
+                } else {
+                    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src);
+                    v[k] = make_uint4(s32[0], s32[1], s32[2], s32[3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = threadIdx.x + k * kK1MmaWarps * 32;
+            const int r = i >> 4, u = i & 15;
+            *reinterpret_cast<uint4*>(q_s + r * 256 + ((u ^ (r & 7)) << 4)) = v[k];
         }
     }
-    __syncthreads();
+    named_bar_sync(1, kK1MmaWarps * 32);  // q_nope staged, barrier initialised
     {
         int dummy = 0;
         if (!mbar_wait(bar, 0, &dummy, p.error_word)) return;
     }
-    // D[16 requests][512] = A[16][128 d] x W_UK[h][128 d][512]; warp w owns columns [128w, 128w+128)
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // D[64 requests][128] = A[64][128 d] x W_UK[h][128 d][128 l]; warp w owns l in [32w, 32w+32)
     const int gq = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;
-    const uint32_t wb = smem_u32(w_s);
-    float acc[16][4];
+    const int n_mt = (nreq + 15) >> 4;
+    const uint32_t wb = smem_u32(w_s), qb = smem_u32(q_s);
+    float acc[4][4][4];
 #pragma unroll
-    for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int n = 0; n < 4; ++n) acc[mt][n][0] = acc[mt][n][1] = acc[mt][n][2] = acc[mt][n][3] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < kNope / 16; ++ks) {
-        uint32_t a[4];
-        {
-            const int row = (m8 & 1) * 8 + r8, col = 16 * ks + (m8 >> 1) * 8;
-            ldsm_x4(qb + row * 256 + ((((col >> 3) ^ (row & 7))) << 4), a[0], a[1], a[2], a[3]);
-        }
         const int d = 16 * ks + (m8 & 1) * 8 + r8;
+        uint32_t bw[2][4];
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {  // latent tiles 2np, 2np+1 of this warp
-            const int l = 128 * warp + 16 * np + (m8 >> 1) * 8;
-            uint32_t b00, b01, b10, b11;
-            ldsm_x4_t(wb + (l >> 6) * (kNope * 128) + d * 128 + ((((l & 63) >> 3) ^ r8) << 4), b00, b01, b10, b11);
-            mma16816(acc[2 * np], a, b00, b01);
-            mma16816(acc[2 * np + 1], a, b10, b11);
+        for (int np = 0; np < 2; ++np) {  // latent tiles 2np, 2np+1 of this warp
+            const int l = 32 * warp + 16 * np + (m8 >> 1) * 8;
+            ldsm_x4_t(wb + (l >> 6) * (kNope * 128) + d * 128 + ((((l & 63) >> 3) ^ r8) << 4), bw[np][0], bw[np][1],
+                      bw[np][2], bw[np][3]);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            if (mt < n_mt) {
+                uint32_t a[4];
+                const int row = 16 * mt + (m8 & 1) * 8 + r8, col = 16 * ks + (m8 >> 1) * 8;
+                ldsm_x4(qb + row * 256 + ((((col >> 3) ^ (row & 7))) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {
+                    mma16816(acc[mt][2 * np], a, bw[np][0], bw[np][1]);
+                    mma16816(acc[mt][2 * np + 1], a, bw[np][2], bw[np][3]);
+                }
+            }
         }
     }
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-        const int l = 128 * warp + 8 * n + 2 * t4;
-        if (gq < nreq)
-            *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + gq) * kQRows + h) * kRow + l) = pack_bf16(acc[n][0], acc[n][1]);
-        if (gq + 8 < nreq)
-            *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + gq + 8) * kQRows + h) * kRow + l) =
-                pack_bf16(acc[n][2], acc[n][3]);
+    for (int mt = 0; mt < 4; ++mt) {
+        if (mt >= n_mt) break;
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+            const int l = kK1LatQ * j + 32 * warp + 8 * n + 2 * t4;
+            const int r0 = 16 * mt + gq, r1 = r0 + 8;
+            if (r0 < nreq)
+                *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + r0) * kQRows + h) * kRow + l) =
+                    pack_bf16(acc[mt][n][0], acc[mt][n][1]);
+            if (r1 < nreq)
+                *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + r1) * kQRows + h) * kRow + l) =
+                    pack_bf16(acc[mt][n][2], acc[mt][n][3]);
+        }
     }
 }
 
@@ -248,10 +299,9 @@ cudaError_t k1_configure() {
     return cudaFuncSetAttribute(k1_prologue, cudaFuncAttributeMaxDynamicSharedMemorySize, kK1SmemBytes);
 }
 
-cudaError_t launch_prologue(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream) {
+cudaError_t launch_prologue(const MlaDecodeParams& p, const CUtensorMap& tmap_wuk, cudaStream_t stream) {
     const K1Grid g(p.batch);
-    k1_prologue<<<g.total, kK1Threads, kK1SmemBytes, stream>>>(p, tmap_kvb);
-    return cudaGetLastError();
+    return launch_pdl(k1_prologue, dim3(g.total), dim3(kK1Threads), kK1SmemBytes, stream, p, tmap_wuk);
 }
 
 }  // namespace mla

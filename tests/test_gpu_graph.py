@@ -1,0 +1,62 @@
+"""DecodeGraph: the captured step (with PDL edges between K1, K2 and K3) must give
+bit-identical outputs and cache rows to the eager step, over a decode loop in which the
+graph itself advances seq_lens."""
+import pytest
+import torch
+
+from mla_testlib import fleet, workloads
+
+pytestmark = pytest.mark.gpu
+LENS = [0, 1, 63, 64, 100, 1000, 2047]
+
+
+def _runner_and_cache(dev, seed=21):
+    cfg = fleet.ModelConfig()
+    cos, sin = fleet.device_rope_tables(cfg, 2200, dev)
+    lw = workloads.make_layer_weights(seed)
+    runner = fleet.MlaDecodeAttention(cfg, fleet.LayerWeights(
+        *(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm, lw.kv_b_proj))), cos, sin)
+    g = torch.Generator().manual_seed(seed)
+    cache = fleet.PagedLatentCache.for_lengths(LENS, extra_tokens=8, spare_pages=2, generator=g, device=dev)
+    cache.pages.copy_(torch.randn(cache.pages.shape, generator=g).to(torch.bfloat16))
+    return runner, cache
+
+
+def _clone(cache):
+    c = fleet.PagedLatentCache(cache.n_pages, cache.batch, cache.max_blocks, device=cache.device)
+    c.pages.copy_(cache.pages)
+    c.block_table.copy_(cache.block_table)
+    c.seq_lens.copy_(cache.seq_lens)
+    return c
+
+
+def test_graph_decode_loop_matches_eager(cuda_device):
+    runner, cache_e = _runner_and_cache(cuda_device)
+    cache_g = _clone(cache_e)
+    graph = fleet.DecodeGraph(runner, cache_g, advance=True)
+    g = torch.Generator().manual_seed(5)
+    for step in range(4):
+        x = torch.randn(len(LENS), 2048, generator=g).to(torch.bfloat16).to(cuda_device)
+        want = runner(x, cache_e).clone()
+        cache_e.advance()
+        graph.x_n.copy_(x)
+        got = graph.replay()
+        torch.cuda.synchronize(cuda_device)
+        runner.check_errors()
+        assert torch.equal(got, want), f"step {step}: graph output differs from the eager step"
+    assert torch.equal(cache_g.seq_lens, cache_e.seq_lens)
+    assert torch.equal(cache_g.pages, cache_e.pages)
+
+
+def test_graph_from_qkv_matches_eager(cuda_device):
+    runner, cache = _runner_and_cache(cuda_device, seed=22)
+    g = torch.Generator().manual_seed(6)
+    q = torch.randn(len(LENS), 3072, generator=g).to(torch.bfloat16).to(cuda_device)
+    kv_a = torch.randn(len(LENS), 576, generator=g).to(torch.bfloat16).to(cuda_device)
+    want = runner.attend(q, kv_a, cache).clone()
+    graph = fleet.DecodeGraph(runner, cache, inputs="qkv", q=q, kv_a=kv_a)
+    for _ in range(3):
+        got = graph.replay()
+    torch.cuda.synchronize(cuda_device)
+    runner.check_errors()
+    assert torch.equal(got, want)
