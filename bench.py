@@ -328,6 +328,22 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     k2_gbs = kv_b / (k2_ms * 1e-3) / 1e9
     traffic = ncu_traffic(args.workload)
 
+    # ---- the q | kv_a projection (the step before the task), decode batches only:
+    # K0 (weight stream, in the library) against cuBLAS on the same x_n; the 14.9 MB
+    # weight fits in L2, so L2 is flushed before every timed call
+    projection = None
+    if B <= native.MAX_PROJECT_BATCH:
+        ptimer = StepTimer(stream, 0, dev)
+        runner.attend_x(x_n, cache, out, stage="project")
+        k0_ms = ptimer(lambda: runner.attend_x(x_n, cache, out, stage="project"), max(5, args.steps))
+        cublas_ms = ptimer(lambda: torch.nn.functional.linear(x_n, runner.w_qkv), max(5, args.steps))
+        w_bytes = runner.w_qkv.numel() * 2
+        projection = {"kernel": "k0_project", "weight_bytes": w_bytes, "k0_us": round(k0_ms * 1e3, 2),
+                      "cublas_us": round(cublas_ms * 1e3, 2),
+                      "k0_gbs": round(w_bytes / (k0_ms * 1e-3) / 1e9, 1),
+                      "k0_frac_of_peak": round(w_bytes / (k0_ms * 1e-3) / 1e9 / peak, 4),
+                      "l2": "flushed: 256 MB written before every timed call, outside its CUDA events"}
+
     # ---- e2e through the public call: pinned host x_n -> device, task, R(out) -> host
     x_host = x_n.cpu().pin_memory()
     out_host = torch.empty(B, 2048, dtype=torch.bfloat16).pin_memory()
@@ -381,9 +397,11 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                      "unit": "GB/s", "frac": round(k2_gbs / peak, 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": kv_b, "peak_source": peak_src},
         "cpu_baseline": cpu,
+        "projection": projection,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": int(x_n.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2),
-                "path": "attention_absorbed-style call: pinned x_n H2D, cuBLAS q|kv_a, K1-K3, R(out) D2H"},
+                "path": "attention_absorbed-style call: pinned x_n H2D, q|kv_a projection (K0 in the library for "
+                        "<= 64 requests, else cuBLAS), K1-K3, R(out) D2H"},
         "gpu_launches": native.load_library().mla_launches_per_step() * args.steps,
         "clocks": clocks.summary(),
     }

@@ -89,10 +89,13 @@ class MlaDecodeAttention:
         self._step_p: native.MlaDecodeParams | None = None
 
     # ------------------------------------------------------------------ params
-    def params(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
+    def params(self, q: torch.Tensor | None, kv_a: torch.Tensor | None, cache: PagedLatentCache,
                out: torch.Tensor | None, *, rope_pos: torch.Tensor | None = None,
-               shard_out: torch.Tensor | None = None, new_row: bool = True) -> native.MlaDecodeParams:
-        B = q.shape[0]
+               shard_out: torch.Tensor | None = None, new_row: bool = True,
+               x_n: torch.Tensor | None = None) -> native.MlaDecodeParams:
+        """The C-ABI params of one step. With `x_n` (and q = kv_a = None) the library
+        projects q | kv_a itself with the fused [W_q; W_kv_a] weight (K0)."""
+        B = (x_n if x_n is not None else q).shape[0]
         p = native.new_params()
         p.softmax_scale = self.cfg.softmax_scale
         p.rms_eps = self.cfg.rms_eps
@@ -100,8 +103,11 @@ class MlaDecodeAttention:
         p.max_blocks = cache.max_blocks
         p.n_pages = cache.n_pages
         p.max_pos = self.cos.shape[0]
-        p.q, p.q_stride = _ptr(q), _row_stride(q)
-        p.kv_a, p.kv_a_stride = _ptr(kv_a), _row_stride(kv_a)
+        if x_n is not None:
+            p.x_n, p.x_stride, p.w_qkv = _ptr(x_n), _row_stride(x_n), _ptr(self.w_qkv)
+        else:
+            p.q, p.q_stride = _ptr(q), _row_stride(q)
+            p.kv_a, p.kv_a_stride = _ptr(kv_a), _row_stride(kv_a)
         p.kv_a_norm_w = _ptr(self.norm_w)
         p.kv_b = _ptr(self.kv_b)
         p.rope_cos, p.rope_sin = _ptr(self.cos), _ptr(self.sin)
@@ -167,6 +173,35 @@ class MlaDecodeAttention:
         native.check(fn(ctypes.byref(p), stream), f"mla {stage}", p)
         return out if shard_out is None else shard_out
 
+    def attend_x(self, x_n: torch.Tensor, cache: PagedLatentCache, out: torch.Tensor | None = None,
+                 stage: str = "all") -> torch.Tensor:
+        """The whole slice in the library, from the post-RMSNorm hidden state x_n
+        [B, 2048] bf16 (B <= 64): K0 projects q | kv_a, then K1-K3 as in attend()."""
+        if x_n.dtype != torch.bfloat16 or x_n.dim() != 2 or x_n.shape[1] != self.cfg.hidden:
+            raise ValueError(f"x_n must be bf16 [B, {self.cfg.hidden}], got {x_n.dtype} {tuple(x_n.shape)}")
+        if x_n.stride(-1) != 1:
+            raise ValueError("x_n rows must be contiguous")
+        if x_n.shape[0] != cache.batch:
+            raise ValueError(f"batch {x_n.shape[0]} does not match the cache's {cache.batch} requests")
+        if x_n.shape[0] > native.MAX_PROJECT_BATCH:
+            raise ValueError(f"the in-library projection takes at most {native.MAX_PROJECT_BATCH} requests")
+        if out is None:
+            out = torch.empty(x_n.shape[0], self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16,
+                              device=self.device)
+        key = ("x", x_n.data_ptr(), _row_stride(x_n), cache.pages.data_ptr(), cache.block_table.data_ptr(),
+               cache.seq_lens.data_ptr(), cache.n_pages, cache.max_blocks, x_n.shape[0], out.data_ptr(),
+               _row_stride(out), self.flags, self.num_ctas, self.cos.data_ptr(), self.cos.shape[0],
+               self.kv_b.data_ptr())
+        p = self._step_p
+        if key != self._step_key or self._ws is None or p.workspace != self._ws.data_ptr():
+            p = self.params(None, None, cache, out, x_n=x_n)
+            self._step_key, self._step_p = key, p
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        fn = {"all": self.lib.mla_decode_step, "project": self.lib.mla_project, "prologue": self.lib.mla_prologue,
+              "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv}[stage]
+        native.check(fn(ctypes.byref(p), stream), f"mla {stage}", p)
+        return out
+
     def project(self, x_n: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """q = R(W_q x_n), kv_a = R(W_kv_a x_n) as views of one bf16 GEMM output."""
         qkv = torch.nn.functional.linear(x_n, self.w_qkv)
@@ -175,6 +210,12 @@ class MlaDecodeAttention:
 
     def __call__(self, x_n: torch.Tensor, cache: PagedLatentCache,
                  out: torch.Tensor | None = None) -> torch.Tensor:
+        """x_n -> R(out). Decode batches (<= 64 requests) run the projection in the
+        library (attend_x: a weight stream at HBM rate); larger batches, where the
+        projection is a compute-bound GEMM, use cuBLAS and then attend()."""
+        if x_n.shape[0] <= native.MAX_PROJECT_BATCH and x_n.stride(-1) == 1 and \
+                x_n.data_ptr() % 16 == 0 and _row_stride(x_n) % 8 == 0:
+            return self.attend_x(x_n, cache, out)
         q, kv_a = self.project(x_n)
         return self.attend(q, kv_a, cache, out)
 

@@ -26,6 +26,9 @@ cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tm
 cudaError_t k2_configure();
 cudaError_t k2_mma_configure();
 cudaError_t k3_configure();
+cudaError_t k0_configure();
+cudaError_t launch_project(const MlaDecodeParams& p, __nv_bfloat16* qkv, const CUtensorMap& tmap_w,
+                           const CUtensorMap& tmap_x, cudaStream_t stream);
 
 namespace {
 
@@ -50,8 +53,8 @@ int device_info(int* sm_count) {
         cudaDeviceProp prop;
         if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
         if (prop.major != 10) { d.status = MLA_E_ARCH; return; }
-        if (k1_configure() != cudaSuccess || k2_configure() != cudaSuccess || k2_mma_configure() != cudaSuccess ||
-            k3_configure() != cudaSuccess) {
+        if (k0_configure() != cudaSuccess || k1_configure() != cudaSuccess || k2_configure() != cudaSuccess ||
+            k2_mma_configure() != cudaSuccess || k3_configure() != cudaSuccess) {
             d.status = MLA_E_LAUNCH;
             return;
         }
@@ -111,6 +114,48 @@ int make_tmap_kvb(CUtensorMap* m, const void* kv_b, int blocks) {
     return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
 }
 
+// The stacked [W_q; W_kv_a] (3648 rows x 2048 bf16) as dims {64 columns, 3648
+// rows (4096 B), 32 column blocks (128 B)}, box {64, 32, 8}: 32 weight rows x
+// 512 columns = 32 KB landing as [8][32 rows][128 B] (128-byte swizzle).
+int make_tmap_wqkv(CUtensorMap* m, const void* w) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn;
+    if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
+    cuuint64_t dims[3] = {64, (cuuint64_t)kQkvRows, kHidden / 64};
+    cuuint64_t strides[2] = {(cuuint64_t)kHidden * 2, 128};
+    cuuint32_t box[3] = {64, 32, 8};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
+}
+
+// x_n (batch rows x 2048 bf16, row pitch x_stride) as dims {64 columns, batch
+// rows, 32 column blocks}, box {64, 16, 32}: 16 rows x 2048 = 64 KB landing as
+// [32][16 rows][128 B]; rows past the batch read as zeros.
+int make_tmap_x(CUtensorMap* m, const void* x, int batch, int64_t x_stride) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn;
+    if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
+    cuuint64_t dims[3] = {64, (cuuint64_t)batch, kHidden / 64};
+    cuuint64_t strides[2] = {(cuuint64_t)x_stride * 2, 128};
+    cuuint32_t box[3] = {64, 16, kHidden / 64};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(x), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
+}
+
+int run_project(const MlaDecodeParams& q, cudaStream_t s) {
+    CUtensorMap tw, tx;
+    int st = make_tmap_wqkv(&tw, q.w_qkv);
+    if (st != MLA_OK) return st;
+    st = make_tmap_x(&tx, q.x_n, q.batch, q.x_stride);
+    if (st != MLA_OK) return st;
+    __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(q.workspace) + ws_layout(q).qkv);
+    return launch_project(q, qkv, tw, tx, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
 int run_prologue(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap t;
     const int st = make_tmap_kvb(&t, q.kv_b, kK1WukBlocks);
@@ -152,14 +197,21 @@ int check_header(const MlaDecodeParams* p) {
 int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
     int st = check_header(p);
     if (st != MLA_OK) return st;
-    if (!p->q || !p->kv_a || !p->kv_a_norm_w || !p->kv_b || !p->rope_cos || !p->rope_sin || !p->block_table ||
+    const bool project = p->x_n != nullptr;
+    if (project ? (p->q || p->kv_a || !p->w_qkv) : (!p->q || !p->kv_a)) return MLA_E_INVALID_ARG;
+    if (!p->kv_a_norm_w || !p->kv_b || !p->rope_cos || !p->rope_sin || !p->block_table ||
         !p->seq_lens || !p->kv_cache || (!p->out && !p->shard_out) || !p->workspace)
         return MLA_E_INVALID_ARG;
+    if (project) {
+        if (p->batch > MLA_MAX_PROJECT_BATCH) return MLA_E_LIMIT;
+        if (p->x_stride < MLA_HIDDEN) return MLA_E_INVALID_ARG;
+        if (!aligned(p->x_n, 16) || (p->x_stride & 7) || !aligned(p->w_qkv, 16)) return MLA_E_MISALIGNED;
+    }
     if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW)) return MLA_E_INVALID_ARG;
     if (p->max_blocks <= 0 || p->n_pages <= 0 || p->max_pos <= 0) return MLA_E_INVALID_ARG;
     if ((int64_t)p->n_pages * MLA_PAGE_SIZE > INT32_MAX || (int64_t)p->batch * p->max_blocks > INT32_MAX)
         return MLA_E_LIMIT;
-    if (p->q_stride < MLA_HEADS * (MLA_QK_NOPE + MLA_QK_ROPE) || p->kv_a_stride < MLA_ROW ||
+    if ((!project && (p->q_stride < MLA_HEADS * (MLA_QK_NOPE + MLA_QK_ROPE) || p->kv_a_stride < MLA_ROW)) ||
         p->out_stride < MLA_HEADS * MLA_V_HEAD)
         return MLA_E_INVALID_ARG;
     if (!(p->softmax_scale > 0.f) || !(p->rms_eps >= 0.f)) return MLA_E_INVALID_ARG;
@@ -174,8 +226,16 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
     *out = *p;
     st = resolve_ctas(p, &out->num_ctas);
     if (st != MLA_OK) return st;
-    const WsLayout ws = ws_layout(p->batch, out->num_ctas);
+    const WsLayout ws = ws_layout(*out);
     if (p->workspace_bytes < ws.total) return MLA_E_WORKSPACE;
+    if (project) {  // K1 onwards read the projection from the workspace
+        const __nv_bfloat16* qkv =
+            reinterpret_cast<const __nv_bfloat16*>(reinterpret_cast<const char*>(p->workspace) + ws.qkv);
+        out->q = qkv;
+        out->q_stride = kQkvRows;
+        out->kv_a = qkv + kHeads * kQHead;
+        out->kv_a_stride = kQkvRows;
+    }
     return MLA_OK;
 }
 
@@ -189,7 +249,7 @@ int run_attention(const MlaDecodeParams& q, cudaStream_t s) {
     if (st != MLA_OK) return st;
     if (!(q.flags & MLA_FLAG_TCGEN05))
         return launch_attention_mma(q, tkv, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
-    const WsLayout ws = ws_layout(q.batch, q.num_ctas);
+    const WsLayout ws = ws_layout(q);
     st = make_tmap_blocks(&tq, reinterpret_cast<const char*>(q.workspace) + ws.qa, (uint64_t)q.batch * kQRows, false);
     if (st != MLA_OK) return st;
     return launch_attention_tc(q, tkv, tq, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
@@ -250,7 +310,7 @@ int mla_workspace_size(const MlaDecodeParams* p, uint64_t* bytes) {
     int ctas = 0;
     st = resolve_ctas(p, &ctas);
     if (st != MLA_OK) return st;
-    *bytes = ws_layout(p->batch, ctas).total;
+    *bytes = ws_layout(p->batch, ctas, p->x_n != nullptr).total;
     return MLA_OK;
 }
 
@@ -261,7 +321,7 @@ int mla_plan_info(const MlaDecodeParams* p, int32_t* num_ctas, int32_t* num_slot
     st = resolve_ctas(p, &ctas);
     if (st != MLA_OK) return st;
     if (num_ctas) *num_ctas = ctas;
-    if (num_slots) *num_slots = ws_layout(p->batch, ctas).slots;
+    if (num_slots) *num_slots = ws_layout(p->batch, ctas, p->x_n != nullptr).slots;
     return MLA_OK;
 }
 
@@ -278,6 +338,14 @@ int mla_combine_shards(const float* parts, int32_t n_shards, int32_t batch, void
     return launch_combine_shards(parts, n_shards, batch, out, out_stride, (cudaStream_t)stream) == cudaSuccess
                ? MLA_OK
                : MLA_E_LAUNCH;
+}
+
+int mla_project(const MlaDecodeParams* p, void* stream) {
+    MlaDecodeParams q;
+    int st = prepare(p, &q);
+    if (st != MLA_OK) return st;
+    if (!q.x_n) return MLA_E_INVALID_ARG;
+    return run_project(q, (cudaStream_t)stream);
 }
 
 int mla_prologue(const MlaDecodeParams* p, void* stream) {
@@ -306,6 +374,10 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream) {
     int st = prepare(p, &q);
     if (st != MLA_OK) return st;
     cudaStream_t s = (cudaStream_t)stream;
+    if (q.x_n) {
+        st = run_project(q, s);
+        if (st != MLA_OK) return st;
+    }
     st = run_prologue(q, s);
     if (st != MLA_OK) return st;
     st = run_attention(q, s);

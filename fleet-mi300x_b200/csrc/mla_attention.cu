@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
     uint8_t* q_s = smem + kOffQ;
     uint8_t* p_s = smem + kOffP;
 
-    const WsLayout ws = ws_layout(p.batch, p.num_ctas);
+    const WsLayout ws = ws_layout(p);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     const int32_t* cum = reinterpret_cast<const int32_t*>(wsb + ws.tiles_cum);
     float* part_ml = reinterpret_cast<float*>(wsb + ws.part_ml);
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kCkThreads)
     __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(qf + kHeads * kRow);  // [64][576]
     float* sc = reinterpret_cast<float*>(tile + kPage * kRow);            // [16][64]
 
-    const WsLayout ws = ws_layout(p.batch, p.num_ctas);
+    const WsLayout ws = ws_layout(p);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     const int32_t* cum = reinterpret_cast<const int32_t*>(wsb + ws.tiles_cum);
     const __nv_bfloat16* qa = reinterpret_cast<const __nv_bfloat16*>(wsb + ws.qa);

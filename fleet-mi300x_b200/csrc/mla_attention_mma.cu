@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     float* spart = reinterpret_cast<float*>(smem + kOffS);
     uint8_t* p_s = smem + kOffP;
 
-    const WsLayout ws = ws_layout(p.batch, p.num_ctas);
+    const WsLayout ws = ws_layout(p);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     const int32_t* cum = reinterpret_cast<const int32_t*>(wsb + ws.tiles_cum);
     const __nv_bfloat16* qa = reinterpret_cast<const __nv_bfloat16*>(wsb + ws.qa);

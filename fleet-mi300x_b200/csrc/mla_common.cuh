@@ -24,6 +24,8 @@ constexpr int kPage = MLA_PAGE_SIZE;       // 64
 constexpr int kQHead = kNope + kRope;      // 192: q row per head
 constexpr int kKvbHead = kNope + kV;       // 256: kv_b rows per head
 constexpr int kQRows = kHeads;             // rows of the absorbed query per request in the workspace
+constexpr int kHidden = MLA_HIDDEN;        // 2048: model width (x_n)
+constexpr int kQkvRows = kHeads * kQHead + kRow;  // 3648: rows of the stacked [W_q; W_kv_a]
 constexpr int kK1LatQ = 128;               // latent columns of W_UK per prologue CTA (a quarter)
 constexpr int kK1WukBlocks = kK1LatQ / 64; // 64-column blocks of that slice (its TMA box)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -37,13 +39,15 @@ constexpr float kLog2e = 1.4426950408889634f;
 // slots = num_ctas + batch: CTA c writes the partial of request b at slot c + b.
 // ---------------------------------------------------------------------------
 struct WsLayout {
-    uint64_t tiles_cum, qa, part_ml, part_acc, total;
+    uint64_t tiles_cum, qa, part_ml, part_acc, qkv, total;
     int32_t slots;
 };
 
 __host__ __device__ inline uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
-__host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas) {
+// with_qkv: the step projects x_n itself (MlaDecodeParams.x_n set), and q | kv_a
+// of every request live in the workspace as [batch][3648] bf16.
+__host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with_qkv = false) {
     WsLayout w;
     w.slots = num_ctas + batch;
     uint64_t off = 0;
@@ -51,8 +55,13 @@ __host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas) {
     w.qa = off;        off = align256(off + uint64_t(batch) * kQRows * kRow * 2);
     w.part_ml = off;   off = align256(off + uint64_t(w.slots) * kHeads * 2 * 4);
     w.part_acc = off;  off = align256(off + uint64_t(w.slots) * kHeads * kLora * 4);
+    w.qkv = off;       off = align256(off + (with_qkv ? uint64_t(batch) * kQkvRows * 2 : 0));
     w.total = off;
     return w;
+}
+
+__host__ __device__ inline WsLayout ws_layout(const MlaDecodeParams& p) {
+    return ws_layout(p.batch, p.num_ctas, p.x_n != nullptr);
 }
 
 // Programmatic dependent launch. A kernel launched with launch_pdl may start

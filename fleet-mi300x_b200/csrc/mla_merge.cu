@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     uint8_t* a_lo = a_hi + kABytes;
     uint64_t* bar = reinterpret_cast<uint64_t*>(a_lo + kABytes);
 
-    const WsLayout ws = ws_layout(p.batch, p.num_ctas);
+    const WsLayout ws = ws_layout(p);
     const char* wsb = reinterpret_cast<const char*>(p.workspace);
     const int32_t* cum = reinterpret_cast<const int32_t*>(wsb + ws.tiles_cum);
     const float* part_ml = reinterpret_cast<const float*>(wsb + ws.part_ml);

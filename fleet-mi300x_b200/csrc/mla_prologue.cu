@@ -177,7 +177,7 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
 
 __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p,
                                                             const __grid_constant__ CUtensorMap tmap_wuk) {
-    const WsLayout ws = ws_layout(p.batch, p.num_ctas);
+    const WsLayout ws = ws_layout(p);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     __nv_bfloat16* qa = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
     const K1Grid g(p.batch);

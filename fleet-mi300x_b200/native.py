@@ -13,7 +13,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libmla_decode.so"
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 HEADS, QK_NOPE, QK_ROPE, V_HEAD, KV_LORA, PAGE_SIZE = 16, 128, 64, 128, 512, 64
 ROW = KV_LORA + QK_ROPE
 MAX_BATCH = 65536
@@ -22,6 +22,7 @@ FLAG_CHECK_KERNEL = 0x2
 FLAG_TCGEN05 = 0x4
 FLAG_NO_NEW_ROW = 0x8
 SHARD_STRIDE = 132
+MAX_PROJECT_BATCH = 64  # MLA_MAX_PROJECT_BATCH: batch limit of the in-library q|kv_a projection
 STATIC_SCRATCH_BYTES = 32 << 20  # MLA_STATIC_SCRATCH_BYTES, the workspace of mla_decode_step_static
 
 STATUS = {
@@ -33,7 +34,7 @@ DEV_ERRORS = {0: "ok", 1: "MLA_DEV_BAD_PAGE", 2: "MLA_DEV_BAD_POSITION", 3: "MLA
 EXPORTED = (
     "mla_abi_version", "mla_status_string", "mla_device_error_string", "mla_params_init",
     "mla_workspace_size", "mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv",
-    "mla_plan_info", "mla_launches_per_step", "mla_combine_shards", "mla_decode_step_static",
+    "mla_plan_info", "mla_launches_per_step", "mla_combine_shards", "mla_decode_step_static", "mla_project",
 )
 
 
@@ -70,6 +71,7 @@ class MlaDecodeParams(ctypes.Structure):
         ("error_word", ctypes.c_void_p),
         ("num_ctas", ctypes.c_int32), ("flags", ctypes.c_int32),
         ("rope_pos", ctypes.c_void_p), ("shard_out", ctypes.c_void_p),
+        ("x_n", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("w_qkv", ctypes.c_void_p),
     ]
 
 
@@ -105,7 +107,8 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.mla_combine_shards.restype = ctypes.c_int
         lib.mla_combine_shards.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                            ctypes.c_int64, ctypes.c_void_p]
-        for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv", "mla_decode_step_static"):
+        for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv", "mla_decode_step_static",
+                   "mla_project"):
             f = getattr(lib, fn)
             f.restype = ctypes.c_int
             f.argtypes = [P, ctypes.c_void_p]

@@ -4,15 +4,17 @@
  * This library is a drop-in for the attention task of the reference's
  * task-by-task decode: reference_decode.py:attention_absorbed
  * (src/host/reference_decode.py:210-256), restricted to the slice between the
- * input RMSNorm (:222) and o_proj (:256). Inputs are the q / kv_a projections
- * of the post-RMSNorm hidden state (:225-231); the output is the
- * head-concatenated, bf16-rounded attention result R(out) before o_proj (:256).
+ * input RMSNorm (:222) and o_proj (:256). Inputs are either the post-RMSNorm
+ * hidden state x_n with the stacked [W_q; W_kv_a] weight (the library then
+ * projects q and kv_a itself, :225-231), or the q / kv_a projections; the
+ * output is the head-concatenated, bf16-rounded attention result R(out)
+ * before o_proj (:256).
  *
  * On the device the reference runs this slice as three task kinds inside its
  * persistent kernel (src/kernels/fleet_kernel.hip:647-654 TASK_Q_ABSORB,
  * :745-798 TASK_ATTENTION, :694-701 TASK_MERGE_UV), launched through
  * `extern "C" hipError_t fleet_launch_step(...)` (fleet_kernel.hip:1068-1078).
- * Here the same work is three stream-ordered kernels behind plain C entry
+ * Here the same work is three (four, with the projection) stream-ordered kernels behind plain C entry
  * points: pointers, sizes and a caller-provided workspace; no allocation, no
  * torch types, no global mutable state except a per-device attribute cache.
  *
@@ -43,7 +45,7 @@
 extern "C" {
 #endif
 
-#define MLA_ABI_VERSION 2
+#define MLA_ABI_VERSION 3
 
 /* Fixed model dimensions. The reference's launcher refuses any other shape
  * (src/host/fleet_launch.hip:573-577: kv_lora != 512 or qk_rope != 64);
@@ -55,6 +57,9 @@ extern "C" {
 #define MLA_KV_LORA 512
 #define MLA_PAGE_SIZE 64
 #define MLA_ROW (MLA_KV_LORA + MLA_QK_ROPE)
+#define MLA_HIDDEN 2048                                     /* model width: x_n rows */
+#define MLA_QKV_ROWS (MLA_HEADS * (MLA_QK_NOPE + MLA_QK_ROPE) + MLA_ROW)  /* 3648: [W_q; W_kv_a] */
+#define MLA_MAX_PROJECT_BATCH 64                            /* batch limit of the in-library projection */
 
 /* Host-side status codes (return values). The reference's launcher dies with
  * a message on bad shapes (fleet_launch.hip:573-577) and returns hipError_t
@@ -128,6 +133,15 @@ typedef struct MlaDecodeParams {
                                  f32 [batch][16][MLA_SHARD_STRIDE] = y[128] (W_UV o_c / L, normalised
                                  within the shard), m (log2-domain max), L (sum of exps), 2 unused;
                                  16-byte aligned */
+
+    /* In-library q | kv_a projection (ABI v3). If x_n is set, the step first
+     * computes q = R(W_q x_n) and kv_a = R(W_kv_a x_n) itself (K0, into the
+     * workspace) and q / kv_a above must be NULL; the batch is then limited to
+     * MLA_MAX_PROJECT_BATCH. NULL = q / kv_a are given (ABI v2 behaviour). */
+    const void* x_n;          /* [batch][x_stride] bf16 post-RMSNorm hidden state, 16-byte aligned */
+    int64_t x_stride;         /* elements between rows, a multiple of 8, >= MLA_HIDDEN */
+    const void* w_qkv;        /* [MLA_QKV_ROWS][MLA_HIDDEN] bf16 = rows of q_proj then kv_a_proj_with_mqa,
+                                 16-byte aligned */
 } MlaDecodeParams;
 
 #define MLA_SHARD_STRIDE (MLA_V_HEAD + 4)
@@ -144,8 +158,8 @@ const char* mla_device_error_string(int code);
 /* Fill a params struct with the fixed dims, scale 0 and no pointers. */
 void mla_params_init(MlaDecodeParams* p);
 
-/* Bytes of workspace a call with these params needs (depends on batch and
- * num_ctas only). Replaces the reference's host-side buffer plan
+/* Bytes of workspace a call with these params needs (depends on batch,
+ * num_ctas, the kernel flags and whether x_n is set). Replaces the reference's host-side buffer plan
  * (fleet_types.h:75-81 Activations.q_absorbed/attn_partial; dev_alloc in
  * fleet_launch.hip:223-237): the caller allocates, the library never does. */
 int mla_workspace_size(const MlaDecodeParams* p, uint64_t* bytes);
@@ -157,10 +171,13 @@ int mla_workspace_size(const MlaDecodeParams* p, uint64_t* bytes);
  * fleet_launch_step (fleet_kernel.hip:647-654, :745-798, :694-701, :1068-1078). */
 int mla_decode_step(const MlaDecodeParams* p, void* stream);
 
-/* The three stages one by one (same params; each expects the previous one's
- * workspace contents). K1 = kv_post (attention.h:62-90) + q_absorb
- * (attention.h:171-216); K2 = attention_chunk (attention.h:230-351);
- * K3 = merge_and_uv (attention.h:358-411). */
+/* The stages one by one (same params; each expects the previous one's
+ * workspace contents). K0 = the q | kv_a projection of x_n (needs p->x_n;
+ * reference_decode.py:225-231, device task TASK_QKV_FUSED fleet_kernel.hip:706-741);
+ * K1 = kv_post (attention.h:62-90) + q_absorb (attention.h:171-216);
+ * K2 = attention_chunk (attention.h:230-351); K3 = merge_and_uv (attention.h:358-411).
+ * With p->x_n set, mla_decode_step runs K0 first. */
+int mla_project(const MlaDecodeParams* p, void* stream);
 int mla_prologue(const MlaDecodeParams* p, void* stream);
 int mla_attention(const MlaDecodeParams* p, void* stream);
 int mla_merge_uv(const MlaDecodeParams* p, void* stream);

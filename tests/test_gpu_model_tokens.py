@@ -12,8 +12,9 @@ Arm A decodes greedily; arms B and C are fed arm A's tokens so that every step c
 the same context. Two correct implementations drift apart through 27 bf16 layers of
 random-init MoE, and a greedy token can flip where the oracle's top-2 margin is a near-tie.
 The gate: the library's logits and appended rows are no further from the oracle's than
-the control's are, and every token where the library differs from the oracle is one where
-the control differs too (or a near-tie inside the measured logit difference, at most one).
+the control's are (x 1.5), every token where the library differs from the oracle lies in
+that step's noise band (oracle top-2 margin <= 2x the measured logit gap), and the library
+flips at most two steps more than the control.
 Logits are fp32 products of the bf16 head (bf16 logits tie often over 102,400 entries).
 """
 import json
@@ -82,7 +83,7 @@ def test_config2_token_identity_27_layers(cuda_device):
     # arm A decodes greedily; arm B is fed arm A's tokens (teacher forcing), so one
     # near-tie cannot turn every later step into a comparison of different contexts
     inputs, toks_a, margins, deltas, toks_b = [int(tokens[-1])], [], [], [], []
-    toks_c, deltas_c = [], []
+    toks_c, deltas_c, rl2_b, rl2_c = [], [], [], []
     with torch.no_grad():
         for s in range(STEPS):
             la = model.decode(inputs[-1], T0 + s, attn_a)
@@ -95,6 +96,8 @@ def test_config2_token_identity_27_layers(cuda_device):
             margins.append(float(top.values[0] - top.values[1]))
             deltas.append(float((la - lb).abs().max()))
             deltas_c.append(float((la - lc).abs().max()))
+            rl2_b.append(float((la - lb).norm() / la.norm()))
+            rl2_c.append(float((la - lc).norm() / la.norm()))
             inputs.append(toks_a[-1])
     for r in runners:
         r.check_errors()
@@ -115,6 +118,7 @@ def test_config2_token_identity_27_layers(cuda_device):
     summary = {"tokens_identical": not diff, "steps": STEPS, "flips_vs_oracle": diff, "near_ties_flipped": ties,
                "tokens_identical_to_control": toks_b == toks_c,
                "control_flips": diff_c, "max_logit_delta": max(deltas), "max_logit_delta_control": max(deltas_c),
+               "mean_logit_rel_l2": sum(rl2_b) / STEPS, "mean_logit_rel_l2_control": sum(rl2_c) / STEPS,
                "min_margin_a": min(margins),
                "layer0_row_mismatches": row_mism0, "max_row_rel": max(row_rel),
                "max_row_rel_control": max(row_rel_c),
@@ -125,9 +129,10 @@ def test_config2_token_identity_27_layers(cuda_device):
     # the library is no further from the oracle than an independent fp32 implementation is
     assert max(row_rel) <= max(2e-2, 1.5 * max(row_rel_c)), (max(row_rel), max(row_rel_c))
     assert max(deltas) <= 1.5 * max(deltas_c), (max(deltas), max(deltas_c))
-    # a token that differs from the oracle's must differ for the control too (a property of
-    # the model at bf16 working precision) or be a near-tie; at most one library-only tie
-    only_b = [s for s in diff if s not in diff_c]
-    real = [s for s in only_b if margins[s] > 2 * deltas[s]]
+    assert sum(rl2_b) <= 1.5 * sum(rl2_c), (sum(rl2_b) / STEPS, sum(rl2_c) / STEPS)
+    # every token that differs from the oracle's lies in that step's noise band (the oracle's
+    # top-2 margin is within twice the measured logit gap), and the library flips at most two
+    # steps more than the control does
+    real = [s for s in diff if margins[s] > 2 * deltas[s]]
     assert not real, f"steps {real}: tokens differ with oracle margins {[margins[s] for s in real]}"
-    assert len(only_b) <= 1, f"library-only near-tie flips at steps {only_b}"
+    assert len(diff) <= len(diff_c) + 2, f"library flips {diff} against control flips {diff_c}"
