@@ -27,6 +27,7 @@ cudaError_t k2_configure();
 cudaError_t k2_mma_configure();
 cudaError_t k3_configure();
 cudaError_t k0_configure();
+cudaError_t launch_rows_to_pages(const MlaRowsToPages& r, int sm_count, cudaStream_t stream);
 cudaError_t launch_project(const MlaDecodeParams& p, __nv_bfloat16* qkv, const CUtensorMap& tmap_w,
                            const CUtensorMap& tmap_x, cudaStream_t stream);
 
@@ -338,6 +339,33 @@ int mla_combine_shards(const float* parts, int32_t n_shards, int32_t batch, void
     return launch_combine_shards(parts, n_shards, batch, out, out_stride, (cudaStream_t)stream) == cudaSuccess
                ? MLA_OK
                : MLA_E_LAUNCH;
+}
+
+void mla_rows_init(MlaRowsToPages* r) {
+    if (!r) return;
+    *r = MlaRowsToPages{};
+    r->struct_size = sizeof(MlaRowsToPages);
+    r->abi_version = MLA_ABI_VERSION;
+    r->rms_eps = 1e-6f;
+}
+
+int mla_rows_to_pages(const MlaRowsToPages* r, void* stream) {
+    if (!r || r->struct_size != sizeof(MlaRowsToPages) || r->abi_version != MLA_ABI_VERSION) return MLA_E_INVALID_ARG;
+    if ((r->mode != MLA_ROWS_FINAL && r->mode != MLA_ROWS_RAW) || r->batch <= 0 || r->total_rows < 0 ||
+        !r->row_start || !r->block_table || !r->kv_cache || r->max_blocks <= 0 || r->n_pages <= 0 ||
+        r->rows_stride < MLA_ROW || (r->total_rows > 0 && !r->rows))
+        return MLA_E_INVALID_ARG;
+    if (r->batch > MLA_MAX_BATCH) return MLA_E_LIMIT;
+    if (r->mode == MLA_ROWS_RAW && (!r->kv_a_norm_w || !r->rope_cos || !r->rope_sin || r->max_pos <= 0 ||
+                                    !(r->rms_eps >= 0.f)))
+        return MLA_E_INVALID_ARG;
+    if (!aligned(r->rows, 16) || (r->rows_stride & 7) || !aligned(r->kv_cache, 16) || !aligned(r->row_start, 8) ||
+        !aligned(r->kv_a_norm_w, 2) || !aligned(r->rope_cos, 4) || !aligned(r->rope_sin, 4))
+        return MLA_E_MISALIGNED;
+    int sms = 0;
+    const int st = device_info(&sms);
+    if (st != MLA_OK) return st;
+    return launch_rows_to_pages(*r, sms, (cudaStream_t)stream) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 int mla_project(const MlaDecodeParams* p, void* stream) {

@@ -22,6 +22,7 @@
 
 #include "mla_common.cuh"
 #include "mla_mma.cuh"
+#include "mla_rowops.cuh"
 
 namespace mla {
 
@@ -42,18 +43,6 @@ struct K1Grid {
         total = n_absorb + 1;
     }
 };
-
-// DeepseekV2 RoPE on 64 values x[0..64): interleave-transpose, then rotate_half
-// (reference_decode.py:120-134). For pair j < 32:
-//   out[j]    = x[2j]*cos[j]       - x[2j+1]*sin[j]
-//   out[32+j] = x[2j+1]*cos[32+j]  + x[2j]*sin[32+j]
-// Products and the sum are rounded separately, as NumPy evaluates
-// `x * cos + rotate_half(x) * sin`.
-__device__ __forceinline__ void rope_pair(float x_even, float x_odd, const float* cs, const float* sn, int j,
-                                          float& lo, float& hi) {
-    lo = __fadd_rn(__fmul_rn(x_even, cs[j]), -__fmul_rn(x_odd, sn[j]));
-    hi = __fadd_rn(__fmul_rn(x_odd, cs[32 + j]), __fmul_rn(x_even, sn[32 + j]));
-}
 
 // Request b is valid if its RoPE position lies in the tables and its rows
 // (cached + the new one, if this call stores it) fit its block-table row.
@@ -121,58 +110,16 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
     }
     if (!new_row_count(p)) return;
 
-    // kv_post (reference_decode.py:60-65): var = mean(x^2); y = x * (1 / sqrt(var + eps));
-    // row = bf16(bf16(y) * weight). Lane owns c[16*lane, 16*lane+16).
-    float x[16];
-    {
-        const uint4* s4 = reinterpret_cast<const uint4*>(src) + 2 * lane;
-        uint4 v[2];
-        if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-            v[0] = s4[0]; v[1] = s4[1];
-            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(v);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) { x[2 * k] = __low2float(h2[k]); x[2 * k + 1] = __high2float(h2[k]); }
-        } else {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) x[k] = __bfloat162float(src[16 * lane + k]);
-        }
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) ss = __fadd_rn(ss, __fmul_rn(x[k], x[k]));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float var = __fdiv_rn(ss, (float)kLora);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.rms_eps)));
-    __align__(16) __nv_bfloat16 gw[16];  // gamma[16 lane, 16 lane + 16)
-    if ((reinterpret_cast<uintptr_t>(gam) & 15) == 0) {
-        reinterpret_cast<uint4*>(gw)[0] = reinterpret_cast<const uint4*>(gam)[2 * lane];
-        reinterpret_cast<uint4*>(gw)[1] = reinterpret_cast<const uint4*>(gam)[2 * lane + 1];
-    } else {
-#pragma unroll
-        for (int k = 0; k < 16; ++k) gw[k] = gam[16 * lane + k];
-    }
     __align__(16) __nv_bfloat16 outc[16];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        const float y = bf16_round(__fmul_rn(x[k], inv));
-        outc[k] = __float2bfloat16_rn(__fmul_rn(y, __bfloat162float(gw[k])));
-    }
     float lo, hi;
-    {
-        const __nv_bfloat16* kp = src + kLora + 2 * lane;
-        rope_pair(__bfloat162float(kp[0]), __bfloat162float(kp[1]), cs, sn, lane, lo, hi);
-    }
+    kv_post_compute(src, gam, p.rms_eps, cs, sn, lane, outc, lo, hi);
     const int page = p.block_table[(int64_t)b * p.max_blocks + pos / kPage];
     if (page < 0 || page >= p.n_pages) {
         if (lane == 0) record_error(p.error_word, MLA_DEV_BAD_PAGE);
         return;
     }
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.kv_cache) + ((int64_t)page * kPage + pos % kPage) * kRow;
-    reinterpret_cast<uint4*>(dst)[2 * lane] = reinterpret_cast<const uint4*>(outc)[0];
-    reinterpret_cast<uint4*>(dst)[2 * lane + 1] = reinterpret_cast<const uint4*>(outc)[1];
-    dst[kLora + lane] = __float2bfloat16_rn(lo);
-    dst[kLora + 32 + lane] = __float2bfloat16_rn(hi);
+    kv_post_store(reinterpret_cast<__nv_bfloat16*>(p.kv_cache) + ((int64_t)page * kPage + pos % kPage) * kRow, outc,
+                  lo, hi, lane);
 }
 
 __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p,

@@ -35,6 +35,7 @@ EXPORTED = (
     "mla_abi_version", "mla_status_string", "mla_device_error_string", "mla_params_init",
     "mla_workspace_size", "mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv",
     "mla_plan_info", "mla_launches_per_step", "mla_combine_shards", "mla_decode_step_static", "mla_project",
+    "mla_rows_init", "mla_rows_to_pages",
 )
 
 
@@ -75,6 +76,25 @@ class MlaDecodeParams(ctypes.Structure):
     ]
 
 
+ROWS_FINAL = 0  # MLA_ROWS_FINAL: finished cache rows, copied
+ROWS_RAW = 1    # MLA_ROWS_RAW: raw kv_a rows, kv_a_layernorm + RoPE applied
+
+
+class MlaRowsToPages(ctypes.Structure):
+    """Mirror of MlaRowsToPages (include/mla_decode.h), field for field."""
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("abi_version", ctypes.c_uint32),
+        ("mode", ctypes.c_int32), ("batch", ctypes.c_int32), ("total_rows", ctypes.c_int64),
+        ("rows", ctypes.c_void_p), ("rows_stride", ctypes.c_int64),
+        ("row_start", ctypes.c_void_p), ("first_pos", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p), ("max_blocks", ctypes.c_int32), ("n_pages", ctypes.c_int32),
+        ("kv_cache", ctypes.c_void_p), ("kv_a_norm_w", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
+        ("max_pos", ctypes.c_int32), ("rms_eps", ctypes.c_float),
+        ("error_word", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -107,6 +127,11 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.mla_combine_shards.restype = ctypes.c_int
         lib.mla_combine_shards.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                            ctypes.c_int64, ctypes.c_void_p]
+        R = ctypes.POINTER(MlaRowsToPages)
+        lib.mla_rows_init.restype = None
+        lib.mla_rows_init.argtypes = [R]
+        lib.mla_rows_to_pages.restype = ctypes.c_int
+        lib.mla_rows_to_pages.argtypes = [R, ctypes.c_void_p]
         for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv", "mla_decode_step_static",
                    "mla_project"):
             f = getattr(lib, fn)
@@ -122,6 +147,12 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
 def check(code: int, what: str, params: "MlaDecodeParams | None" = None) -> None:
     if code != 0:
         raise MlaError(code, what, params)
+
+
+def new_rows() -> MlaRowsToPages:
+    r = MlaRowsToPages()
+    load_library().mla_rows_init(ctypes.byref(r))
+    return r
 
 
 def new_params() -> MlaDecodeParams:

@@ -198,6 +198,43 @@ int mla_launches_per_step(void);
 int mla_combine_shards(const float* parts, int32_t n_shards, int32_t batch, void* out, int64_t out_stride,
                        void* stream);
 
+/* Prefill hand-off: rows of a prefill into the paged cache. Replaces the
+ * reference's flat per-layer cache [max_pos][576] bf16, built from the hooked
+ * kv_a_proj_with_mqa output by src/host/kv_convert.py:36-139 and uploaded as-is
+ * by src/host/fleet_launch.hip:651-669; here each request's rows are scattered
+ * into its pages at positions first_pos[b], first_pos[b] + 1, ... */
+#define MLA_ROWS_FINAL 0  /* rows are cache rows already (c after kv_a_layernorm | k_pe after RoPE): copied;
+                             this is the reference's cache-file row format */
+#define MLA_ROWS_RAW 1    /* rows are raw kv_a (the kv_a_proj_with_mqa output): kv_a_layernorm and RoPE at the
+                             row's position are applied, with the arithmetic of the decode step's new row */
+
+typedef struct MlaRowsToPages {
+    uint32_t struct_size;      /* sizeof(MlaRowsToPages) */
+    uint32_t abi_version;      /* MLA_ABI_VERSION */
+    int32_t mode;              /* MLA_ROWS_FINAL or MLA_ROWS_RAW */
+    int32_t batch;             /* requests, 1..MLA_MAX_BATCH */
+    int64_t total_rows;        /* row_start[batch], as known to the host (sizes the grid) */
+    const void* rows;          /* bf16 [total_rows][rows_stride], 16-byte aligned */
+    int64_t rows_stride;       /* elements between rows: >= 576, a multiple of 8 */
+    const int64_t* row_start;  /* device [batch + 1]: request b's rows are rows[row_start[b], row_start[b+1]) */
+    const int32_t* first_pos;  /* device [batch]: position of request b's first row; NULL = 0 */
+    const int32_t* block_table;
+    int32_t max_blocks;
+    int32_t n_pages;
+    void* kv_cache;            /* [n_pages][64][576] bf16, 16-byte aligned */
+    const void* kv_a_norm_w;   /* MLA_ROWS_RAW: bf16 [512] kv_a_layernorm.weight */
+    const float* rope_cos;     /* MLA_ROWS_RAW: [max_pos][64] YaRN tables */
+    const float* rope_sin;
+    int32_t max_pos;           /* MLA_ROWS_RAW */
+    float rms_eps;             /* MLA_ROWS_RAW */
+    int32_t* error_word;       /* optional: MLA_DEV_BAD_POSITION / MLA_DEV_BAD_PAGE; such rows are skipped */
+} MlaRowsToPages;
+
+/* Fill an MlaRowsToPages with its size and version, everything else zero. */
+void mla_rows_init(MlaRowsToPages* r);
+
+int mla_rows_to_pages(const MlaRowsToPages* r, void* stream);
+
 /* Size of the workspace that mla_decode_step_static keeps inside the library, per
  * device: 32 MiB, which holds mla_workspace_size() for up to 558 requests at 148
  * CTAs (one per SM of a B200). */

@@ -289,3 +289,38 @@ def combine_partials(parts):
         acc = acc + w[:, None] * y
         W = W + w
     return bf16_round((acc / W[:, None]).reshape(-1).astype(np.float32))
+
+
+# ------------------------------------------------------------------ prefill hand-off
+
+def flat_cache_file_bytes(rows_per_layer, max_pos: int) -> bytes:
+    """The reference's prefill->decode cache file (src/host/kv_convert.py:124-139,
+    write_fleet_cache_bin): raw bf16 [layers][max_pos][576] in C order, each layer's
+    prefill rows at positions 0..S-1 and zeros after. rows_per_layer: fp32 arrays
+    [S, 576] holding bf16 values."""
+    layers = len(rows_per_layer)
+    full = np.zeros((layers, max_pos, rows_per_layer[0].shape[1]), np.float32)
+    for l, r in enumerate(rows_per_layer):
+        full[l, : r.shape[0]] = r
+    u = bf16_round(full).view(np.uint32) >> np.uint32(16)
+    return u.astype(np.uint16).tobytes(order="C")
+
+
+def scatter_rows(pages: np.ndarray, block_table: np.ndarray, rows: np.ndarray, row_start, first_pos=None) -> None:
+    """Paged placement of request b's rows row_start[b]..row_start[b+1]-1 at positions
+    first_pos[b] + i: position t is page block_table[b][t // 64], slot t % 64 (the
+    paged layout that replaces the flat [max_pos][576] cache of
+    src/runtime/fleet_types.h:106-111). pages: [n_pages, 64, 576], updated in place."""
+    for b in range(len(row_start) - 1):
+        p0 = 0 if first_pos is None else int(first_pos[b])
+        for i in range(int(row_start[b]), int(row_start[b + 1])):
+            t = p0 + i - int(row_start[b])
+            pages[int(block_table[b][t // 64]), t % 64] = rows[i]
+
+
+def prefill_rows(cfg: Config, w: Weights, kv_a_raw: np.ndarray, first_pos: int, cos, sin) -> np.ndarray:
+    """Cache rows of a prefill's raw kv_a rows [S, 576] at positions first_pos + i: the
+    decode step's row arithmetic (kv_post, reference_decode.py:230-237) per position,
+    which is what kv_convert.build_fleet_cache (src/host/kv_convert.py:92-121) computes
+    with HF's bf16 modules."""
+    return np.stack([kv_post(cfg, w, kv_a_raw[i], first_pos + i, cos, sin) for i in range(kv_a_raw.shape[0])])
