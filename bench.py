@@ -124,7 +124,7 @@ def build_workload(name: str, dev: torch.device, rank: int):
     cfg = fleet.ModelConfig()
     lw = workloads.make_layer_weights(wl.seed)
     w = fleet.LayerWeights(*(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm,
-                                                   lw.kv_b_proj)))
+                                                   lw.kv_b_proj, lw.o_proj)))
     cos, sin = fleet.device_rope_tables(cfg, max(lengths) + 8, dev)
     cache = fleet.PagedLatentCache.for_lengths(lengths, permute=wl.permute, zero=False,
                                                generator=torch.Generator().manual_seed(wl.seed + rank), device=dev)
@@ -155,7 +155,8 @@ class StepTimer:
     """CUDA-event timing of repeated calls on the launching stream. When a step reads
     less than 4x L2 of cache rows, 256 MB are written between timed calls (outside the
     timed events, one event pair per call) so that no call finds the previous one's
-    rows in L2."""
+    rows in L2; a ~50 us spin follows the flush, so that the call's launches are queued
+    before its start event fires and the events hold device time only."""
 
     def __init__(self, stream: torch.cuda.Stream, kv_bytes: int, device):
         self.stream = stream
@@ -170,6 +171,7 @@ class StepTimer:
         torch.cuda.synchronize()
         for a, b in evs:
             self.flush.zero_()
+            torch.cuda._sleep(100_000)
             a.record(self.stream)
             fn()
             b.record(self.stream)
@@ -343,6 +345,19 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                       "k0_gbs": round(w_bytes / (k0_ms * 1e-3) / 1e9, 1),
                       "k0_frac_of_peak": round(w_bytes / (k0_ms * 1e-3) / 1e9 / peak, 4),
                       "l2": "flushed: 256 MB written before every timed call, outside its CUDA events"}
+        # K5: o_proj + residual after the task, against cuBLAS o_proj + the bf16 add
+        h = torch.randn(B, 2048, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(dev)
+        h2 = torch.empty_like(h)
+        po = runner.params(None, None, cache, out, x_n=x_n, residual=h, h_out=h2)
+        native.check(lib.mla_o_proj(ctypes.byref(po), sptr), "o_proj")
+        k5_ms = ptimer(lambda: lib.mla_o_proj(ctypes.byref(po), sptr), max(5, args.steps))
+        cub5_ms = ptimer(lambda: torch.add(h, torch.nn.functional.linear(out, runner.w_o), out=h2),
+                         max(5, args.steps))
+        wo_bytes = runner.w_o.numel() * 2
+        projection["o_proj"] = {"kernel": "k_weight_stream<16, residual>", "weight_bytes": wo_bytes,
+                                "k5_us": round(k5_ms * 1e3, 2), "cublas_plus_add_us": round(cub5_ms * 1e3, 2),
+                                "k5_gbs": round(wo_bytes / (k5_ms * 1e-3) / 1e9, 1),
+                                "k5_frac_of_peak": round(wo_bytes / (k5_ms * 1e-3) / 1e9 / peak, 4)}
 
     # ---- e2e through the public call: pinned host x_n -> device, task, R(out) -> host
     x_host = x_n.cpu().pin_memory()

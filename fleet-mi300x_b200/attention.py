@@ -35,6 +35,7 @@ class LayerWeights:
     kv_a_proj_with_mqa: torch.Tensor   # [576, hidden] bf16
     kv_a_layernorm: torch.Tensor       # [512] bf16
     kv_b_proj: torch.Tensor            # [heads*256, 512] bf16
+    o_proj: torch.Tensor | None = None  # [hidden, heads*v_head] bf16 (optional: attention_block)
 
     def fused_qkv(self) -> torch.Tensor:
         return torch.cat([self.q_proj, self.kv_a_proj_with_mqa], dim=0).contiguous()
@@ -75,6 +76,7 @@ class MlaDecodeAttention:
         self.device = dev
         self.w = w
         self.w_qkv = w.fused_qkv()
+        self.w_o = None if w.o_proj is None else w.o_proj.contiguous()
         self.kv_b = w.kv_b_proj.contiguous()
         self.norm_w = w.kv_a_layernorm.contiguous()
         self.cos = rope_cos.contiguous().float()
@@ -92,9 +94,11 @@ class MlaDecodeAttention:
     def params(self, q: torch.Tensor | None, kv_a: torch.Tensor | None, cache: PagedLatentCache,
                out: torch.Tensor | None, *, rope_pos: torch.Tensor | None = None,
                shard_out: torch.Tensor | None = None, new_row: bool = True,
-               x_n: torch.Tensor | None = None) -> native.MlaDecodeParams:
+               x_n: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+               h_out: torch.Tensor | None = None) -> native.MlaDecodeParams:
         """The C-ABI params of one step. With `x_n` (and q = kv_a = None) the library
-        projects q | kv_a itself with the fused [W_q; W_kv_a] weight (K0)."""
+        projects q | kv_a itself with the fused [W_q; W_kv_a] weight (K0); with
+        `residual` and `h_out` it ends with h_out = R(residual + R(W_o R(out))) (K5)."""
         B = (x_n if x_n is not None else q).shape[0]
         p = native.new_params()
         p.softmax_scale = self.cfg.softmax_scale
@@ -121,6 +125,12 @@ class MlaDecodeAttention:
         p.flags = self.flags | (0 if new_row else native.FLAG_NO_NEW_ROW)
         p.rope_pos = _ptr(rope_pos)
         p.shard_out = _ptr(shard_out)
+        if h_out is not None:
+            if self.w_o is None:
+                raise ValueError("o_proj + residual needs LayerWeights.o_proj")
+            p.w_o = _ptr(self.w_o)
+            p.residual, p.residual_stride = _ptr(residual), _row_stride(residual)
+            p.h_out, p.h_out_stride = _ptr(h_out), _row_stride(h_out)
         need = ctypes.c_uint64()
         native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
         if self._ws is None or self._ws.numel() < need.value:
@@ -177,14 +187,7 @@ class MlaDecodeAttention:
                  stage: str = "all") -> torch.Tensor:
         """The whole slice in the library, from the post-RMSNorm hidden state x_n
         [B, 2048] bf16 (B <= 64): K0 projects q | kv_a, then K1-K3 as in attend()."""
-        if x_n.dtype != torch.bfloat16 or x_n.dim() != 2 or x_n.shape[1] != self.cfg.hidden:
-            raise ValueError(f"x_n must be bf16 [B, {self.cfg.hidden}], got {x_n.dtype} {tuple(x_n.shape)}")
-        if x_n.stride(-1) != 1:
-            raise ValueError("x_n rows must be contiguous")
-        if x_n.shape[0] != cache.batch:
-            raise ValueError(f"batch {x_n.shape[0]} does not match the cache's {cache.batch} requests")
-        if x_n.shape[0] > native.MAX_PROJECT_BATCH:
-            raise ValueError(f"the in-library projection takes at most {native.MAX_PROJECT_BATCH} requests")
+        self._check_x(x_n, cache)
         if out is None:
             out = torch.empty(x_n.shape[0], self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16,
                               device=self.device)
@@ -201,6 +204,45 @@ class MlaDecodeAttention:
               "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv}[stage]
         native.check(fn(ctypes.byref(p), stream), f"mla {stage}", p)
         return out
+
+    def attention_block(self, x_n: torch.Tensor, cache: PagedLatentCache, residual: torch.Tensor,
+                        h_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The attention half of a decoder layer (reference_decode.py:300):
+        h_out = R(residual + R(W_o R(attention(x_n)))), with R(out) left in `out`.
+        Decode batches (<= 64 requests) run as one library call, K0 through K5;
+        larger ones use cuBLAS for the two projections around attend()."""
+        B = x_n.shape[0]
+        if self.w_o is None:
+            raise ValueError("attention_block needs LayerWeights.o_proj")
+        if residual.dtype != torch.bfloat16 or tuple(residual.shape) != (B, self.cfg.hidden):
+            raise ValueError(f"residual must be bf16 [{B}, {self.cfg.hidden}]")
+        if h_out is None:
+            h_out = torch.empty_like(residual)
+        if out is None:
+            out = torch.empty(B, self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16, device=self.device)
+        fused = (B <= native.MAX_PROJECT_BATCH and x_n.stride(-1) == 1 and x_n.data_ptr() % 16 == 0
+                 and _row_stride(x_n) % 8 == 0 and out.data_ptr() % 16 == 0 and _row_stride(out) % 8 == 0
+                 and residual.stride(-1) == 1 and h_out.stride(-1) == 1 and _row_stride(residual) % 4 == 0
+                 and _row_stride(h_out) % 4 == 0)
+        if not fused:
+            attn = self(x_n, cache, out)
+            h_out.copy_(residual + torch.nn.functional.linear(attn, self.w_o))
+            return h_out
+        self._check_x(x_n, cache)
+        p = self.params(None, None, cache, out, x_n=x_n, residual=residual, h_out=h_out)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        native.check(self.lib.mla_decode_step(ctypes.byref(p), stream), "mla attention block", p)
+        return h_out
+
+    def _check_x(self, x_n: torch.Tensor, cache: PagedLatentCache) -> None:
+        if x_n.dtype != torch.bfloat16 or x_n.dim() != 2 or x_n.shape[1] != self.cfg.hidden:
+            raise ValueError(f"x_n must be bf16 [B, {self.cfg.hidden}], got {x_n.dtype} {tuple(x_n.shape)}")
+        if x_n.stride(-1) != 1:
+            raise ValueError("x_n rows must be contiguous")
+        if x_n.shape[0] != cache.batch:
+            raise ValueError(f"batch {x_n.shape[0]} does not match the cache's {cache.batch} requests")
+        if x_n.shape[0] > native.MAX_PROJECT_BATCH:
+            raise ValueError(f"the in-library projection takes at most {native.MAX_PROJECT_BATCH} requests")
 
     def project(self, x_n: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """q = R(W_q x_n), kv_a = R(W_kv_a x_n) as views of one bf16 GEMM output."""

@@ -28,6 +28,8 @@ cudaError_t k2_mma_configure();
 cudaError_t k3_configure();
 cudaError_t k0_configure();
 cudaError_t launch_rows_to_pages(const MlaRowsToPages& r, int sm_count, cudaStream_t stream);
+cudaError_t launch_o_proj(const MlaDecodeParams& p, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                          cudaStream_t stream);
 cudaError_t launch_project(const MlaDecodeParams& p, __nv_bfloat16* qkv, const CUtensorMap& tmap_w,
                            const CUtensorMap& tmap_x, cudaStream_t stream);
 
@@ -115,15 +117,16 @@ int make_tmap_kvb(CUtensorMap* m, const void* kv_b, int blocks) {
     return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
 }
 
-// The stacked [W_q; W_kv_a] (3648 rows x 2048 bf16) as dims {64 columns, 3648
-// rows (4096 B), 32 column blocks (128 B)}, box {64, 32, 8}: 32 weight rows x
-// 512 columns = 32 KB landing as [8][32 rows][128 B] (128-byte swizzle).
-int make_tmap_wqkv(CUtensorMap* m, const void* w) {
+// A [rows x 2048] bf16 weight (the stacked [W_q; W_kv_a], 3648 rows, or W_o,
+// 2048 rows) as dims {64 columns, rows (4096 B), 32 column blocks (128 B)}, box
+// {64, box_rows, 8}: box_rows weight rows x 512 columns landing as
+// [8][box_rows rows][128 B] (128-byte swizzle).
+int make_tmap_weight(CUtensorMap* m, const void* w, int rows, int box_rows) {
     PFN_cuTensorMapEncodeTiled_v12000 fn;
     if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
-    cuuint64_t dims[3] = {64, (cuuint64_t)kQkvRows, kHidden / 64};
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, kHidden / 64};
     cuuint64_t strides[2] = {(cuuint64_t)kHidden * 2, 128};
-    cuuint32_t box[3] = {64, 32, 8};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 8};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -149,12 +152,21 @@ int make_tmap_x(CUtensorMap* m, const void* x, int batch, int64_t x_stride) {
 
 int run_project(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap tw, tx;
-    int st = make_tmap_wqkv(&tw, q.w_qkv);
+    int st = make_tmap_weight(&tw, q.w_qkv, kQkvRows, 32);
     if (st != MLA_OK) return st;
     st = make_tmap_x(&tx, q.x_n, q.batch, q.x_stride);
     if (st != MLA_OK) return st;
     __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(q.workspace) + ws_layout(q).qkv);
     return launch_project(q, qkv, tw, tx, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+int run_o_proj(const MlaDecodeParams& q, cudaStream_t s) {
+    CUtensorMap tw, tx;
+    int st = make_tmap_weight(&tw, q.w_o, kHidden, 16);
+    if (st != MLA_OK) return st;
+    st = make_tmap_x(&tx, q.out, q.batch, q.out_stride);
+    if (st != MLA_OK) return st;
+    return launch_o_proj(q, tw, tx, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 int run_prologue(const MlaDecodeParams& q, cudaStream_t s) {
@@ -203,6 +215,14 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
     if (!p->kv_a_norm_w || !p->kv_b || !p->rope_cos || !p->rope_sin || !p->block_table ||
         !p->seq_lens || !p->kv_cache || (!p->out && !p->shard_out) || !p->workspace)
         return MLA_E_INVALID_ARG;
+    if (p->w_o) {  // K5 reads `out` back through a TMA map and writes h_out
+        if (!p->out || p->shard_out || !p->residual || !p->h_out) return MLA_E_INVALID_ARG;
+        if (p->batch > MLA_MAX_PROJECT_BATCH) return MLA_E_LIMIT;
+        if (p->residual_stride < MLA_HIDDEN || p->h_out_stride < MLA_HIDDEN) return MLA_E_INVALID_ARG;
+        if (!aligned(p->out, 16) || (p->out_stride & 7) || !aligned(p->w_o, 16) || !aligned(p->residual, 8) ||
+            (p->residual_stride & 3) || !aligned(p->h_out, 8) || (p->h_out_stride & 3))
+            return MLA_E_MISALIGNED;
+    }
     if (project) {
         if (p->batch > MLA_MAX_PROJECT_BATCH) return MLA_E_LIMIT;
         if (p->x_stride < MLA_HIDDEN) return MLA_E_INVALID_ARG;
@@ -376,6 +396,14 @@ int mla_project(const MlaDecodeParams* p, void* stream) {
     return run_project(q, (cudaStream_t)stream);
 }
 
+int mla_o_proj(const MlaDecodeParams* p, void* stream) {
+    MlaDecodeParams q;
+    int st = prepare(p, &q);
+    if (st != MLA_OK) return st;
+    if (!q.w_o) return MLA_E_INVALID_ARG;
+    return run_o_proj(q, (cudaStream_t)stream);
+}
+
 int mla_prologue(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;
     int st = prepare(p, &q);
@@ -410,7 +438,9 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream) {
     if (st != MLA_OK) return st;
     st = run_attention(q, s);
     if (st != MLA_OK) return st;
-    return run_merge(q, s);
+    st = run_merge(q, s);
+    if (st != MLA_OK || !q.w_o) return st;
+    return run_o_proj(q, s);
 }
 
 }  // extern "C"

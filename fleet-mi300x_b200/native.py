@@ -13,7 +13,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libmla_decode.so"
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 HEADS, QK_NOPE, QK_ROPE, V_HEAD, KV_LORA, PAGE_SIZE = 16, 128, 64, 128, 512, 64
 ROW = KV_LORA + QK_ROPE
 MAX_BATCH = 65536
@@ -35,7 +35,7 @@ EXPORTED = (
     "mla_abi_version", "mla_status_string", "mla_device_error_string", "mla_params_init",
     "mla_workspace_size", "mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv",
     "mla_plan_info", "mla_launches_per_step", "mla_combine_shards", "mla_decode_step_static", "mla_project",
-    "mla_rows_init", "mla_rows_to_pages",
+    "mla_rows_init", "mla_rows_to_pages", "mla_o_proj",
 )
 
 
@@ -73,6 +73,8 @@ class MlaDecodeParams(ctypes.Structure):
         ("num_ctas", ctypes.c_int32), ("flags", ctypes.c_int32),
         ("rope_pos", ctypes.c_void_p), ("shard_out", ctypes.c_void_p),
         ("x_n", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("w_qkv", ctypes.c_void_p),
+        ("w_o", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("residual_stride", ctypes.c_int64),
+        ("h_out", ctypes.c_void_p), ("h_out_stride", ctypes.c_int64),
     ]
 
 
@@ -133,7 +135,7 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.mla_rows_to_pages.restype = ctypes.c_int
         lib.mla_rows_to_pages.argtypes = [R, ctypes.c_void_p]
         for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv", "mla_decode_step_static",
-                   "mla_project"):
+                   "mla_project", "mla_o_proj"):
             f = getattr(lib, fn)
             f.restype = ctypes.c_int
             f.argtypes = [P, ctypes.c_void_p]

@@ -69,7 +69,9 @@ def make_layer_weights(seed: int, device="cpu", std: float = 0.02, norm: str = "
         gam = torch.ones(c.kv_lora_rank)
     else:
         gam = torch.rand(c.kv_lora_rank, generator=g) * 0.4 + 0.8
-    return LayerWeights(_bf16(q).to(device), _bf16(kva).to(device), _bf16(gam).to(device), _bf16(kvb).to(device))
+    wo = torch.randn(c.hidden, c.heads * c.v_head, generator=g) * std  # drawn last: the others keep their values
+    return LayerWeights(_bf16(q).to(device), _bf16(kva).to(device), _bf16(gam).to(device), _bf16(kvb).to(device),
+                        _bf16(wo).to(device))
 
 
 def rms_normalise(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:

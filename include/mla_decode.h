@@ -14,7 +14,8 @@
  * persistent kernel (src/kernels/fleet_kernel.hip:647-654 TASK_Q_ABSORB,
  * :745-798 TASK_ATTENTION, :694-701 TASK_MERGE_UV), launched through
  * `extern "C" hipError_t fleet_launch_step(...)` (fleet_kernel.hip:1068-1078).
- * Here the same work is three (four, with the projection) stream-ordered kernels behind plain C entry
+ * Here the same work is three stream-ordered kernels (up to five, with the
+ * q | kv_a projection before and o_proj + residual after) behind plain C entry
  * points: pointers, sizes and a caller-provided workspace; no allocation, no
  * torch types, no global mutable state except a per-device attribute cache.
  *
@@ -45,7 +46,7 @@
 extern "C" {
 #endif
 
-#define MLA_ABI_VERSION 3
+#define MLA_ABI_VERSION 4
 
 /* Fixed model dimensions. The reference's launcher refuses any other shape
  * (src/host/fleet_launch.hip:573-577: kv_lora != 512 or qk_rope != 64);
@@ -142,6 +143,17 @@ typedef struct MlaDecodeParams {
     int64_t x_stride;         /* elements between rows, a multiple of 8, >= MLA_HIDDEN */
     const void* w_qkv;        /* [MLA_QKV_ROWS][MLA_HIDDEN] bf16 = rows of q_proj then kv_a_proj_with_mqa,
                                  16-byte aligned */
+
+    /* In-library o_proj with the layer's residual add (ABI v4). If w_o is set,
+     * the step ends with h_out = R(residual + R(W_o R(out))) (K5;
+     * reference_decode.py:256, 300), reading `out` back (then 16-byte aligned,
+     * out_stride a multiple of 8, not with shard_out); the batch is limited to
+     * MLA_MAX_PROJECT_BATCH. NULL = the step ends at R(out). */
+    const void* w_o;          /* [MLA_HIDDEN][MLA_HEADS*MLA_V_HEAD] bf16 o_proj.weight, 16-byte aligned */
+    const void* residual;     /* [batch][residual_stride] bf16: the layer's input hidden state */
+    int64_t residual_stride;  /* elements between rows, a multiple of 4, >= MLA_HIDDEN */
+    void* h_out;              /* [batch][h_out_stride] bf16: the new hidden state; may be `residual` itself */
+    int64_t h_out_stride;     /* elements between rows, a multiple of 4, >= MLA_HIDDEN */
 } MlaDecodeParams;
 
 #define MLA_SHARD_STRIDE (MLA_V_HEAD + 4)
@@ -179,6 +191,10 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream);
  * With p->x_n set, mla_decode_step runs K0 first. */
 int mla_project(const MlaDecodeParams* p, void* stream);
 int mla_prologue(const MlaDecodeParams* p, void* stream);
+/* K5 = o_proj + residual (needs p->w_o; TASK_O_PROJ with the EPI_RESIDUAL
+ * epilogue, fleet_kernel.hip:805-824, gemv.h:225). With p->w_o set,
+ * mla_decode_step runs it last. */
+int mla_o_proj(const MlaDecodeParams* p, void* stream);
 int mla_attention(const MlaDecodeParams* p, void* stream);
 int mla_merge_uv(const MlaDecodeParams* p, void* stream);
 

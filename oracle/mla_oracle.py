@@ -324,3 +324,10 @@ def prefill_rows(cfg: Config, w: Weights, kv_a_raw: np.ndarray, first_pos: int, 
     which is what kv_convert.build_fleet_cache (src/host/kv_convert.py:92-121) computes
     with HF's bf16 modules."""
     return np.stack([kv_post(cfg, w, kv_a_raw[i], first_pos + i, cos, sin) for i in range(kv_a_raw.shape[0])])
+
+
+def o_proj_residual(cfg: Config, w_o: np.ndarray, out: np.ndarray, h: np.ndarray) -> np.ndarray:
+    """The attention half's last two lines: R(W_o R(out)) (reference_decode.py:256),
+    then the bf16 residual add x = R(x + attn) (:300). out: R(out) [heads*v_head],
+    h: the layer input [hidden]; both bf16-valued."""
+    return cfg.r(h + cfg.r(w_o @ out))
