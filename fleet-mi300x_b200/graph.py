@@ -69,3 +69,61 @@ class DecodeGraph:
         """Run the captured step on the current stream; returns `out`."""
         self.graph.replay()
         return self.out
+
+
+class HostPipeline:
+    """The host-facing decode loop of one layer: x_n from pinned host memory in, R(out)
+    to pinned host memory out, with the copies of neighbouring steps overlapping the
+    compute of this one.
+
+    Two DecodeGraphs over double-buffered device x_n / out are replayed on a compute
+    stream; the host-to-device copy of step k+1 and the device-to-host copy of step k-1
+    run on two copy streams meanwhile, ordered by events. `submit(x_host)` queues one step
+    and returns the pinned host tensor that will hold its R(out); that tensor is reused
+    two steps later, so read it (after `wait()` or `synchronize()`) before then.
+    """
+
+    def __init__(self, runner: MlaDecodeAttention, cache: PagedLatentCache, *, advance: bool = False):
+        cfg, dev, B = runner.cfg, runner.device, cache.batch
+        bf = torch.bfloat16
+        self.device = dev
+        self.x_dev = [torch.zeros(B, cfg.hidden, dtype=bf, device=dev) for _ in range(2)]
+        self.out_dev = [torch.empty(B, cfg.heads * cfg.v_head, dtype=bf, device=dev) for _ in range(2)]
+        self.out_host = [torch.empty(B, cfg.heads * cfg.v_head, dtype=bf).pin_memory() for _ in range(2)]
+        self.graphs = [DecodeGraph(runner, cache, inputs="x_n", advance=advance, x_n=self.x_dev[i],
+                                   out=self.out_dev[i]) for i in range(2)]
+        self.compute = torch.cuda.Stream(dev)
+        self.h2d = torch.cuda.Stream(dev)  # separate from d2h: the input copy of step k+1 must not
+        self.d2h = torch.cuda.Stream(dev)  # queue behind the output copy of step k
+        self.x_ready = [torch.cuda.Event() for _ in range(2)]
+        self.done = [torch.cuda.Event() for _ in range(2)]
+        self.out_read = [torch.cuda.Event() for _ in range(2)]
+        self.k = 0
+        self._used = [False, False]
+
+    def submit(self, x_host: torch.Tensor) -> torch.Tensor:
+        """Queue one step whose input is the pinned host tensor x_host [B, hidden] bf16."""
+        i = self.k % 2
+        with torch.cuda.stream(self.h2d):
+            if self._used[i]:
+                self.h2d.wait_event(self.done[i])  # x_dev[i] is free once step k-2 has computed
+            self.x_dev[i].copy_(x_host, non_blocking=True)
+            self.x_ready[i].record(self.h2d)
+        with torch.cuda.stream(self.compute):
+            self.compute.wait_event(self.x_ready[i])
+            if self._used[i]:
+                self.compute.wait_event(self.out_read[i])  # out_dev[i] copied out by step k-2
+            self.graphs[i].replay()
+            self.done[i].record(self.compute)
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(self.done[i])
+            self.out_host[i].copy_(self.out_dev[i], non_blocking=True)
+            self.out_read[i].record(self.d2h)
+        self._used[i] = True
+        self.k += 1
+        return self.out_host[i]
+
+    def wait(self) -> None:
+        """Block until every submitted step's R(out) is in host memory."""
+        for st in (self.h2d, self.compute, self.d2h):
+            st.synchronize()

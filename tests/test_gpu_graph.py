@@ -60,3 +60,26 @@ def test_graph_from_qkv_matches_eager(cuda_device):
     torch.cuda.synchronize(cuda_device)
     runner.check_errors()
     assert torch.equal(got, want)
+
+
+def test_host_pipeline_matches_eager_loop(cuda_device):
+    runner, cache_e = _runner_and_cache(cuda_device, seed=23)
+    cache_p = _clone(cache_e)
+    pipe = fleet.HostPipeline(runner, cache_p, advance=True)
+    g = torch.Generator().manual_seed(8)
+    xs = [torch.randn(len(LENS), 2048, generator=g).to(torch.bfloat16).pin_memory() for _ in range(5)]
+    got = []
+    for k, x in enumerate(xs):
+        got.append(pipe.submit(x))
+        if k % 2 == 1:  # each host buffer is reused two steps later: read it before then
+            pipe.wait()
+            got[k - 1], got[k] = got[k - 1].clone(), got[k].clone()
+    pipe.wait()
+    got[-1] = got[-1].clone()
+    for k, x in enumerate(xs):
+        want = runner(x.to(cuda_device), cache_e).cpu()
+        cache_e.advance()
+        assert torch.equal(got[k], want), f"step {k}"
+    runner.check_errors()
+    assert torch.equal(cache_p.seq_lens, cache_e.seq_lens)
+    assert torch.equal(cache_p.pages, cache_e.pages)
