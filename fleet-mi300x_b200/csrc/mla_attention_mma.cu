@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 int page = p.block_table[(int64_t)cur.b * p.max_blocks + cur.page_index()];
                 if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
                 const uint32_t slot = t % kNTile, n = t / kNTile;
-                if (n > 0 && !mbar_wait(&S.tile_empty[slot], (n - 1) & 1, abort, p.error_word)) break;
+                if (n > 0 && !mbar_wait_idle(&S.tile_empty[slot], (n - 1) & 1, abort, p.error_word)) break;
                 mbar_arrive_expect_tx(&S.tile_full[slot], kTileBytes);
                 tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.tile_full[slot], 0, 0, 0, page, kCacheEvictFirst);
             }
