@@ -22,7 +22,7 @@ cudaError_t k1_configure();
 cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,
                                   cudaStream_t stream);
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
-                                 cudaStream_t stream);
+                                 int sm_count, cudaStream_t stream);
 cudaError_t k2_configure();
 cudaError_t k2_mma_configure();
 cudaError_t k3_configure();
@@ -84,15 +84,16 @@ int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* fn) {
 // bf16 tensor maps over 576-wide rows (1152 B pitch) that land in shared
 // memory as 9 column blocks of [rows x 64] with the 128-byte swizzle:
 // dims {64 columns, rows (pitch 1152 B), 9 blocks (pitch 128 B)[, pages]}.
-// The page map (rank 4) serves one whole 64-row page per request; the
+// The page map (rank 4) serves box_rows rows of one page per request (64: a
+// whole page, the tcgen05 kernel; 32: half a page, the m16n8k16 kernel); the
 // query map (rank 3) one request's 16 absorbed-query rows.
-int make_tmap_blocks(CUtensorMap* m, const void* base, uint64_t rows_or_pages, bool paged) {
+int make_tmap_blocks(CUtensorMap* m, const void* base, uint64_t rows_or_pages, bool paged, int box_rows) {
     PFN_cuTensorMapEncodeTiled_v12000 fn;
     if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
     const cuuint32_t rank = paged ? 4 : 3;
     cuuint64_t dims[4] = {64, paged ? (cuuint64_t)kPage : (cuuint64_t)rows_or_pages, 9, (cuuint64_t)rows_or_pages};
     cuuint64_t strides[3] = {(cuuint64_t)kRow * 2, 128, (cuuint64_t)kPage * kRow * 2};
-    cuuint32_t box[4] = {64, paged ? (cuuint32_t)kPage : (cuuint32_t)kQRows, 9, 1};
+    cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 9, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -185,13 +186,16 @@ int run_merge(const MlaDecodeParams& q, cudaStream_t s) {
 
 bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }
 
+// CTAs of the split plan: p->num_ctas, or by default as many as run at once:
+// two per SM for the m16n8k16 kernel (each of its CTAs runs two plan CTAs as
+// independent warp groups) and the checker, one per SM for the tcgen05 kernel.
 int resolve_ctas(const MlaDecodeParams* p, int* ctas) {
     if (p->num_ctas < 0 || p->num_ctas > kMaxCtas) return MLA_E_LIMIT;
     if (p->num_ctas > 0) { *ctas = p->num_ctas; return MLA_OK; }
     int sms = 0;
     const int st = device_info(&sms);
     if (st != MLA_OK) return st;
-    *ctas = sms;
+    *ctas = (p->flags & MLA_FLAG_TCGEN05) ? sms : 2 * sms;
     return MLA_OK;
 }
 
@@ -266,12 +270,18 @@ int run_attention(const MlaDecodeParams& q, cudaStream_t s) {
         return launch_attention_check(q, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
     }
     CUtensorMap tkv, tq;
-    int st = make_tmap_blocks(&tkv, q.kv_cache, (uint64_t)q.n_pages, true);
+    const bool tc = (q.flags & MLA_FLAG_TCGEN05) != 0;
+    int st = make_tmap_blocks(&tkv, q.kv_cache, (uint64_t)q.n_pages, true, tc ? kPage : kPage / 2);
     if (st != MLA_OK) return st;
-    if (!(q.flags & MLA_FLAG_TCGEN05))
-        return launch_attention_mma(q, tkv, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    if (!tc) {
+        int sms = 0;
+        st = device_info(&sms);
+        if (st != MLA_OK) return st;
+        return launch_attention_mma(q, tkv, scale_log2, sms, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    }
     const WsLayout ws = ws_layout(q);
-    st = make_tmap_blocks(&tq, reinterpret_cast<const char*>(q.workspace) + ws.qa, (uint64_t)q.batch * kQRows, false);
+    st = make_tmap_blocks(&tq, reinterpret_cast<const char*>(q.workspace) + ws.qa, (uint64_t)q.batch * kQRows, false,
+                          kQRows);
     if (st != MLA_OK) return st;
     return launch_attention_tc(q, tkv, tq, scale_log2, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }

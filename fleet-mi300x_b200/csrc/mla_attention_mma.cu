@@ -1,31 +1,38 @@
 // K2 (default) — split-KV absorbed-MLA attention with exactly 16 heads on the
 // MMA's M dimension: mma.sync m16n8k16 (bf16 in, fp32 accumulate) fed by
-// whole-page TMA tiles.
+// half-page TMA tiles, two independent compute groups per CTA.
 //
 // Why this shape: with 16 heads and one query per request the contractions
 // are [16 x 576] x [576 x tokens] (scores) and [16 x tokens] x [tokens x 512]
 // (output). A 5th-generation (tcgen05) MMA costs the same issue slot whatever
 // its N, so at N = 16 it runs ~16x below its rate and the score contraction
-// alone (36 MMAs per 64-token page) cannot keep up with HBM; m16n8k16 has M =
-// 16 = heads exactly and sustains ~2 cycles per instruction per SM, so a page
-// (544 MMAs, 2.2 MFLOP) costs ~0.6 us against ~1.6 us of HBM time. The
+// alone cannot keep up with HBM; m16n8k16 has M = 16 = heads exactly. The
 // tensor-memory kernel (mla_attention.cu) stays available for comparison.
 //
-// Per CTA (one per SM), 160 threads:
-//   warp 0      TMA producer: one 4-D box per 64-token page (72 KB), landing
-//               as 9 swizzled [64 tokens x 64 columns] blocks, 2-slot ring.
-//   warps 1-4   compute warp w (0..3):
-//     scores    S_w = Q[:, 144w : 144w+144] C[:, 144w : 144w+144]^T for all 64
-//               tokens (9 k-steps x 8 token tiles), Q fragments in registers;
-//     exchange  the 4 partial S through shared memory; warp w sums the 16
-//               tokens [16w, 16w+16) and runs the softmax on them;
-//     softmax   lazy rescale: the running max per head is kept unless a score
-//               exceeds it by more than 2^8 (one barrier-reduction decides),
-//               probabilities rounded to bf16 and shared through shared memory;
-//     output    O_w[16 x 128] += P[16 x 64] C[:, 128w : 128w+128] (4 k-steps x
-//               16 latent tiles), accumulated in registers (rescale = multiply).
-// The split plan and the partial layout are the same as the other K2 kernels
-// (mla_tiles.cuh), so K3 merges any of them.
+// Why two groups: one group's work per tile is a serial chain (scores ->
+// score exchange -> softmax -> output, with group barriers), and with one
+// warp per scheduler a 64-token page took ~1.5 us of it against ~1.6 us of
+// HBM time per page per SM. Two groups of four warps (one warp of each on
+// every scheduler) run independent chains that hide each other's latency.
+// Each group is one CTA of the split-KV plan (vc = CTA + grid * group),
+// with its own 2-slot ring of 32-row half pages (36 KB, one contiguous
+// stretch of the page, one TMA box each), so the plan and the partial layout
+// are those of num_ctas virtual CTAs and K3 is unchanged.
+//
+// Per group (4 warps), per half page:
+//   scores    S_w = Q[:, 144w : 144w+144] C[:, 144w : 144w+144]^T for the 32
+//             tokens (9 k-steps x 4 token tiles), Q fragments in registers;
+//   exchange  the 4 partial S through shared memory; warp w sums the 8 tokens
+//             [8w, 8w+8) and runs the softmax on them;
+//   softmax   lazy rescale: the running max per head is kept unless a score
+//             exceeds it by more than 2^8 (one barrier-reduction decides),
+//             probabilities rounded to bf16 and shared through shared memory;
+//   output    O_w[16 x 128] += P[16 x 32] C[:, 128w : 128w+128] (2 k-steps x
+//             16 latent tiles), accumulated in registers (rescale = multiply).
+// Loads: the group's leader thread issues half page j+2 into the slot of half
+// page j as soon as all four warps have released it (mbarrier, bounded wait).
+// A page whose valid tokens fit in its first half is loaded and computed as
+// that half only.
 #include <cuda.h>
 
 #include "mla_common.cuh"
@@ -36,29 +43,32 @@ namespace mla {
 
 namespace mmak {
 
-constexpr int kThreads = 160;
-constexpr int kWarps = 4;                    // compute warps
-constexpr int kNTile = 2;                    // whole-page ring
-constexpr int kChunkBytes = 8192;
-constexpr int kTileBytes = 9 * kChunkBytes;
-constexpr int kSPitch = 72;                  // floats per head row of a partial-score block (64-bit
-                                             // accesses by a half-warp then hit 32 distinct banks)
-constexpr int kSPartBytes = kWarps * kHeads * kSPitch * 4;   // 17,408
-constexpr int kPBytes = kHeads * 128;        // [16 heads][64 tokens] bf16, 128-byte swizzled rows
+constexpr int kGroups = 2;
+constexpr int kGroupWarps = 4;
+constexpr int kThreads = kGroups * kGroupWarps * 32;  // 256
+constexpr int kHalf = kPage / 2;                      // tokens per half page
+constexpr int kNSlot = 2;                             // half-page ring per group
+constexpr int kChunkBytes = kHalf * 128;              // [32 tokens][64 columns] bf16
+constexpr int kTileBytes = 9 * kChunkBytes;           // 36,864
+constexpr int kSPitch = 40;                           // floats per head row of a partial-score block
+                                                      // (64-bit accesses by a half-warp hit 32 banks)
+constexpr int kSPartBytes = kGroupWarps * kHeads * kSPitch * 4;  // 10,240
+constexpr int kPBytes = kHeads * 64;                  // [16 heads][32 tokens] bf16, 64-byte rows, swizzled
 
-struct Smem {
-    uint64_t tile_full[kNTile], tile_empty[kNTile];
+struct GroupSmem {
+    uint64_t full[kNSlot], empty[kNSlot];
     int abort;
-    float tmax[kWarps][16];
-    float lsum[kWarps][16];
+    float tmax[kGroupWarps][16];
+    float lsum[kGroupWarps][16];
 };
 
-constexpr int kOffTile = 0;
-constexpr int kOffS = kOffTile + kNTile * kTileBytes;
-constexpr int kOffP = kOffS + kSPartBytes;
-constexpr int kOffMisc = kOffP + 2 * kPBytes;
-constexpr int kSmemBytes = kOffMisc + (int)sizeof(Smem) + 1024;
+constexpr int kOffTile = 0;                                      // [group][slot]
+constexpr int kOffS = kOffTile + kGroups * kNSlot * kTileBytes;  // [group]
+constexpr int kOffP = kOffS + kGroups * kSPartBytes;             // [group][2]
+constexpr int kOffMisc = kOffP + kGroups * 2 * kPBytes;          // [group]
+constexpr int kSmemBytes = kOffMisc + kGroups * (int)sizeof(GroupSmem) + 1024;
 static_assert(kSmemBytes <= 232448, "K2 (mma) shared memory exceeds 227 KB");
+static_assert(kTileBytes % 1024 == 0 && kOffS % 1024 == 0, "TMA slots must stay 1024-byte aligned");
 
 // Zero the bf16 halves of a B fragment register whose token index is >= valid.
 __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok_lo, int valid) {
@@ -67,6 +77,11 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int tok_lo, int valid)
     return v;
 }
 
+// Byte offset of (head, 16-byte unit u < 4) in a P block: 64-byte rows whose units
+// are XOR-swizzled with bits 1-2 of the head, so that the 8 rows an ldmatrix
+// reads, and the 8 rows a warp's stores touch, fall in distinct banks.
+__device__ __forceinline__ int p_offset(int head, int u) { return head * 64 + ((u ^ ((head >> 1) & 3)) << 4); }
+
 }  // namespace mmak
 
 __global__ void __launch_bounds__(mmak::kThreads, 1)
@@ -74,10 +89,13 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     using namespace mmak;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Smem& S = *reinterpret_cast<Smem*>(smem + kOffMisc);
-    uint8_t* tile_s = smem + kOffTile;
-    float* spart = reinterpret_cast<float*>(smem + kOffS);
-    uint8_t* p_s = smem + kOffP;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = warp / kGroupWarps, w = warp % kGroupWarps;
+    const int bar_id = 1 + grp;  // named barrier of this group (0 is __syncthreads)
+    GroupSmem& S = *reinterpret_cast<GroupSmem*>(smem + kOffMisc + grp * (int)sizeof(GroupSmem));
+    uint8_t* tile_s = smem + kOffTile + grp * kNSlot * kTileBytes;
+    float* spart = reinterpret_cast<float*>(smem + kOffS + grp * kSPartBytes);
+    uint8_t* p_s = smem + kOffP + grp * 2 * kPBytes;
 
     const WsLayout ws = ws_layout(p);
     char* wsb = reinterpret_cast<char*>(p.workspace);
@@ -90,54 +108,55 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     pdl_wait();  // the plan, absorbed queries and new rows come from K1
     const int64_t U = cum[p.batch];
     const int G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
-    const int c = blockIdx.x;
-    if (c >= G) return;
-    const int64_t u_begin = plan_begin(c, U, G), u_end = plan_begin(c + 1, U, G);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan
+                                                  // has more CTAs than the grid)
+    const bool leader = w == 0 && lane == 0;
 
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kNTile; ++i) { mbar_init(&S.tile_full[i], 1); mbar_init(&S.tile_empty[i], kWarps); }
-        S.abort = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-    volatile int* abort = &S.abort;
-
-    TileCursor cur;
-    cur.init(cum, p.seq_lens, p.batch, u_begin, u_end, new_row_count(p));
-
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            prefetch_tmap(&tmap_kv);
-            uint32_t t = 0;
-            for (; cur.valid(); cur.next(), ++t) {
-                int page = p.block_table[(int64_t)cur.b * p.max_blocks + cur.page_index()];
-                if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
-                const uint32_t slot = t % kNTile, n = t / kNTile;
-                if (n > 0 && !mbar_wait_idle(&S.tile_empty[slot], (n - 1) & 1, abort, p.error_word)) break;
-                mbar_arrive_expect_tx(&S.tile_full[slot], kTileBytes);
-                tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.tile_full[slot], 0, 0, 0, page, kCacheEvictFirst);
-            }
-            for (uint32_t sl = 0; sl < kNTile; ++sl) {
-                const uint32_t fills = t / kNTile + (sl < t % kNTile ? 1u : 0u);
-                if (fills) mbar_drain(&S.tile_full[sl], (fills - 1) & 1, p.error_word);
-            }
+    if (vc < G) {
+        const int64_t u_begin = plan_begin(vc, U, G), u_end = plan_begin(vc + 1, U, G);
+        if (leader) {
+            for (int i = 0; i < kNSlot; ++i) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], kGroupWarps); }
+            S.abort = 0;
+            fence_mbar_init();
         }
-    } else {
-        // ------------------------------------------------------------ compute warps
-        const int w = warp - 1;                // 0..3
+        named_bar_sync(bar_id, kGroupWarps * 32);
+        volatile int* abort = &S.abort;
+
+        // The leader's look-ahead over half pages (loads run two half pages ahead).
+        TileCursor la;
+        int la_half = 0;
+        uint32_t issued = 0;
+        auto issue_next = [&]() {
+            int page = p.block_table[(int64_t)la.b * p.max_blocks + la.page_index()];
+            if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
+            const uint32_t slot = issued % kNSlot;
+            mbar_arrive_expect_tx(&S.full[slot], kTileBytes);
+            tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.full[slot], 0, kHalf * la_half, 0, page,
+                        kCacheEvictFirst);
+            ++issued;
+            if (la_half == 0 && la.tokens() > kHalf) la_half = 1;
+            else { la_half = 0; la.next(); }
+        };
+        if (leader) {
+            prefetch_tmap(&tmap_kv);
+            la.init(cum, p.seq_lens, p.batch, u_begin, u_end, new_row_count(p));
+            while (issued < kNSlot && la.valid()) issue_next();
+        }
+        __syncwarp();  // the leader's warp reconverges before its first .aligned MMA
+
+        TileCursor cur;
+        cur.init(cum, p.seq_lens, p.batch, u_begin, u_end, new_row_count(p));
         const int g = lane >> 2, t4 = lane & 3;
         const int m8 = lane >> 3, r8 = lane & 7;  // ldmatrix: matrix index, row in matrix
-        const int cw_tid = threadIdx.x - 32;
         const uint32_t tile_addr = smem_u32(tile_s), p_addr = smem_u32(p_s);
 
         uint32_t qf[9][4];                     // Q fragments, k-steps [9w, 9w+9)
         float o[16][4];                        // O_w: 16 latent tiles of 8
         float m_run[2], l_run[2];              // heads g, g+8
-        int rows_b = 0;                        // rows attended by the current request (seq_lens[b] + 1)
-        int i = 0;
-        for (; cur.valid(); cur.next(), ++i) {
+        int rows_b = 0;                        // rows attended by the current request
+        uint32_t i = 0;                        // half pages consumed
+        bool ok = true;
+        for (; ok && cur.valid(); cur.next()) {
             const bool first = cur.first(), last = cur.last();
             if (first) rows_b = p.seq_lens[cur.b] + new_row_count(p);
             const int valid = min(kPage, rows_b - cur.page_index() * kPage);
@@ -156,142 +175,147 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 m_run[0] = m_run[1] = -INFINITY;
                 l_run[0] = l_run[1] = 0.f;
             }
-            const uint32_t slot = (uint32_t)i % kNTile;
-            if (!mbar_wait(&S.tile_full[slot], ((uint32_t)i / kNTile) & 1, abort, p.error_word)) break;
-            const uint32_t tbase = tile_addr + slot * kTileBytes;
+            const int halves = valid > kHalf ? 2 : 1;
+            for (int hh = 0; hh < halves; ++hh, ++i) {
+                const int hvalid = min(kHalf, valid - kHalf * hh);  // valid tokens of this half page
+                const bool tile_first = first && hh == 0;
+                const uint32_t slot = i % kNSlot;
+                if (!mbar_wait(&S.full[slot], (i / kNSlot) & 1, abort, p.error_word)) { ok = false; break; }
+                const uint32_t tbase = tile_addr + slot * kTileBytes;
 
-            // ---- partial scores over this warp's 144 columns, all 64 tokens ----
-            float sacc[8][4];
+                // ---- partial scores over this warp's 144 columns, the 32 tokens ----
+                float sacc[4][4];
 #pragma unroll
-            for (int n = 0; n < 8; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+                for (int n = 0; n < 4; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
 #pragma unroll
-            for (int j = 0; j < 9; ++j) {
-                const int k = 144 * w + 16 * j;
-                const int chunk = k >> 6, unit = ((k & 63) >> 3) + (m8 & 1);
+                for (int j = 0; j < 9; ++j) {
+                    const int k = 144 * w + 16 * j;
+                    const int chunk = k >> 6, unit = ((k & 63) >> 3) + (m8 & 1);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {  // token tiles 2q, 2q+1
-                    const int tok = 16 * q + (m8 >> 1) * 8 + r8;
-                    uint32_t b00, b01, b10, b11;
-                    ldsm_x4(tbase + chunk * kChunkBytes + tok * 128 + ((unit ^ r8) << 4), b00, b01, b10, b11);
-                    mma16816(sacc[2 * q], qf[j], b00, b01);
-                    mma16816(sacc[2 * q + 1], qf[j], b10, b11);
-                }
-            }
-            // ---- exchange: every warp publishes its partials, then sums its 16 tokens ----
-            {
-                float* mine = spart + w * (kHeads * kSPitch);
-#pragma unroll
-                for (int n = 0; n < 8; ++n) {
-                    *reinterpret_cast<float2*>(mine + g * kSPitch + 8 * n + 2 * t4) = make_float2(sacc[n][0], sacc[n][1]);
-                    *reinterpret_cast<float2*>(mine + (g + 8) * kSPitch + 8 * n + 2 * t4) =
-                        make_float2(sacc[n][2], sacc[n][3]);
-                }
-            }
-            named_bar_sync(1, 128);
-            float s[2][4];  // token tile n' (tokens 16w + 8n' + 2t4 + {0,1}); [0..1] head g, [2..3] head g+8
-#pragma unroll
-            for (int n = 0; n < 2; ++n) {
-                const int col = 16 * w + 8 * n + 2 * t4;
-                float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int v = 0; v < kWarps; ++v) {
-                    const float* part = spart + v * (kHeads * kSPitch);
-                    const float2 a = *reinterpret_cast<const float2*>(part + g * kSPitch + col);
-                    const float2 b = *reinterpret_cast<const float2*>(part + (g + 8) * kSPitch + col);
-                    lo.x += a.x; lo.y += a.y; hi.x += b.x; hi.y += b.y;
-                }
-                const int tk = col;  // token index of element 0
-                s[n][0] = tk < valid ? lo.x * scale_log2 : -INFINITY;
-                s[n][1] = tk + 1 < valid ? lo.y * scale_log2 : -INFINITY;
-                s[n][2] = tk < valid ? hi.x * scale_log2 : -INFINITY;
-                s[n][3] = tk + 1 < valid ? hi.y * scale_log2 : -INFINITY;
-            }
-            // ---- running max (log2 domain), lazy rescale ----
-            bool exchange = first;
-            if (!first) {
-                const bool ex = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1])) > m_run[0] + 8.f ||
-                                fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3])) > m_run[1] + 8.f;
-                exchange = bar_red_or(1, 128, ex);
-            }
-            if (exchange) {
-                float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-                float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-                if (t4 == 0) { S.tmax[w][g] = mx0; S.tmax[w][g + 8] = mx1; }
-                named_bar_sync(1, 128);
-                const float t0 = fmaxf(fmaxf(S.tmax[0][g], S.tmax[1][g]), fmaxf(S.tmax[2][g], S.tmax[3][g]));
-                const float t1 = fmaxf(fmaxf(S.tmax[0][g + 8], S.tmax[1][g + 8]), fmaxf(S.tmax[2][g + 8], S.tmax[3][g + 8]));
-                const float n0 = fmaxf(m_run[0], t0), n1 = fmaxf(m_run[1], t1);
-                if (!first) {
-                    const float f0 = fast_exp2(m_run[0] - n0), f1 = fast_exp2(m_run[1] - n1);
-#pragma unroll
-                    for (int n = 0; n < 16; ++n) { o[n][0] *= f0; o[n][1] *= f0; o[n][2] *= f1; o[n][3] *= f1; }
-                    l_run[0] *= f0;
-                    l_run[1] *= f1;
-                }
-                m_run[0] = n0;
-                m_run[1] = n1;
-            }
-            // ---- probabilities (bf16) for this warp's 16 tokens -> P buffer ----
-            uint8_t* pb = p_s + (i & 1) * kPBytes;
-#pragma unroll
-            for (int n = 0; n < 2; ++n) {
-                const float e0 = bf16_round(fast_exp2(s[n][0] - m_run[0]));
-                const float e1 = bf16_round(fast_exp2(s[n][1] - m_run[0]));
-                const float e2 = bf16_round(fast_exp2(s[n][2] - m_run[1]));
-                const float e3 = bf16_round(fast_exp2(s[n][3] - m_run[1]));
-                l_run[0] += e0 + e1;
-                l_run[1] += e2 + e3;
-                const int unit = 2 * w + n;  // token / 8
-                *reinterpret_cast<uint32_t*>(pb + g * 128 + ((unit ^ (g & 7)) << 4) + 4 * t4) = pack_bf16(e0, e1);
-                *reinterpret_cast<uint32_t*>(pb + (g + 8) * 128 + ((unit ^ (g & 7)) << 4) + 4 * t4) = pack_bf16(e2, e3);
-            }
-            named_bar_sync(1, 128);
-
-            // ---- O_w += P C[:, 128w : 128w+128] ----
-            const uint32_t pbase = p_addr + (i & 1) * kPBytes;
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                uint32_t a[4];
-                {
-                    const int head = (m8 & 1) * 8 + r8;
-                    const int unit = 2 * ks + (m8 >> 1);
-                    ldsm_x4(pbase + head * 128 + ((unit ^ r8) << 4), a[0], a[1], a[2], a[3]);
-                }
-                const int tok = 16 * ks + (m8 & 1) * 8 + r8;
-#pragma unroll
-                for (int pp = 0; pp < 8; ++pp) {  // latent tiles 2pp, 2pp+1 of this warp
-                    const int chunk = 2 * w + (pp >> 2);
-                    const int unit = 2 * (pp & 3) + (m8 >> 1);
-                    uint32_t b00, b01, b10, b11;
-                    ldsm_x4_t(tbase + chunk * kChunkBytes + tok * 128 + ((unit ^ r8) << 4), b00, b01, b10, b11);
-                    if (valid < kPage) {
-                        const int tl = 16 * ks + 2 * t4;
-                        b00 = mask_pair(b00, tl, valid);
-                        b10 = mask_pair(b10, tl, valid);
-                        b01 = mask_pair(b01, tl + 8, valid);
-                        b11 = mask_pair(b11, tl + 8, valid);
+                    for (int q = 0; q < 2; ++q) {  // token tiles 2q, 2q+1
+                        const int tok = 16 * q + (m8 >> 1) * 8 + r8;
+                        uint32_t b00, b01, b10, b11;
+                        ldsm_x4(tbase + chunk * kChunkBytes + tok * 128 + ((unit ^ r8) << 4), b00, b01, b10, b11);
+                        mma16816(sacc[2 * q], qf[j], b00, b01);
+                        mma16816(sacc[2 * q + 1], qf[j], b10, b11);
                     }
-                    mma16816(o[2 * pp], a, b00, b01);
-                    mma16816(o[2 * pp + 1], a, b10, b11);
                 }
+                // ---- exchange: every warp publishes its partials, then sums its 8 tokens ----
+                {
+                    float* mine = spart + w * (kHeads * kSPitch);
+#pragma unroll
+                    for (int n = 0; n < 4; ++n) {
+                        *reinterpret_cast<float2*>(mine + g * kSPitch + 8 * n + 2 * t4) =
+                            make_float2(sacc[n][0], sacc[n][1]);
+                        *reinterpret_cast<float2*>(mine + (g + 8) * kSPitch + 8 * n + 2 * t4) =
+                            make_float2(sacc[n][2], sacc[n][3]);
+                    }
+                }
+                named_bar_sync(bar_id, kGroupWarps * 32);
+                float s[4];  // tokens 8w + 2t4 + {0,1}: [0..1] head g, [2..3] head g+8
+                {
+                    const int col = 8 * w + 2 * t4;
+                    float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int v = 0; v < kGroupWarps; ++v) {
+                        const float* part = spart + v * (kHeads * kSPitch);
+                        const float2 x0 = *reinterpret_cast<const float2*>(part + g * kSPitch + col);
+                        const float2 x1 = *reinterpret_cast<const float2*>(part + (g + 8) * kSPitch + col);
+                        lo.x += x0.x; lo.y += x0.y; hi.x += x1.x; hi.y += x1.y;
+                    }
+                    s[0] = col < hvalid ? lo.x * scale_log2 : -INFINITY;
+                    s[1] = col + 1 < hvalid ? lo.y * scale_log2 : -INFINITY;
+                    s[2] = col < hvalid ? hi.x * scale_log2 : -INFINITY;
+                    s[3] = col + 1 < hvalid ? hi.y * scale_log2 : -INFINITY;
+                }
+                // ---- running max (log2 domain), lazy rescale ----
+                bool exchange = tile_first;
+                if (!tile_first) {
+                    const bool ex = fmaxf(s[0], s[1]) > m_run[0] + 8.f || fmaxf(s[2], s[3]) > m_run[1] + 8.f;
+                    exchange = bar_red_or(bar_id, kGroupWarps * 32, ex);
+                }
+                if (exchange) {
+                    float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+                    if (t4 == 0) { S.tmax[w][g] = mx0; S.tmax[w][g + 8] = mx1; }
+                    named_bar_sync(bar_id, kGroupWarps * 32);
+                    const float t0 = fmaxf(fmaxf(S.tmax[0][g], S.tmax[1][g]), fmaxf(S.tmax[2][g], S.tmax[3][g]));
+                    const float t1 =
+                        fmaxf(fmaxf(S.tmax[0][g + 8], S.tmax[1][g + 8]), fmaxf(S.tmax[2][g + 8], S.tmax[3][g + 8]));
+                    const float n0 = fmaxf(m_run[0], t0), n1 = fmaxf(m_run[1], t1);
+                    if (!tile_first) {
+                        const float f0 = fast_exp2(m_run[0] - n0), f1 = fast_exp2(m_run[1] - n1);
+#pragma unroll
+                        for (int n = 0; n < 16; ++n) { o[n][0] *= f0; o[n][1] *= f0; o[n][2] *= f1; o[n][3] *= f1; }
+                        l_run[0] *= f0;
+                        l_run[1] *= f1;
+                    }
+                    m_run[0] = n0;
+                    m_run[1] = n1;
+                }
+                // ---- probabilities (bf16) for this warp's 8 tokens -> P buffer ----
+                uint8_t* pb = p_s + (i & 1) * kPBytes;
+                {
+                    const float e0 = bf16_round(fast_exp2(s[0] - m_run[0]));
+                    const float e1 = bf16_round(fast_exp2(s[1] - m_run[0]));
+                    const float e2 = bf16_round(fast_exp2(s[2] - m_run[1]));
+                    const float e3 = bf16_round(fast_exp2(s[3] - m_run[1]));
+                    l_run[0] += e0 + e1;
+                    l_run[1] += e2 + e3;
+                    *reinterpret_cast<uint32_t*>(pb + p_offset(g, w) + 4 * t4) = pack_bf16(e0, e1);
+                    *reinterpret_cast<uint32_t*>(pb + p_offset(g + 8, w) + 4 * t4) = pack_bf16(e2, e3);
+                }
+                named_bar_sync(bar_id, kGroupWarps * 32);
+
+                // ---- O_w += P C[:, 128w : 128w+128] ----
+                const uint32_t pbase = p_addr + (i & 1) * kPBytes;
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks) {
+                    uint32_t a[4];
+                    ldsm_x4(pbase + p_offset((m8 & 1) * 8 + r8, 2 * ks + (m8 >> 1)), a[0], a[1], a[2], a[3]);
+                    const int tok = 16 * ks + (m8 & 1) * 8 + r8;
+#pragma unroll
+                    for (int pp = 0; pp < 8; ++pp) {  // latent tiles 2pp, 2pp+1 of this warp
+                        const int chunk = 2 * w + (pp >> 2);
+                        const int unit = 2 * (pp & 3) + (m8 >> 1);
+                        uint32_t b00, b01, b10, b11;
+                        ldsm_x4_t(tbase + chunk * kChunkBytes + tok * 128 + ((unit ^ r8) << 4), b00, b01, b10, b11);
+                        if (hvalid < kHalf) {
+                            const int tl = 16 * ks + 2 * t4;
+                            b00 = mask_pair(b00, tl, hvalid);
+                            b10 = mask_pair(b10, tl, hvalid);
+                            b01 = mask_pair(b01, tl + 8, hvalid);
+                            b11 = mask_pair(b11, tl + 8, hvalid);
+                        }
+                        mma16816(o[2 * pp], a, b00, b01);
+                        mma16816(o[2 * pp + 1], a, b10, b11);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.empty[slot]);
+                // the leader refills this slot with the half page two ahead once all four warps released it
+                bool refill_ok = true;
+                if (leader && la.valid()) {
+                    refill_ok = mbar_wait_idle(&S.empty[slot], (i / kNSlot) & 1, abort, p.error_word);
+                    if (refill_ok) issue_next();
+                }
+                if (!__shfl_sync(0xffffffffu, refill_ok, 0)) { ok = false; break; }  // reconverges the warp
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.tile_empty[slot]);
+            if (!ok) break;
 
             if (last) {
-                // ---- partial of (request, this CTA): m, l, unnormalised O ----
+                // ---- partial of (request, this virtual CTA): m, l, unnormalised O ----
                 float l0 = l_run[0], l1 = l_run[1];
                 l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
                 l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
                 l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
                 l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
                 if (t4 == 0) { S.lsum[w][g] = l0; S.lsum[w][g + 8] = l1; }
-                named_bar_sync(1, 128);
-                const int64_t slot_idx = (int64_t)c + cur.b;
+                named_bar_sync(bar_id, kGroupWarps * 32);
+                const int64_t slot_idx = (int64_t)vc + cur.b;
                 if (w == 0 && t4 == 0) {
                     const float L0 = (S.lsum[0][g] + S.lsum[1][g]) + (S.lsum[2][g] + S.lsum[3][g]);
                     const float L1 = (S.lsum[0][g + 8] + S.lsum[1][g + 8]) + (S.lsum[2][g + 8] + S.lsum[3][g + 8]);
@@ -307,10 +331,16 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                     *reinterpret_cast<float2*>(acc + (g + 8) * kLora + 8 * n) = make_float2(o[n][2], o[n][3]);
                 }
                 // the lsum buffer is reused by the next segment's epilogue only after
-                // at least one more tile's barriers, which every warp passes after this read
+                // at least one more half page's barriers, which every warp passes after this read
             }
         }
-        (void)cw_tid;
+        // Drain: every copy the leader issued must land before the CTA's shared memory is released.
+        if (leader) {
+            for (uint32_t sl = 0; sl < kNSlot; ++sl) {
+                const uint32_t fills = issued / kNSlot + (sl < issued % kNSlot ? 1u : 0u);
+                if (fills) mbar_drain(&S.full[sl], (fills - 1) & 1, p.error_word);
+            }
+        }
     }
     __syncthreads();
 }
@@ -322,8 +352,12 @@ cudaError_t k2_mma_configure() {
 }
 
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
-                                 cudaStream_t stream) {
-    const cudaError_t e = launch_pdl(k2_attention_mma, dim3(p.num_ctas), dim3(mmak::kThreads), mmak::kSmemBytes,
+                                 int sm_count, cudaStream_t stream) {
+    // Plan CTAs are warp groups: up to one CTA per SM with one group each, then a second group
+    // in the same CTAs; beyond two per SM, CTAs of two groups each.
+    const int paired = (p.num_ctas + mmak::kGroups - 1) / mmak::kGroups;
+    const int grid = p.num_ctas <= sm_count ? p.num_ctas : (paired > sm_count ? paired : sm_count);
+    const cudaError_t e = launch_pdl(k2_attention_mma, dim3(grid), dim3(mmak::kThreads), mmak::kSmemBytes,
                                      stream, p, tmap_kv, scale_log2);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
