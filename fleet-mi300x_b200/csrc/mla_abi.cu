@@ -26,6 +26,7 @@ cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tm
 cudaError_t k2_configure();
 cudaError_t k2_mma_configure();
 cudaError_t k3_configure();
+int k3_w_rows(int batch);
 cudaError_t k0_configure();
 cudaError_t launch_rows_to_pages(const MlaRowsToPages& r, int sm_count, cudaStream_t stream);
 cudaError_t launch_o_proj(const MlaDecodeParams& p, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
@@ -101,16 +102,17 @@ int make_tmap_blocks(CUtensorMap* m, const void* base, uint64_t rows_or_pages, b
     return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
 }
 
-// kv_b (16*256 rows x 512 bf16) as 128-row blocks of W_UK / W_UV: dims {64
-// columns, 4096 rows (1024 B), 8 column blocks (128 B)}, box {64, 128, blocks}
-// = one request of blocks x 16 KB landing as [blocks][128 rows][128 B] with the
-// 128-byte swizzle (8 blocks: a whole 128 x 512 head block; 2: a quarter of it).
-int make_tmap_kvb(CUtensorMap* m, const void* kv_b, int blocks) {
+// kv_b (16*256 rows x 512 bf16) as row blocks of W_UK / W_UV: dims {64 columns,
+// 4096 rows (1024 B), 8 column blocks (128 B)}, box {64, box_rows, blocks} = one
+// request of box_rows x blocks x 128 B landing as [blocks][box_rows rows][128 B]
+// with the 128-byte swizzle (128 x 8: a whole 128 x 512 head block for the plain
+// merge; 32 x 8: a cluster CTA's rows of W_UV; 128 x 2: a quarter of W_UK's columns).
+int make_tmap_kvb(CUtensorMap* m, const void* kv_b, int box_rows, int blocks) {
     PFN_cuTensorMapEncodeTiled_v12000 fn;
     if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
     cuuint64_t dims[3] = {64, (cuuint64_t)kHeads * kKvbHead, 8};
     cuuint64_t strides[2] = {(cuuint64_t)kLora * 2, 128};
-    cuuint32_t box[3] = {64, 128, (cuuint32_t)blocks};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)blocks};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(kv_b), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -172,14 +174,14 @@ int run_o_proj(const MlaDecodeParams& q, cudaStream_t s) {
 
 int run_prologue(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap t;
-    const int st = make_tmap_kvb(&t, q.kv_b, kK1WukBlocks);
+    const int st = make_tmap_kvb(&t, q.kv_b, 128, kK1WukBlocks);
     if (st != MLA_OK) return st;
     return launch_prologue(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 int run_merge(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap t;
-    const int st = make_tmap_kvb(&t, q.kv_b, 8);
+    const int st = make_tmap_kvb(&t, q.kv_b, k3_w_rows(q.batch), 8);
     if (st != MLA_OK) return st;
     return launch_merge_uv(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }

@@ -24,10 +24,53 @@ namespace k3 {
 constexpr int kReq = 16;
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kWBytes = kV * kLora * 2;          // 131072: [8 column blocks][128 rows][128 B], swizzled
 constexpr int kABytes = kReq * kLora * 2;        // 16384: [16 requests][512] bf16, 1024-byte rows, swizzled
-constexpr int kSmemBytes = kWBytes + 2 * kABytes + 64 + kWarps * kLora * 4 + 1024;
+constexpr int kRedBytes = kWarps * kLora * 4;     // 16384: one fp32 o_c row per warp (warp-group combine)
+
+// kCl CTAs (a thread-block cluster when > 1) share one (head, block of 16
+// requests): each folds every kCl-th partial, and owns kV / kCl rows of W_UV.
+template <int kCl>
+struct Shape {
+    static constexpr int kVRows = kV / kCl;                   // W_UV rows (v) of this CTA
+    static constexpr int kWBytes = kVRows * kLora * 2;         // [8 column blocks][kVRows rows][128 B], swizzled
+    static constexpr int kXBytes = kCl > 1 ? kReq * (kLora + 4) * 4 : 0;  // cluster exchange: per request
+                                                                         // acc[512], m, L (fp32)
+    static constexpr int kSmemBytes = kWBytes + 2 * kABytes + kRedBytes + kXBytes + 64 + 1024;
+};
+constexpr int kClusterCtas = 4;  // cluster form: CTAs per (head, request block)
 }  // namespace k3
+
+// The cluster form runs when the batch has at most 4 blocks of 16 requests, where
+// the plain form would leave most SMs idle.
+inline bool k3_use_cluster(int batch) { return (batch + k3::kReq - 1) / k3::kReq <= 4; }
+
+// Thread-block cluster primitives (sm_90+): this CTA's rank, a cluster-wide
+// barrier with release/acquire ordering of shared memory, and loads from a
+// peer CTA's shared memory.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float2 dsmem_ld2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+    return v;
+}
 
 // Partial slot s = (c + b) * heads + h: its (m, L) pair and the lane's four
 // float4 of acc (latent l = 4 lane + 128 k, k < 4).
@@ -56,7 +99,9 @@ __device__ __forceinline__ void fold_partial(float2 ml, const float4 (&a)[4], fl
 }
 
 // Fold of the partials c = first, first + stride, ... <= last of (request b,
-// head h), in order. Loads are issued four partials at a time.
+// head h), in order. Loads are issued kDepth partials (kDepth x 2 KB per warp)
+// at a time. (Eight at a time measured no faster than four.)
+template <int kDepth = 4>
 __device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
                                                int b, int h, int first, int last, int stride, int lane, float& m,
                                                float& L, float4 (&acc)[4]) {
@@ -64,14 +109,14 @@ __device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml
     L = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int cc = first; cc <= last; cc += 4 * stride) {
-        float2 ml[4];
-        float4 a[4][4];
+    for (int cc = first; cc <= last; cc += kDepth * stride) {
+        float2 ml[kDepth];
+        float4 a[kDepth][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < kDepth; ++j)
             if (cc + j * stride <= last) load_partial(part_ml, part_acc, b, h, cc + j * stride, lane, ml[j], a[j]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < kDepth; ++j)
             if (cc + j * stride <= last) fold_partial(ml[j], a[j], m, L, acc);
     }
 }
@@ -82,15 +127,19 @@ __device__ __forceinline__ uint32_t swz1024(uint32_t base, int row, int col) {
     return base + row * 1024 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2;
 }
 
+template <int kCl>
 __global__ void __launch_bounds__(k3::kThreads, 1)
     k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb) {
     using namespace k3;
+    using Sh = Shape<kCl>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* w_s = smem;
-    uint8_t* a_hi = smem + kWBytes;
+    uint8_t* a_hi = smem + Sh::kWBytes;
     uint8_t* a_lo = a_hi + kABytes;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(a_lo + kABytes);
+    float* red_acc = reinterpret_cast<float*>(a_lo + kABytes);           // [kWarps][512]
+    float* xch = reinterpret_cast<float*>(a_lo + kABytes + kRedBytes);     // [16][512 + 4]: acc, m, L
+    uint64_t* bar = reinterpret_cast<uint64_t*>(a_lo + kABytes + kRedBytes + Sh::kXBytes);
 
     const WsLayout ws = ws_layout(p);
     const char* wsb = reinterpret_cast<const char*>(p.workspace);
@@ -99,15 +148,16 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     const float* part_acc = reinterpret_cast<const float*>(wsb + ws.part_acc);
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 
-    const int h = blockIdx.x;
+    const int q = kCl > 1 ? (int)cluster_rank() : 0;  // rank within the (head, request block) cluster
+    const int h = blockIdx.x / kCl;
     const int b0 = blockIdx.y * kReq;
     const int nreq = min(kReq, p.batch - b0);
 
     if (threadIdx.x == 0) {  // W_UV is a weight: no kernel writes it, so it may load before pdl_wait
         mbar_init(bar, 1);
         fence_mbar_init();
-        mbar_arrive_expect_tx(bar, kWBytes);
-        tma_load_3d(w_s, &tmap_kvb, bar, 0, h * kKvbHead + kNope, 0, kCacheEvictLast);
+        mbar_arrive_expect_tx(bar, Sh::kWBytes);
+        tma_load_3d(w_s, &tmap_kvb, bar, 0, h * kKvbHead + kNope + q * Sh::kVRows, 0, kCacheEvictLast);
     }
     pdl_trigger();
     pdl_wait();  // partials from K2, plan from K1
@@ -115,11 +165,17 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     const int G = (int)(U < 1 ? 1 : (U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas));
 
     // ---- merge: o_c[r][l] = sum_c w_c acc_c[l] / sum_c w_c l_c ----
-    // Every fold visits partials in CTA order; requests without tiles (invalid
+    // Every fold visits partials in plan-CTA order; requests without tiles (invalid
     // position) get a zero o_c.
     __shared__ int32_t cum_s[kReq + 1];
     __shared__ float red_ml[kWarps][2];
     if (threadIdx.x <= kReq) cum_s[threadIdx.x] = cum[min(b0 + (int)threadIdx.x, p.batch)];
+    for (int i = threadIdx.x; i < (kReq - nreq) * (kLora / 8); i += kThreads) {  // rows past nreq: zero operands
+        const int r = nreq + i / (kLora / 8), col = (i % (kLora / 8)) * 8;
+        const uint32_t ahi0 = smem_u32(a_hi), alo0 = smem_u32(a_lo);
+        *reinterpret_cast<uint4*>(a_hi + (swz1024(ahi0, r, col) - ahi0)) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(a_lo + (swz1024(alo0, r, col) - alo0)) = make_uint4(0u, 0u, 0u, 0u);
+    }
     __syncthreads();
     const uint32_t ahi = smem_u32(a_hi), alo = smem_u32(a_lo);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -144,41 +200,46 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         }
     };
     auto store_ml = [&](int r, float m, float L) {
-        if (p.shard_out && r < nreq && lane == 0) {
+        if (p.shard_out && r < nreq && lane == 0 && q == 0) {
             float* so = p.shard_out + ((int64_t)(b0 + r) * kHeads + h) * MLA_SHARD_STRIDE;
             so[kV] = m;
             so[kV + 1] = L;
         }
     };
+    // this CTA's fold of request r: finished here (kCl = 1), or published for the cluster
+    auto publish = [&](int r, float m, float L, const float4 (&acc)[4]) {
+        if (kCl == 1) {
+            store_ml(r, m, L);
+            store_oc(r, acc, L > 0.f ? 1.f / L : 0.f);
+        } else {
+            float* x = xch + r * (kLora + 4);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) *reinterpret_cast<float4*>(x + 4 * lane + 128 * k) = acc[k];
+            if (lane == 0) { x[kLora] = m; x[kLora + 1] = L; }
+        }
+    };
 
     // Warps per request: the largest power of two <= 8 / nreq (8 for one request,
-    // 1 for 5 or more). A group of wpr warps folds request r's partials c0 + wi,
-    // c0 + wi + wpr, ... (wi = warp within the group), then the group's warp
-    // results are combined through shared memory in warp order.
-    for (int i = threadIdx.x; i < (kReq - nreq) * (kLora / 8); i += kThreads) {  // rows past nreq: zero operands
-        const int r = nreq + i / (kLora / 8), col = (i % (kLora / 8)) * 8;
-        *reinterpret_cast<uint4*>(a_hi + (swz1024(ahi, r, col) - ahi)) = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(a_lo + (swz1024(alo, r, col) - alo)) = make_uint4(0u, 0u, 0u, 0u);
-    }
+    // 1 for 5 or more). A group of wpr warps of cluster rank q folds request r's
+    // partials c0 + q + kCl wi, c0 + q + kCl (wi + wpr), ... (wi = warp within the
+    // group), then the group's warp results are combined through shared memory in
+    // warp order.
     const int wpr = nreq == 1 ? 8 : nreq == 2 ? 4 : nreq <= 4 ? 2 : 1;
     const int groups = kWarps / wpr, gi = warp / wpr, wi = warp % wpr;
     const int iters = (nreq + groups - 1) / groups;
-    float* red_acc = reinterpret_cast<float*>(bar + 2);  // [kWarps][512] f32, 16-B aligned after the barrier
 #pragma unroll 1
     for (int it = 0; it < iters; ++it) {  // uniform trip count: the barriers below are CTA-wide
         const int r = gi + it * groups;
         int c0 = 0, c1 = -1;
         float4 acc[4];
         float m = -INFINITY, L = 0.f;
-        if (part_range(r, c0, c1) && c0 + wi <= c1)
-            merge_partials(part_ml, part_acc, b0 + r, h, c0 + wi, c1, wpr, lane, m, L, acc);
+        const int first = q + kCl * wi;
+        if (part_range(r, c0, c1) && c0 + first <= c1)
+            merge_partials(part_ml, part_acc, b0 + r, h, c0 + first, c1, kCl * wpr, lane, m, L, acc);
         else
             for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (wpr == 1) {
-            if (r < nreq) {
-                store_ml(r, m, L);
-                store_oc(r, acc, L > 0.f ? 1.f / L : 0.f);
-            }
+            if (r < nreq) publish(r, m, L, acc);
             continue;
         }
         if (lane == 0) { red_ml[warp][0] = m; red_ml[warp][1] = L; }
@@ -189,7 +250,8 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         if (wi == 0 && r < nreq) {
             const int w0 = warp;
             float gm = -INFINITY;
-            for (int v = 0; v < wpr; ++v) gm = fmaxf(gm, red_ml[w0 + v][0]);
+            for (int v = 0; v < wpr; ++v)
+                if (red_ml[w0 + v][1] > 0.f) gm = fmaxf(gm, red_ml[w0 + v][0]);
             float Lt = 0.f;
             float4 tot[4];
 #pragma unroll
@@ -204,10 +266,49 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
                     tot[k].z = fmaf(wv, x.z, tot[k].z); tot[k].w = fmaf(wv, x.w, tot[k].w);
                 }
             }
+            publish(r, gm, Lt, tot);
+        }
+        __syncthreads();
+    }
+
+    if (kCl > 1) {
+        // The cluster's kCl folds of each request, combined in rank order: every CTA
+        // reads all ranks' (acc, m, L) from distributed shared memory, so each holds the
+        // whole o_c for its slice of W_UV. Warp w combines requests w and w + 8.
+        cluster_sync_all();  // every rank has published
+        const uint32_t xbase = smem_u32(xch);
+#pragma unroll 1
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = warp + kWarps * rr;
+            if (r >= nreq) continue;
+            const uint32_t off = (uint32_t)(r * (kLora + 4)) * 4u;
+            float2 ml[kCl];
+            float gm = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kCl; ++c) {
+                ml[c] = dsmem_ld2(dsmem_addr(xbase + off + kLora * 4u, (uint32_t)c));
+                if (ml[c].y > 0.f) gm = fmaxf(gm, ml[c].x);
+            }
+            float Lt = 0.f;
+            float4 tot[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tot[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int c = 0; c < kCl; ++c) {
+                const float wv = ml[c].y > 0.f ? exp2f(ml[c].x - gm) : 0.f;
+                Lt = fmaf(wv, ml[c].y, Lt);
+                const uint32_t src = dsmem_addr(xbase + off, (uint32_t)c);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 x = dsmem_ld4(src + (uint32_t)(4 * lane + 128 * k) * 4u);
+                    tot[k].x = fmaf(wv, x.x, tot[k].x); tot[k].y = fmaf(wv, x.y, tot[k].y);
+                    tot[k].z = fmaf(wv, x.z, tot[k].z); tot[k].w = fmaf(wv, x.w, tot[k].w);
+                }
+            }
             store_ml(r, gm, Lt);
             store_oc(r, tot, Lt > 0.f ? 1.f / Lt : 0.f);
         }
-        __syncthreads();
+        cluster_sync_all();  // no rank reuses or releases its exchange buffer while others read it
     }
     __syncthreads();
     {
@@ -215,7 +316,9 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         if (!mbar_wait(bar, 0, &dummy, p.error_word)) return;
     }
 
-    // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l]; warp w owns v in [16w, 16w+16) ----
+    // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] for this CTA's kVRows rows of v;
+    // warp w owns v in [16w, 16w+16) ----
+    if (warp * 16 >= Sh::kVRows) return;
     const int g = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;
     const uint32_t wb = smem_u32(w_s);
     float acc[2][4];
@@ -233,17 +336,18 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
             const int v = 16 * warp + (m8 >> 1) * 8 + r8;
             const int l = 16 * ks + (m8 & 1) * 8;
             uint32_t b00, b01, b10, b11;
-            ldsm_x4(wb + (l >> 6) * (kV * 128) + v * 128 + ((((l & 63) >> 3) ^ r8) << 4), b00, b01, b10, b11);
+            ldsm_x4(wb + (l >> 6) * (Sh::kVRows * 128) + v * 128 + ((((l & 63) >> 3) ^ r8) << 4), b00, b01, b10, b11);
             mma16816(acc[0], ah, b00, b01);
             mma16816(acc[0], al, b00, b01);
             mma16816(acc[1], ah, b10, b11);
             mma16816(acc[1], al, b10, b11);
         }
     }
+    const int v_base = q * Sh::kVRows;
     if (p.shard_out) {  // sequence-sharded step: fp32 y = W_UV o_c / L of this shard
 #pragma unroll
         for (int n = 0; n < 2; ++n) {
-            const int v = 16 * warp + 8 * n + 2 * t4;
+            const int v = v_base + 16 * warp + 8 * n + 2 * t4;
             if (g < nreq)
                 *reinterpret_cast<float2*>(p.shard_out + ((int64_t)(b0 + g) * kHeads + h) * MLA_SHARD_STRIDE + v) =
                     make_float2(acc[n][0], acc[n][1]);
@@ -255,7 +359,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     }
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
-        const int v = 16 * warp + 8 * n + 2 * t4;
+        const int v = v_base + 16 * warp + 8 * n + 2 * t4;
         if (g < nreq)
             *reinterpret_cast<uint32_t*>(out + (int64_t)(b0 + g) * p.out_stride + h * kV + v) =
                 pack_bf16(acc[n][0], acc[n][1]);
@@ -306,12 +410,40 @@ cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, v
 }
 
 cudaError_t k3_configure() {
-    return cudaFuncSetAttribute(k3_merge_uv, cudaFuncAttributeMaxDynamicSharedMemorySize, k3::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(k3_merge_uv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         k3::Shape<1>::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k3_merge_uv<k3::kClusterCtas>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                k3::Shape<k3::kClusterCtas>::kSmemBytes);
 }
 
+// Rows of W_UV per CTA of the launch chosen by launch_merge_uv (its TMA box height).
+int k3_w_rows(int batch) { return k3_use_cluster(batch) ? k3::Shape<k3::kClusterCtas>::kVRows : kV; }
+
 cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream) {
-    dim3 grid(kHeads, (p.batch + k3::kReq - 1) / k3::kReq);
-    return launch_pdl(k3_merge_uv, grid, dim3(k3::kThreads), k3::kSmemBytes, stream, p, tmap_kvb);
+    const int blocks = (p.batch + k3::kReq - 1) / k3::kReq;
+    if (!k3_use_cluster(p.batch))
+        return launch_pdl(k3_merge_uv<1>, dim3(kHeads, blocks), dim3(k3::kThreads), k3::Shape<1>::kSmemBytes, stream,
+                          p, tmap_kvb);
+    // few request blocks: a cluster of kClusterCtas CTAs per (head, block), so that a
+    // long run of partials (one long sequence split over every plan CTA) is folded by
+    // kClusterCtas SMs and combined through distributed shared memory
+    constexpr int kCl = k3::kClusterCtas;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kHeads * kCl, blocks);
+    cfg.blockDim = dim3(k3::kThreads);
+    cfg.dynamicSmemBytes = k3::Shape<kCl>::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kCl;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl>, p, tmap_kvb);
 }
 
 }  // namespace mla
