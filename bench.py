@@ -448,8 +448,11 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
 
 def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torch.device, dist) -> None:
     """Config 5b across `world` GPUs: one 131,072-token sequence split by page-aligned KV
-    ranges; per step K1+K2+K3 on each range, one NCCL all-gather of the 8.4 KB partials
-    and the fixed-order combine (distributed.py). Total work is fixed: strong scaling."""
+    ranges; per step K1+K2+K3 on each range and the fixed-order combine of the 8.4 KB
+    partials (distributed.py). --exchange peer (default): K3 stores the partials into
+    every rank's exchange buffer over NVLink and K4 combines, one library call per
+    step; --exchange nccl: an NCCL all-gather and mla_combine_shards. Total work is
+    fixed: strong scaling."""
     dmod = importlib.import_module("fleet-mi300x_b200.distributed")
     wl = workloads.WORKLOADS["config5b"]
     T = wl.seq_lens()[0]
@@ -471,8 +474,12 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
     parts = torch.empty(world, 1, 16, native.SHARD_STRIDE, dtype=torch.float32, device=dev)
     out = torch.empty(1, 2048, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
+    ex = dmod.ExchangeBuffers.create(rank, world, max_batch=1) if args.exchange == "peer" else None
 
     def step():
+        if ex is not None:
+            runner.attend(q, kv_a, cache, out, rope_pos=pos, new_row=last, exchange=ex)
+            return
         runner.attend(q, kv_a, cache, rope_pos=pos, shard_out=local, new_row=last)
         dist.all_gather_into_tensor(parts, local)
         fleet.combine_shards(parts, out)
@@ -493,7 +500,38 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     runner.check_errors()
+
+    # ---- stage timings (each stage repeated alone on every rank at once; max over
+    # ranks). A K3 repeated without its K4 rewrites the same slot and flags, which the
+    # next whole step's K4 then reads, so the exchange protocol stays in step.
+    def stage(name):
+        if name == "combine" and ex is None:
+            return lambda: fleet.combine_shards(parts, out)
+        if name == "all_gather":
+            return lambda: dist.all_gather_into_tensor(parts, local)
+        if name == "k1_k2_k3":
+            return lambda: [runner.attend(q, kv_a, cache, out if ex is not None else None, st, rope_pos=pos,
+                                          shard_out=None if ex is not None else local, new_row=last, exchange=ex)
+                            for st in ("prologue", "attention", "merge")]
+        return lambda: runner.attend(q, kv_a, cache, out if ex is not None else None, name, rope_pos=pos,
+                                     shard_out=None if ex is not None else local, new_row=last, exchange=ex)
+    names = ["prologue", "attention", "merge", "k1_k2_k3"] + ([] if ex is not None else ["all_gather", "combine"])
+    stage_ms = []
+    for name in names:
+        dist.barrier()
+        torch.cuda.synchronize()
+        stage_ms.append(timer(stage(name), max(5, args.steps // 2)))
+    step()  # a whole step last: the peer protocol's step counter advances again
+    torch.cuda.synchronize()
+    runner.check_errors()
+    t = torch.tensor(stage_ms, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    stages_us = {n: round(float(v) * 1e3, 2) for n, v in zip(names, t.tolist())}
     peak, _ = measured_peak()
+    torch.cuda.synchronize()
+    dist.barrier()
+    if ex is not None:
+        ex.close()
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
@@ -504,13 +542,19 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
         "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents, N(0,0.02) weights)",
         "config": {"workload": "config5b", "batch": 1, "context": T, "page_size": 64,
-                   "parallelism": f"sequence-sharded x{world}: page-aligned KV ranges, NCCL all-gather of "
-                                  f"{16 * native.SHARD_STRIDE * 4} B partials per GPU, fixed-order combine",
+                   "parallelism": (f"sequence-sharded x{world}: page-aligned KV ranges, " +
+                                   (f"peer exchange of {16 * native.SHARD_STRIDE * 4} B partials per GPU (K3 stores "
+                                    "into every rank's buffer over NVLink, K4 waits on flags and combines; no NCCL "
+                                    "in the step)" if ex is not None else
+                                    f"NCCL all-gather of {16 * native.SHARD_STRIDE * 4} B partials per GPU, "
+                                    "fixed-order combine")),
                    "kv_bytes_per_step": kv_b, "kv_bytes_per_gpu": kv_b // world,
                    "l2": timer.describe()},
         "us_per_layer_step": round(ms_max * 1e3, 3),
         "kv_frac_of_hbm_peak_per_gpu": round(value / world / peak, 4),
         "gpu_launches": (native.load_library().mla_launches_per_step() + 1) * args.steps,
+        "exchange": args.exchange,
+        "stages_us": stages_us,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -562,6 +606,8 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="config5b on N > 1 GPUs: how the shard partials move (peer memory or NCCL)")
     ap.add_argument("--sweep-splits", type=lambda v: [int(x) for x in v.split(",")], default=None,
                     help="comma-separated CTA counts of the split plan, e.g. 1,2,4,8,16,32,64,148; "
                          "prints a sweep line instead of the bench line (one GPU)")

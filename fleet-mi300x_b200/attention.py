@@ -95,10 +95,12 @@ class MlaDecodeAttention:
                out: torch.Tensor | None, *, rope_pos: torch.Tensor | None = None,
                shard_out: torch.Tensor | None = None, new_row: bool = True,
                x_n: torch.Tensor | None = None, residual: torch.Tensor | None = None,
-               h_out: torch.Tensor | None = None) -> native.MlaDecodeParams:
+               h_out: torch.Tensor | None = None, exchange=None) -> native.MlaDecodeParams:
         """The C-ABI params of one step. With `x_n` (and q = kv_a = None) the library
         projects q | kv_a itself with the fused [W_q; W_kv_a] weight (K0); with
-        `residual` and `h_out` it ends with h_out = R(residual + R(W_o R(out))) (K5)."""
+        `residual` and `h_out` it ends with h_out = R(residual + R(W_o R(out))) (K5);
+        with `exchange` (distributed.ExchangeBuffers) the step is one shard of a
+        sequence-sharded step and ends with the peer exchange and combine (K4)."""
         B = (x_n if x_n is not None else q).shape[0]
         p = native.new_params()
         p.softmax_scale = self.cfg.softmax_scale
@@ -125,6 +127,8 @@ class MlaDecodeAttention:
         p.flags = self.flags | (0 if new_row else native.FLAG_NO_NEW_ROW)
         p.rope_pos = _ptr(rope_pos)
         p.shard_out = _ptr(shard_out)
+        if exchange is not None:
+            exchange.apply(p)
         if h_out is not None:
             if self.w_o is None:
                 raise ValueError("o_proj + residual needs LayerWeights.o_proj")
@@ -153,15 +157,23 @@ class MlaDecodeAttention:
     # ------------------------------------------------------------------ calls
     def attend(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
                out: torch.Tensor | None = None, stage: str = "all", *, rope_pos: torch.Tensor | None = None,
-               shard_out: torch.Tensor | None = None, new_row: bool = True) -> torch.Tensor:
+               shard_out: torch.Tensor | None = None, new_row: bool = True, exchange=None) -> torch.Tensor:
         """K1+K2+K3 from q [B, 3072] and kv_a [B, 576] (bf16 views allowed).
         Appends each request's row at seq_lens[b]; does not advance seq_lens.
 
         Sequence-sharded use: `rope_pos` gives the new token's global position,
-        `new_row=False` marks a shard that does not own the new token, and
+        `new_row=False` marks a shard that does not own the new token, and either
         `shard_out` (f32 [B, 16, 132]) receives this shard's partial instead of
-        R(out); combine the gathered partials with `combine_shards`."""
+        R(out), to be gathered and combined with `combine_shards`, or `exchange`
+        (this rank's distributed.ExchangeBuffers) moves the partials between the
+        ranks' GPUs inside the step, which then returns the combined R(out) (stage
+        "combine" runs K4 alone)."""
         self._check_inputs(q, kv_a, cache)
+        if exchange is not None:
+            if shard_out is not None:
+                raise ValueError("shard_out and exchange are exclusive")
+            if q.shape[0] > exchange.max_batch:
+                raise ValueError(f"batch {q.shape[0]} exceeds the exchange buffers' {exchange.max_batch}")
         if shard_out is not None:
             if shard_out.dtype != torch.float32 or tuple(shard_out.shape) != (q.shape[0], 16, native.SHARD_STRIDE):
                 raise ValueError(f"shard_out must be f32 [{q.shape[0]}, 16, {native.SHARD_STRIDE}]")
@@ -172,14 +184,17 @@ class MlaDecodeAttention:
         key = (q.data_ptr(), _row_stride(q), kv_a.data_ptr(), _row_stride(kv_a), cache.pages.data_ptr(),
                cache.block_table.data_ptr(), cache.seq_lens.data_ptr(), cache.n_pages, cache.max_blocks,
                q.shape[0], _ptr(out), None if out is None else _row_stride(out), _ptr(rope_pos), _ptr(shard_out),
-               new_row, self.flags, self.num_ctas, self.cos.data_ptr(), self.cos.shape[0], self.kv_b.data_ptr())
+               new_row, self.flags, self.num_ctas, self.cos.data_ptr(), self.cos.shape[0], self.kv_b.data_ptr(),
+               None if exchange is None else exchange.key)
         p = self._step_p
         if key != self._step_key or self._ws is None or p.workspace != self._ws.data_ptr():
-            p = self.params(q, kv_a, cache, out, rope_pos=rope_pos, shard_out=shard_out, new_row=new_row)
+            p = self.params(q, kv_a, cache, out, rope_pos=rope_pos, shard_out=shard_out, new_row=new_row,
+                            exchange=exchange)
             self._step_key, self._step_p = key, p
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         fn = {"all": self.lib.mla_decode_step, "prologue": self.lib.mla_prologue,
-              "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv}[stage]
+              "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv,
+              "combine": self.lib.mla_exchange_combine}[stage]
         native.check(fn(ctypes.byref(p), stream), f"mla {stage}", p)
         return out if shard_out is None else shard_out
 

@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "mla_common.cuh"
@@ -21,6 +22,7 @@ cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kv
 cudaError_t k1_configure();
 cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,
                                   cudaStream_t stream);
+cudaError_t launch_exchange_combine(const MlaDecodeParams& p, cudaStream_t stream);
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
                                  int sm_count, cudaStream_t stream);
 cudaError_t k2_configure();
@@ -235,6 +237,16 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         if (!aligned(p->x_n, 16) || (p->x_stride & 7) || !aligned(p->w_qkv, 16)) return MLA_E_MISALIGNED;
     }
     if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW)) return MLA_E_INVALID_ARG;
+    if (p->world < 0 || p->world > MLA_MAX_RANKS) return MLA_E_INVALID_ARG;
+    if (p->world > 0) {  // peer exchange: K3 writes every rank's buffer, K4 combines into out
+        if (p->rank < 0 || p->rank >= p->world || p->shard_out || !p->out || p->exchange_timeout_us < 0)
+            return MLA_E_INVALID_ARG;
+        if (p->exchange_batch < p->batch) return MLA_E_LIMIT;
+        for (int r = 0; r < p->world; ++r) {
+            if (!p->exchange[r]) return MLA_E_INVALID_ARG;
+            if (!aligned(p->exchange[r], 256)) return MLA_E_MISALIGNED;
+        }
+    }
     if (p->max_blocks <= 0 || p->n_pages <= 0 || p->max_pos <= 0) return MLA_E_INVALID_ARG;
     if ((int64_t)p->n_pages * MLA_PAGE_SIZE > INT32_MAX || (int64_t)p->batch * p->max_blocks > INT32_MAX)
         return MLA_E_LIMIT;
@@ -264,6 +276,10 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         out->kv_a_stride = kQkvRows;
     }
     return MLA_OK;
+}
+
+int run_exchange_combine(const MlaDecodeParams& q, cudaStream_t s) {
+    return launch_exchange_combine(q, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 int run_attention(const MlaDecodeParams& q, cudaStream_t s) {
@@ -318,6 +334,7 @@ const char* mla_device_error_string(int code) {
         case MLA_DEV_BAD_PAGE: return "block_table entry outside [0, n_pages)";
         case MLA_DEV_BAD_POSITION: return "seq_lens entry outside the rope table or block table";
         case MLA_DEV_TIMEOUT: return "on-chip pipeline wait timed out";
+        case MLA_DEV_PEER_TIMEOUT: return "shard exchange: a peer's flag did not arrive in time";
         default: return "unknown device error";
     }
 }
@@ -437,6 +454,14 @@ int mla_merge_uv(const MlaDecodeParams* p, void* stream) {
     return run_merge(q, (cudaStream_t)stream);
 }
 
+int mla_exchange_combine(const MlaDecodeParams* p, void* stream) {
+    MlaDecodeParams q;
+    int st = prepare(p, &q);
+    if (st != MLA_OK) return st;
+    if (q.world <= 0) return MLA_E_INVALID_ARG;
+    return run_exchange_combine(q, (cudaStream_t)stream);
+}
+
 int mla_decode_step(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;
     int st = prepare(p, &q);
@@ -451,8 +476,66 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream) {
     st = run_attention(q, s);
     if (st != MLA_OK) return st;
     st = run_merge(q, s);
-    if (st != MLA_OK || !q.w_o) return st;
-    return run_o_proj(q, s);
+    if (st != MLA_OK) return st;
+    if (q.world > 0) {
+        st = run_exchange_combine(q, s);
+        if (st != MLA_OK) return st;
+    }
+    return q.w_o ? run_o_proj(q, s) : MLA_OK;
+}
+
+int mla_exchange_bytes(int32_t world, int32_t max_batch, uint64_t* bytes) {
+    if (!bytes || world <= 0 || max_batch <= 0) return MLA_E_INVALID_ARG;
+    if (world > MLA_MAX_RANKS || max_batch > MLA_MAX_BATCH) return MLA_E_LIMIT;
+    *bytes = ex_layout(world, max_batch).total;
+    return MLA_OK;
+}
+
+int mla_exchange_alloc(uint64_t bytes, void** buf, void* ipc_handle) {
+    if (!buf || bytes == 0) return MLA_E_INVALID_ARG;
+    *buf = nullptr;
+    const int st = device_info(nullptr);
+    if (st != MLA_OK) return st;
+    void* ptr = nullptr;
+    if (cudaMalloc(&ptr, bytes) != cudaSuccess) return MLA_E_LAUNCH;
+    if (cudaMemset(ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(ptr);
+        return MLA_E_LAUNCH;
+    }
+    if (ipc_handle) {
+        cudaIpcMemHandle_t h;
+        static_assert(sizeof(h) == MLA_IPC_HANDLE_BYTES, "IPC handle size");
+        if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) {
+            cudaFree(ptr);
+            return MLA_E_LAUNCH;
+        }
+        memcpy(ipc_handle, &h, sizeof(h));
+    }
+    *buf = ptr;
+    return MLA_OK;
+}
+
+int mla_exchange_free(void* buf) {
+    if (!buf) return MLA_E_INVALID_ARG;
+    return cudaFree(buf) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+int mla_exchange_open(const void* ipc_handle, void** buf) {
+    if (!ipc_handle || !buf) return MLA_E_INVALID_ARG;
+    *buf = nullptr;
+    const int st = device_info(nullptr);
+    if (st != MLA_OK) return st;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return MLA_E_LAUNCH;
+    *buf = ptr;
+    return MLA_OK;
+}
+
+int mla_exchange_close(void* buf) {
+    if (!buf) return MLA_E_INVALID_ARG;
+    return cudaIpcCloseMemHandle(buf) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 }  // extern "C"

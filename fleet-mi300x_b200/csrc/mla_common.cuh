@@ -64,6 +64,7 @@ __host__ __device__ inline WsLayout ws_layout(const MlaDecodeParams& p) {
     return ws_layout(p.batch, p.num_ctas, p.x_n != nullptr);
 }
 
+
 // Programmatic dependent launch. A kernel launched with launch_pdl may start
 // while the kernel before it on the stream is still running; pdl_wait() returns
 // once that kernel has completed and its writes are visible, so it must come
@@ -187,6 +188,75 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// ---------------------------------------------------------------------------
+// Exchange buffer of the peer-memory shard exchange (MlaDecodeParams.world > 0),
+// one per rank, written by every rank's K3 and read by this rank's K4:
+//   ctl    u32   [2]        steps completed by this rank's K4, K4 blocks done
+//   lines  u64x2 [2][world][max_batch][16][kExLines]
+//          the shard partial of (source rank, request, head) at parity = step & 1:
+//          line j < 64 holds y[2j], y[2j+1]; line 64 holds m, L. Each 8-byte half of
+//          a line is (step << 32) | f32 bits, stored and loaded as one 64-bit access,
+//          so a reader that sees this step's number in a half also sees its value;
+//          no flag or fence orders the data (the low-latency line format NCCL uses).
+// ---------------------------------------------------------------------------
+constexpr int kMaxRanks = MLA_MAX_RANKS;
+constexpr int kK3ClusterCtas = 4;   // K3 cluster form: CTAs per (head, block of 16 requests)
+constexpr int kExLines = kV / 2 + 1;  // 65 lines of 16 bytes per (source, request, head)
+
+struct ExLayout {
+    uint64_t ctl, lines, total;
+};
+
+__host__ __device__ inline ExLayout ex_layout(int world, int max_batch) {
+    ExLayout e;
+    uint64_t off = 0;
+    e.ctl = off;   off = align256(off + 8);
+    e.lines = off; off = align256(off + 2ull * world * max_batch * kHeads * kExLines * 16);
+    e.total = off;
+    return e;
+}
+
+// p.exchange[r] without a dynamically indexed parameter array (which would copy
+// the whole parameter block to local memory).
+__device__ __forceinline__ char* ex_buf(const MlaDecodeParams& p, int r) {
+    char* b = nullptr;
+#pragma unroll
+    for (int d = 0; d < kMaxRanks; ++d)
+        if (d == r) b = reinterpret_cast<char*>(p.exchange[d]);
+    return b;
+}
+
+// First line of (source src, request b, head h) at parity par in an exchange buffer.
+__device__ __forceinline__ ulonglong2* ex_lines(char* buf, const ExLayout& ex, int world, int max_batch,
+                                                uint32_t par, int src, int b, int h) {
+    return reinterpret_cast<ulonglong2*>(buf + ex.lines) +
+           ((((int64_t)par * world + src) * max_batch + b) * kHeads + h) * kExLines;
+}
+
+// One line: two f32 values, each tagged with the step number in its 64-bit half.
+__device__ __forceinline__ void st_line(ulonglong2* line, float a, float b, uint32_t step) {
+    const unsigned long long x = ((unsigned long long)step << 32) | __float_as_uint(a);
+    const unsigned long long y = ((unsigned long long)step << 32) | __float_as_uint(b);
+    asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(line), "l"(x), "l"(y) : "memory");
+}
+
+// Poll a line until both halves carry `step` (true, values in a, b) or until
+// limit_ns have passed since t0 (false).
+__device__ __forceinline__ bool poll_line(const ulonglong2* line, uint32_t step, float& a, float& b, uint64_t t0,
+                                          uint64_t limit_ns) {
+    for (uint32_t k = 1;; ++k) {
+        unsigned long long x, y;
+        asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(line) : "memory");
+        if ((uint32_t)(x >> 32) == step && (uint32_t)(y >> 32) == step) {
+            a = __uint_as_float((uint32_t)x);
+            b = __uint_as_float((uint32_t)y);
+            return true;
+        }
+        if ((k & 31) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+        __nanosleep(32);
+    }
 }
 
 // A wait on one phase of an mbarrier that gives up after `kWaitLimitNs` or

@@ -37,12 +37,12 @@ struct Shape {
                                                                          // acc[512], m, L (fp32)
     static constexpr int kSmemBytes = kWBytes + 2 * kABytes + kRedBytes + kXBytes + 64 + 1024;
 };
-constexpr int kClusterCtas = 4;  // cluster form: CTAs per (head, request block)
+constexpr int kClusterCtas = kK3ClusterCtas;  // cluster form: CTAs per (head, request block)
 }  // namespace k3
 
 // The cluster form runs when the batch has at most 4 blocks of 16 requests, where
 // the plain form would leave most SMs idle.
-inline bool k3_use_cluster(int batch) { return (batch + k3::kReq - 1) / k3::kReq <= 4; }
+__host__ __device__ inline bool k3_use_cluster(int batch) { return (batch + k3::kReq - 1) / k3::kReq <= 4; }
 
 // Thread-block cluster primitives (sm_90+): this CTA's rank, a cluster-wide
 // barrier with release/acquire ordering of shared memory, and loads from a
@@ -128,6 +128,12 @@ __device__ __forceinline__ uint32_t swz1024(uint32_t base, int row, int col) {
 }
 
 template <int kCl>
+__device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const uint8_t* w_s, uint32_t ahi,
+                                               uint32_t alo, int warp, int lane, int q, int h, int b0, int nreq,
+                                               bool xmode, const ExLayout& ex, uint32_t step,
+                                               __nv_bfloat16* __restrict__ out);
+
+template <int kCl>
 __global__ void __launch_bounds__(k3::kThreads, 1)
     k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb) {
     using namespace k3;
@@ -163,6 +169,15 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     pdl_wait();  // partials from K2, plan from K1
     const int64_t U = cum[p.batch];
     const int G = (int)(U < 1 ? 1 : (U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas));
+
+    // Peer exchange (p.world > 0): this step's number = steps completed + 1. The
+    // counter was last written by the previous step's K4, which completed before
+    // this kernel's pdl_wait returned.
+    const bool xmode = p.world > 0;
+    const ExLayout ex = ex_layout(p.world, p.exchange_batch);
+    __shared__ uint32_t step_s;
+    if (xmode && threadIdx.x == 0)
+        step_s = __ldcg(reinterpret_cast<const uint32_t*>(ex_buf(p, p.rank) + ex.ctl)) + 1;
 
     // ---- merge: o_c[r][l] = sum_c w_c acc_c[l] / sum_c w_c l_c ----
     // Every fold visits partials in plan-CTA order; requests without tiles (invalid
@@ -200,7 +215,15 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         }
     };
     auto store_ml = [&](int r, float m, float L) {
-        if (p.shard_out && r < nreq && lane == 0 && q == 0) {
+        if (r >= nreq || lane != 0 || q != 0) return;
+        if (xmode) {  // into slot p.rank of every rank's exchange buffer
+#pragma unroll
+            for (int d = 0; d < kMaxRanks; ++d) {
+                if (d >= p.world) break;
+                st_line(ex_lines(ex_buf(p, d), ex, p.world, p.exchange_batch, step_s & 1u, p.rank, b0 + r, h) + kV / 2,
+                        m, L, step_s);
+            }
+        } else if (p.shard_out) {
             float* so = p.shard_out + ((int64_t)(b0 + r) * kHeads + h) * MLA_SHARD_STRIDE;
             so[kV] = m;
             so[kV + 1] = L;
@@ -319,6 +342,18 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] for this CTA's kVRows rows of v;
     // warp w owns v in [16w, 16w+16) ----
     if (warp * 16 >= Sh::kVRows) return;
+    k3_uv_epilogue<kCl>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, xmode, ex, xmode ? step_s : 0u, out);
+}
+
+// The W_UV MMA and the epilogue of one K3 warp (its 16 rows of v): R(out) in
+// bf16, or the fp32 shard partial y (into shard_out, or in exchange mode into
+// slot p.rank of every rank's exchange buffer).
+template <int kCl>
+__device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const uint8_t* w_s, uint32_t ahi,
+                                               uint32_t alo, int warp, int lane, int q, int h, int b0, int nreq,
+                                               bool xmode, const ExLayout& ex, uint32_t step,
+                                               __nv_bfloat16* __restrict__ out) {
+    using Sh = k3::Shape<kCl>;
     const int g = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;
     const uint32_t wb = smem_u32(w_s);
     float acc[2][4];
@@ -344,6 +379,24 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         }
     }
     const int v_base = q * Sh::kVRows;
+    if (xmode) {  // fp32 y = W_UV o_c / L of this shard, to every rank
+#pragma unroll
+        for (int d = 0; d < kMaxRanks; ++d) {
+            if (d >= p.world) break;
+            char* buf = ex_buf(p, d);
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+                const int v = v_base + 16 * warp + 8 * n + 2 * t4;
+                if (g < nreq)
+                    st_line(ex_lines(buf, ex, p.world, p.exchange_batch, step & 1u, p.rank, b0 + g, h) + v / 2,
+                            acc[n][0], acc[n][1], step);
+                if (g + 8 < nreq)
+                    st_line(ex_lines(buf, ex, p.world, p.exchange_batch, step & 1u, p.rank, b0 + g + 8, h) + v / 2,
+                            acc[n][2], acc[n][3], step);
+            }
+        }
+        return;
+    }
     if (p.shard_out) {  // sequence-sharded step: fp32 y = W_UV o_c / L of this shard
 #pragma unroll
         for (int n = 0; n < 2; ++n) {
@@ -369,37 +422,129 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     }
 }
 
-// Cross-shard combine of a sequence-sharded step (parts gathered from all GPUs):
-// out[b][128h + v] = bf16( sum_r w_r y_r[v] / sum_r w_r ), w_r = L_r 2^(m_r - max m),
-// shards folded in order. Block = request, thread = (head, 8 values of v).
-__global__ void __launch_bounds__(256) k4_combine_shards(const float* __restrict__ parts, int n_shards, int batch,
-                                                         __nv_bfloat16* __restrict__ out, int64_t out_stride) {
-    const int b = blockIdx.x;
-    const int h = threadIdx.x >> 4, v0 = (threadIdx.x & 15) * 8;
-    const int64_t shard_stride = (int64_t)batch * kHeads * MLA_SHARD_STRIDE;
-    const float* base = parts + ((int64_t)b * kHeads + h) * MLA_SHARD_STRIDE;
+// Cross-shard combine of one (request, head): out[128h + v] = bf16( sum_r w_r y_r[v] /
+// sum_r w_r ), w_r = L_r 2^(m_r - max m), shards r = 0, 1, ... folded in order from
+// base + r * shard_stride. kPeerData: the partials were written by other GPUs during
+// this kernel's lifetime, so they are read from L2 (ld.global.cg), not through L1.
+template <bool kPeerData>
+__device__ __forceinline__ void combine_head(const float* __restrict__ base, int64_t shard_stride, int n_shards,
+                                             int v0, __nv_bfloat16* __restrict__ o) {
+    auto ld1 = [](const float* a) -> float { return kPeerData ? __ldcg(a) : *a; };
+    auto ld4 = [](const float* a) -> float4 {
+        return kPeerData ? __ldcg(reinterpret_cast<const float4*>(a)) : *reinterpret_cast<const float4*>(a);
+    };
     float gm = -INFINITY;
-    for (int r = 0; r < n_shards; ++r) gm = fmaxf(gm, base[r * shard_stride + kV]);
+    for (int r = 0; r < n_shards; ++r) gm = fmaxf(gm, ld1(base + r * shard_stride + kV));
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float W = 0.f;
     for (int r = 0; r < n_shards; ++r) {
         const float* pr = base + r * shard_stride;
-        const float Lr = pr[kV + 1];
+        const float Lr = ld1(pr + kV + 1);
         if (!(Lr > 0.f)) continue;  // an empty shard contributes nothing
-        const float w = Lr * exp2f(pr[kV] - gm);
+        const float w = Lr * exp2f(ld1(pr + kV) - gm);
         W += w;
-        const float4 y0 = *reinterpret_cast<const float4*>(pr + v0);
-        const float4 y1 = *reinterpret_cast<const float4*>(pr + v0 + 4);
+        const float4 y0 = ld4(pr + v0);
+        const float4 y1 = ld4(pr + v0 + 4);
         acc[0] = fmaf(w, y0.x, acc[0]); acc[1] = fmaf(w, y0.y, acc[1]);
         acc[2] = fmaf(w, y0.z, acc[2]); acc[3] = fmaf(w, y0.w, acc[3]);
         acc[4] = fmaf(w, y1.x, acc[4]); acc[5] = fmaf(w, y1.y, acc[5]);
         acc[6] = fmaf(w, y1.z, acc[6]); acc[7] = fmaf(w, y1.w, acc[7]);
     }
     const float inv = W > 0.f ? 1.f / W : 0.f;
-    __nv_bfloat16* o = out + (int64_t)b * out_stride + h * kV + v0;
 #pragma unroll
     for (int k = 0; k < 8; k += 2)
         *reinterpret_cast<uint32_t*>(o + k) = pack_bf16(acc[k] * inv, acc[k + 1] * inv);
+}
+
+// Cross-shard combine of a sequence-sharded step whose partials were gathered by
+// the caller (parts [n_shards][batch][16][132]). Block = request, thread = (head,
+// 8 values of v).
+__global__ void __launch_bounds__(256) k4_combine_shards(const float* __restrict__ parts, int n_shards, int batch,
+                                                         __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+    const int b = blockIdx.x;
+    const int h = threadIdx.x >> 4, v0 = (threadIdx.x & 15) * 8;
+    combine_head<false>(parts + ((int64_t)b * kHeads + h) * MLA_SHARD_STRIDE,
+                        (int64_t)batch * kHeads * MLA_SHARD_STRIDE, n_shards, v0,
+                        out + (int64_t)b * out_stride + h * kV + v0);
+}
+
+// K4 of the peer exchange: the combine of combine_head, over the shard partials
+// every rank's K3 stored into this rank's exchange buffer as step-tagged lines.
+// Block = request, thread = (head, 8 values of v). Each thread polls the lines it
+// needs until they carry this step's number (bounded by exchange_timeout_us; on
+// timeout the block records MLA_DEV_PEER_TIMEOUT and writes zeros). The last block
+// to finish advances the buffer's step counter.
+__global__ void __launch_bounds__(256) k4_exchange_combine(const MlaDecodeParams p) {
+    const int b = blockIdx.x;
+    const int h = threadIdx.x >> 4, v0 = (threadIdx.x & 15) * 8;
+    pdl_trigger();
+    pdl_wait();  // this rank's K3 has completed (and read the step counter)
+    const ExLayout ex = ex_layout(p.world, p.exchange_batch);
+    char* own = ex_buf(p, p.rank);
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(own + ex.ctl);
+    __shared__ uint32_t step_s;
+    __shared__ int fail_s;
+    if (threadIdx.x == 0) {
+        step_s = __ldcg(ctl) + 1;
+        fail_s = 0;
+    }
+    __syncthreads();
+    const uint32_t step = step_s;
+    const uint64_t limit_ns = (uint64_t)(p.exchange_timeout_us > 0 ? p.exchange_timeout_us : 2000000) * 1000ull;
+    const uint64_t t0 = globaltimer_ns();
+    bool ok = true;
+    float m[kMaxRanks], L[kMaxRanks];
+    float gm = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+        m[r] = -INFINITY;
+        L[r] = 0.f;
+        if (r < p.world && ok) {
+            const ulonglong2* ln = ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h);
+            ok = poll_line(ln + kV / 2, step, m[r], L[r], t0, limit_ns);
+            gm = fmaxf(gm, m[r]);
+        }
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float W = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+        if (r >= p.world || !ok) continue;
+        if (!(L[r] > 0.f)) continue;  // an empty shard contributes nothing
+        const ulonglong2* ln = ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h) + v0 / 2;
+        float y[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (ok) ok = poll_line(ln + k, step, y[2 * k], y[2 * k + 1], t0, limit_ns);
+        if (!ok) continue;
+        const float w = L[r] * exp2f(m[r] - gm);
+        W += w;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = fmaf(w, y[k], acc[k]);
+    }
+    if (!ok) {
+        record_error(p.error_word, MLA_DEV_PEER_TIMEOUT);
+        fail_s = 1;
+    }
+    __syncthreads();
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.out_stride + h * kV + v0;
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k += 2)
+        *reinterpret_cast<uint32_t*>(o + k) = fail_s ? 0u : pack_bf16(acc[k] * inv, acc[k + 1] * inv);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(ctl + 1, 1u) == gridDim.x - 1) {  // every block has read the counter
+            ctl[1] = 0;
+            __threadfence();
+            atomicExch(ctl, step);
+        }
+    }
+}
+
+cudaError_t launch_exchange_combine(const MlaDecodeParams& p, cudaStream_t stream) {
+    return launch_pdl(k4_exchange_combine, dim3(p.batch), dim3(256), 0, stream, p);
 }
 
 cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,

@@ -13,7 +13,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libmla_decode.so"
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 HEADS, QK_NOPE, QK_ROPE, V_HEAD, KV_LORA, PAGE_SIZE = 16, 128, 64, 128, 512, 64
 ROW = KV_LORA + QK_ROPE
 MAX_BATCH = 65536
@@ -24,19 +24,27 @@ FLAG_NO_NEW_ROW = 0x8
 SHARD_STRIDE = 132
 MAX_PROJECT_BATCH = 64  # MLA_MAX_PROJECT_BATCH: batch limit of the in-library q|kv_a projection
 STATIC_SCRATCH_BYTES = 32 << 20  # MLA_STATIC_SCRATCH_BYTES, the workspace of mla_decode_step_static
+MAX_RANKS = 8              # MLA_MAX_RANKS: shards of a step with the peer exchange
+IPC_HANDLE_BYTES = 64      # MLA_IPC_HANDLE_BYTES
 
 STATUS = {
     0: "MLA_OK", -1: "MLA_E_INVALID_ARG", -2: "MLA_E_UNSUPPORTED_DIMS", -3: "MLA_E_MISALIGNED",
     -4: "MLA_E_WORKSPACE", -5: "MLA_E_ARCH", -6: "MLA_E_LAUNCH", -7: "MLA_E_DRIVER", -8: "MLA_E_LIMIT",
 }
-DEV_ERRORS = {0: "ok", 1: "MLA_DEV_BAD_PAGE", 2: "MLA_DEV_BAD_POSITION", 3: "MLA_DEV_TIMEOUT"}
+DEV_ERRORS = {0: "ok", 1: "MLA_DEV_BAD_PAGE", 2: "MLA_DEV_BAD_POSITION", 3: "MLA_DEV_TIMEOUT",
+              4: "MLA_DEV_PEER_TIMEOUT"}
 
 EXPORTED = (
     "mla_abi_version", "mla_status_string", "mla_device_error_string", "mla_params_init",
     "mla_workspace_size", "mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv",
     "mla_plan_info", "mla_launches_per_step", "mla_combine_shards", "mla_decode_step_static", "mla_project",
-    "mla_rows_init", "mla_rows_to_pages", "mla_o_proj",
+    "mla_rows_init", "mla_rows_to_pages", "mla_o_proj", "mla_exchange_bytes", "mla_exchange_alloc",
+    "mla_exchange_free", "mla_exchange_open", "mla_exchange_close", "mla_exchange_combine",
 )
+
+
+def _field_str(v) -> str:
+    return str(list(v)) if isinstance(v, ctypes.Array) else str(v)
 
 
 class MlaError(RuntimeError):
@@ -46,7 +54,7 @@ class MlaError(RuntimeError):
         self.code = code
         msg = f"{what}: {STATUS.get(code, DEV_ERRORS.get(code, code))} ({code})"
         if params is not None:
-            fields = ", ".join(f"{n}={getattr(params, n)}" for n, _ in params._fields_)
+            fields = ", ".join(f"{n}={_field_str(getattr(params, n))}" for n, _ in params._fields_)
             msg += f" [params: {fields}]"
         super().__init__(msg)
 
@@ -75,6 +83,8 @@ class MlaDecodeParams(ctypes.Structure):
         ("x_n", ctypes.c_void_p), ("x_stride", ctypes.c_int64), ("w_qkv", ctypes.c_void_p),
         ("w_o", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("residual_stride", ctypes.c_int64),
         ("h_out", ctypes.c_void_p), ("h_out_stride", ctypes.c_int64),
+        ("exchange", ctypes.c_void_p * MAX_RANKS), ("rank", ctypes.c_int32), ("world", ctypes.c_int32),
+        ("exchange_batch", ctypes.c_int32), ("exchange_timeout_us", ctypes.c_int32),
     ]
 
 
@@ -134,8 +144,17 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.mla_rows_init.argtypes = [R]
         lib.mla_rows_to_pages.restype = ctypes.c_int
         lib.mla_rows_to_pages.argtypes = [R, ctypes.c_void_p]
+        lib.mla_exchange_bytes.restype = ctypes.c_int
+        lib.mla_exchange_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64)]
+        lib.mla_exchange_alloc.restype = ctypes.c_int
+        lib.mla_exchange_alloc.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+        lib.mla_exchange_open.restype = ctypes.c_int
+        lib.mla_exchange_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        for fn in ("mla_exchange_free", "mla_exchange_close"):
+            getattr(lib, fn).restype = ctypes.c_int
+            getattr(lib, fn).argtypes = [ctypes.c_void_p]
         for fn in ("mla_decode_step", "mla_prologue", "mla_attention", "mla_merge_uv", "mla_decode_step_static",
-                   "mla_project", "mla_o_proj"):
+                   "mla_project", "mla_o_proj", "mla_exchange_combine"):
             f = getattr(lib, fn)
             f.restype = ctypes.c_int
             f.argtypes = [P, ctypes.c_void_p]

@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define MLA_ABI_VERSION 4
+#define MLA_ABI_VERSION 5
 
 /* Fixed model dimensions. The reference's launcher refuses any other shape
  * (src/host/fleet_launch.hip:573-577: kv_lora != 512 or qk_rope != 64);
@@ -61,6 +61,8 @@ extern "C" {
 #define MLA_HIDDEN 2048                                     /* model width: x_n rows */
 #define MLA_QKV_ROWS (MLA_HEADS * (MLA_QK_NOPE + MLA_QK_ROPE) + MLA_ROW)  /* 3648: [W_q; W_kv_a] */
 #define MLA_MAX_PROJECT_BATCH 64                            /* batch limit of the in-library projection */
+#define MLA_MAX_RANKS 8                                     /* shards of a step with the peer exchange */
+#define MLA_IPC_HANDLE_BYTES 64                             /* size of an exchange buffer's IPC handle */
 
 /* Host-side status codes (return values). The reference's launcher dies with
  * a message on bad shapes (fleet_launch.hip:573-577) and returns hipError_t
@@ -85,6 +87,8 @@ typedef enum {
 #define MLA_DEV_BAD_PAGE 1      /* block_table entry outside [0, n_pages) */
 #define MLA_DEV_BAD_POSITION 2  /* seq_lens[b] >= max_pos or >= max_blocks * 64, or < 0 */
 #define MLA_DEV_TIMEOUT 3       /* a bounded on-chip wait gave up (pipeline stall) */
+#define MLA_DEV_PEER_TIMEOUT 4  /* the exchange combine gave up waiting for a shard's flag
+                                   (a peer that did not run its step within exchange_timeout_us) */
 
 /* Flags. */
 #define MLA_FLAG_CHECK_KERNEL 0x2 /* run the CUDA-core split-KV kernel instead of the tensor-core one
@@ -154,6 +158,23 @@ typedef struct MlaDecodeParams {
     int64_t residual_stride;  /* elements between rows, a multiple of 4, >= MLA_HIDDEN */
     void* h_out;              /* [batch][h_out_stride] bf16: the new hidden state; may be `residual` itself */
     int64_t h_out_stride;     /* elements between rows, a multiple of 4, >= MLA_HIDDEN */
+
+    /* Sequence-sharded step with the shard exchange over peer memory (ABI v5).
+     * world > 0 turns it on. K3 then stores this shard's partial (y, m, L as in
+     * shard_out) into slot `rank` of every rank's exchange buffer, with plain stores
+     * over NVLink to the peers' memory, each value tagged with the step number in
+     * the same 64-bit store; a last kernel (K4) waits until the values of all
+     * `world` shards carry this step, bounded by exchange_timeout_us, and combines
+     * them in rank order into `out` with the arithmetic of mla_combine_shards. No
+     * flag, fence or collective library call is on the path.
+     * shard_out must be NULL; w_o (K5) may follow. Every rank must run the same
+     * sequence of steps with the same batch. world = 0: no exchange. */
+    void* exchange[MLA_MAX_RANKS]; /* every rank's exchange buffer as mapped in this process
+                                      (mla_exchange_alloc / mla_exchange_open); [rank] is this rank's own */
+    int32_t rank;                  /* this shard's index in sequence order, 0..world-1 */
+    int32_t world;                 /* number of shards: 0 (no exchange) or 1..MLA_MAX_RANKS */
+    int32_t exchange_batch;        /* the batch the buffers were sized for; batch <= exchange_batch */
+    int32_t exchange_timeout_us;   /* K4's limit on waiting for a shard; 0 = 2,000,000 (2 s) */
 } MlaDecodeParams;
 
 #define MLA_SHARD_STRIDE (MLA_V_HEAD + 4)
@@ -214,6 +235,27 @@ int mla_launches_per_step(void);
 int mla_combine_shards(const float* parts, int32_t n_shards, int32_t batch, void* out, int64_t out_stride,
                        void* stream);
 
+/* Exchange buffers of the peer-memory shard exchange (MlaDecodeParams.world > 0).
+ * One buffer per rank, allocated by that rank's process on its GPU, zeroed, and
+ * mapped into every other rank's process through its CUDA IPC handle; all ranks
+ * must use the same world and max_batch. Layout: a step counter and two parities
+ * (step & 1) of [world][max_batch][16 heads][65] 16-byte lines; line j < 64 holds
+ * y[2j], y[2j+1] and line 64 holds m, L, each as (step << 32) | f32 bits in 64 bits.
+ * The reference runs on one GPU and has no counterpart; the exchange replaces an
+ * all-gather of the shard partials over a collective library. */
+int mla_exchange_bytes(int32_t world, int32_t max_batch, uint64_t* bytes);
+/* cudaMalloc + zero on the current device; ipc_handle (MLA_IPC_HANDLE_BYTES, may be
+ * NULL) receives the handle that other processes pass to mla_exchange_open. */
+int mla_exchange_alloc(uint64_t bytes, void** buf, void* ipc_handle);
+int mla_exchange_free(void* buf);
+/* Map another process's exchange buffer (peer access enabled lazily). */
+int mla_exchange_open(const void* ipc_handle, void** buf);
+int mla_exchange_close(void* buf);
+/* K4 alone: wait for every shard's flags and combine (needs p->world > 0). In
+ * exchange mode mla_merge_uv (K3) must be followed by this call before the next
+ * step; mla_decode_step runs both. */
+int mla_exchange_combine(const MlaDecodeParams* p, void* stream);
+
 /* Prefill hand-off: rows of a prefill into the paged cache. Replaces the
  * reference's flat per-layer cache [max_pos][576] bf16, built from the hooked
  * kv_a_proj_with_mqa output by src/host/kv_convert.py:36-139 and uploaded as-is
@@ -252,8 +294,8 @@ void mla_rows_init(MlaRowsToPages* r);
 int mla_rows_to_pages(const MlaRowsToPages* r, void* stream);
 
 /* Size of the workspace that mla_decode_step_static keeps inside the library, per
- * device: 32 MiB, which holds mla_workspace_size() for up to 558 requests at 148
- * CTAs (one per SM of a B200). */
+ * device: 32 MiB, which holds mla_workspace_size() for up to 463 requests at the
+ * default 296 split-KV CTAs of a B200 (558 at num_ctas = 148). */
 #define MLA_STATIC_SCRATCH_BYTES (32ull << 20)
 
 /* No counterpart in the reference: its launcher allocates every buffer itself

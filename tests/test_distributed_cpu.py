@@ -114,3 +114,72 @@ def test_gloo_two_ranks_sequence_sharded():
     for rank, rel, cs, _ in res:
         assert rel <= 1e-2 and cs >= 0.99999, (rank, rel, cs)
     assert res[0][3] == res[1][3], "every rank must hold the same combined output"
+
+
+# ---------------------------------------------------------------- peer exchange (host side)
+native = importlib.import_module("fleet-mi300x_b200.native")
+
+
+def _align256(x):
+    return (x + 255) // 256 * 256
+
+
+@pytest.mark.parametrize("world,max_batch", [(1, 1), (2, 1), (8, 1), (3, 70), (8, 256), (2, 16), (2, 17)])
+def test_exchange_buffer_size(world, max_batch):
+    """mla_exchange_bytes (host arithmetic, no GPU): the step counter and two parities of
+    [world][max_batch][16 heads][65] step-tagged 16-byte lines (64 lines of y pairs and
+    one of m, L), each region 256-byte aligned."""
+    want = 256 + _align256(2 * world * max_batch * 16 * 65 * 16)
+    assert dist_mod.exchange_bytes(world, max_batch) == want
+
+
+def test_exchange_buffer_size_refused():
+    import ctypes
+    lib = native.load_library()
+    n = ctypes.c_uint64()
+    assert lib.mla_exchange_bytes(0, 1, ctypes.byref(n)) == -1
+    assert lib.mla_exchange_bytes(native.MAX_RANKS + 1, 1, ctypes.byref(n)) == -8
+    assert lib.mla_exchange_bytes(2, 0, ctypes.byref(n)) == -1
+
+
+def test_exchange_views_fill_params():
+    ex = dist_mod.ExchangeBuffers([0x1000, 0x2000, 0x3000], 1, 3, 5, timeout_us=777)
+    p = native.new_params()
+    ex.apply(p)
+    assert list(p.exchange)[:3] == [0x1000, 0x2000, 0x3000]
+    assert all(v is None for v in list(p.exchange)[3:])
+    assert (p.rank, p.world, p.exchange_batch, p.exchange_timeout_us) == (1, 3, 5, 777)
+    with pytest.raises(ValueError):
+        dist_mod.ExchangeBuffers([0] * 9, 0, 9, 1)
+    with pytest.raises(ValueError):
+        dist_mod.ExchangeBuffers([0, 0], 2, 2, 1)
+
+
+def _handle_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        got = dist_mod.gather_handles(bytes([rank + 1]) * native.IPC_HANDLE_BYTES, world)
+        q.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_ranks_gather_ipc_handles():
+    """The handle exchange of ExchangeBuffers.create: every rank ends with every
+    rank's handle in rank order."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world = 3
+    port = _free_port()
+    procs = [ctx.Process(target=_handle_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = [bytes([r + 1]) * native.IPC_HANDLE_BYTES for r in range(world)]
+    for rank, got in res:
+        assert got == want, rank
