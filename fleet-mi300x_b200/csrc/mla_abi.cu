@@ -18,7 +18,8 @@ cudaError_t launch_prologue(const MlaDecodeParams& p, const CUtensorMap& tmap_kv
 cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, const CUtensorMap& tmap_q,
                                 float scale_log2, cudaStream_t stream);
 cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream);
-cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream);
+cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, int sm_count,
+                            cudaStream_t stream);
 cudaError_t k1_configure();
 cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,
                                   cudaStream_t stream);
@@ -183,9 +184,12 @@ int run_prologue(const MlaDecodeParams& q, cudaStream_t s) {
 
 int run_merge(const MlaDecodeParams& q, cudaStream_t s) {
     CUtensorMap t;
-    const int st = make_tmap_kvb(&t, q.kv_b, k3_w_rows(q.batch), 8);
+    int st = make_tmap_kvb(&t, q.kv_b, k3_w_rows(q.batch), 8);
     if (st != MLA_OK) return st;
-    return launch_merge_uv(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    int sms = 0;
+    st = device_info(&sms);
+    if (st != MLA_OK) return st;
+    return launch_merge_uv(q, t, sms, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }

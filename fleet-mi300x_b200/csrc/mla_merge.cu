@@ -21,20 +21,23 @@
 namespace mla {
 
 namespace k3 {
-constexpr int kReq = 16;
+constexpr int kReq = 16;                          // requests per block (per m16 tile of the W_UV MMA)
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kABytes = kReq * kLora * 2;        // 16384: [16 requests][512] bf16, 1024-byte rows, swizzled
 constexpr int kRedBytes = kWarps * kLora * 4;     // 16384: one fp32 o_c row per warp (warp-group combine)
 
-// kCl CTAs (a thread-block cluster when > 1) share one (head, block of 16
+// kCl CTAs (a thread-block cluster when > 1) share one (head, block of kRq
 // requests): each folds every kCl-th partial, and owns kV / kCl rows of W_UV.
-template <int kCl>
+// kRq = 32 (plain form only) runs two m16 tiles against one staged W_UV[h].
+template <int kCl, int kRq = kReq>
 struct Shape {
-    static constexpr int kVRows = kV / kCl;                   // W_UV rows (v) of this CTA
+    static_assert(kRq == kReq || (kRq == 2 * kReq && kCl == 1), "32-request blocks exist in the plain form only");
+    static constexpr int kMt = kRq / 16;                       // m16 tiles of requests
+    static constexpr int kVRows = kV / kCl;                    // W_UV rows (v) of this CTA
     static constexpr int kWBytes = kVRows * kLora * 2;         // [8 column blocks][kVRows rows][128 B], swizzled
-    static constexpr int kXBytes = kCl > 1 ? kReq * (kLora + 4) * 4 : 0;  // cluster exchange: per request
-                                                                         // acc[512], m, L (fp32)
+    static constexpr int kABytes = kRq * kLora * 2;            // [kRq requests][512] bf16, 1024-byte rows, swizzled
+    static constexpr int kXBytes = kCl > 1 ? kRq * (kLora + 4) * 4 : 0;  // cluster exchange: per request
+                                                                        // acc[512], m, L (fp32)
     static constexpr int kSmemBytes = kWBytes + 2 * kABytes + kRedBytes + kXBytes + 64 + 1024;
 };
 constexpr int kClusterCtas = kK3ClusterCtas;  // cluster form: CTAs per (head, request block)
@@ -127,17 +130,18 @@ __device__ __forceinline__ uint32_t swz1024(uint32_t base, int row, int col) {
     return base + row * 1024 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2;
 }
 
-template <int kCl>
+template <int kCl, int kRq>
 __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const uint8_t* w_s, uint32_t ahi,
                                                uint32_t alo, int warp, int lane, int q, int h, int b0, int nreq,
                                                bool xmode, const ExLayout& ex, uint32_t step,
                                                __nv_bfloat16* __restrict__ out);
 
-template <int kCl>
+template <int kCl, int kRq>
 __global__ void __launch_bounds__(k3::kThreads, 1)
     k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb) {
     using namespace k3;
-    using Sh = Shape<kCl>;
+    using Sh = Shape<kCl, kRq>;
+    constexpr int kABytes = Sh::kABytes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* w_s = smem;
@@ -156,8 +160,8 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
 
     const int q = kCl > 1 ? (int)cluster_rank() : 0;  // rank within the (head, request block) cluster
     const int h = blockIdx.x / kCl;
-    const int b0 = blockIdx.y * kReq;
-    const int nreq = min(kReq, p.batch - b0);
+    const int b0 = blockIdx.y * kRq;
+    const int nreq = min(kRq, p.batch - b0);
 
     if (threadIdx.x == 0) {  // W_UV is a weight: no kernel writes it, so it may load before pdl_wait
         mbar_init(bar, 1);
@@ -182,10 +186,10 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     // ---- merge: o_c[r][l] = sum_c w_c acc_c[l] / sum_c w_c l_c ----
     // Every fold visits partials in plan-CTA order; requests without tiles (invalid
     // position) get a zero o_c.
-    __shared__ int32_t cum_s[kReq + 1];
+    __shared__ int32_t cum_s[kRq + 1];
     __shared__ float red_ml[kWarps][2];
-    if (threadIdx.x <= kReq) cum_s[threadIdx.x] = cum[min(b0 + (int)threadIdx.x, p.batch)];
-    for (int i = threadIdx.x; i < (kReq - nreq) * (kLora / 8); i += kThreads) {  // rows past nreq: zero operands
+    if (threadIdx.x <= kRq) cum_s[threadIdx.x] = cum[min(b0 + (int)threadIdx.x, p.batch)];
+    for (int i = threadIdx.x; i < (kRq - nreq) * (kLora / 8); i += kThreads) {  // rows past nreq: zero operands
         const int r = nreq + i / (kLora / 8), col = (i % (kLora / 8)) * 8;
         const uint32_t ahi0 = smem_u32(a_hi), alo0 = smem_u32(a_lo);
         *reinterpret_cast<uint4*>(a_hi + (swz1024(ahi0, r, col) - ahi0)) = make_uint4(0u, 0u, 0u, 0u);
@@ -342,84 +346,75 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] for this CTA's kVRows rows of v;
     // warp w owns v in [16w, 16w+16) ----
     if (warp * 16 >= Sh::kVRows) return;
-    k3_uv_epilogue<kCl>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, xmode, ex, xmode ? step_s : 0u, out);
+    k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, xmode, ex, xmode ? step_s : 0u, out);
 }
 
-// The W_UV MMA and the epilogue of one K3 warp (its 16 rows of v): R(out) in
-// bf16, or the fp32 shard partial y (into shard_out, or in exchange mode into
-// slot p.rank of every rank's exchange buffer).
-template <int kCl>
+// The W_UV MMA and the epilogue of one K3 warp (its 16 rows of v, all kRq
+// requests of the block as kRq / 16 m16 tiles): R(out) in bf16, or the fp32 shard
+// partial y (into shard_out, or in exchange mode into slot p.rank of every rank's
+// exchange buffer).
+template <int kCl, int kRq>
 __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const uint8_t* w_s, uint32_t ahi,
                                                uint32_t alo, int warp, int lane, int q, int h, int b0, int nreq,
                                                bool xmode, const ExLayout& ex, uint32_t step,
                                                __nv_bfloat16* __restrict__ out) {
-    using Sh = k3::Shape<kCl>;
+    using Sh = k3::Shape<kCl, kRq>;
+    constexpr int kMt = Sh::kMt;
     const int g = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;
     const uint32_t wb = smem_u32(w_s);
-    float acc[2][4];
+    float acc[kMt][2][4];
 #pragma unroll
-    for (int n = 0; n < 2; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    for (int mt = 0; mt < kMt; ++mt)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) acc[mt][n][0] = acc[mt][n][1] = acc[mt][n][2] = acc[mt][n][3] = 0.f;
 #pragma unroll 4
     for (int ks = 0; ks < kLora / 16; ++ks) {
-        uint32_t ah[4], al[4];
+        uint32_t b00, b01, b10, b11;  // v tiles 0, 1 of this warp
         {
-            const int row = (m8 & 1) * 8 + r8, col = 16 * ks + (m8 >> 1) * 8;
-            ldsm_x4(swz1024(ahi, row, col), ah[0], ah[1], ah[2], ah[3]);
-            ldsm_x4(swz1024(alo, row, col), al[0], al[1], al[2], al[3]);
-        }
-        {  // v tiles 0, 1 of this warp
             const int v = 16 * warp + (m8 >> 1) * 8 + r8;
             const int l = 16 * ks + (m8 & 1) * 8;
-            uint32_t b00, b01, b10, b11;
             ldsm_x4(wb + (l >> 6) * (Sh::kVRows * 128) + v * 128 + ((((l & 63) >> 3) ^ r8) << 4), b00, b01, b10, b11);
-            mma16816(acc[0], ah, b00, b01);
-            mma16816(acc[0], al, b00, b01);
-            mma16816(acc[1], ah, b10, b11);
-            mma16816(acc[1], al, b10, b11);
+        }
+#pragma unroll
+        for (int mt = 0; mt < kMt; ++mt) {
+            uint32_t ah[4], al[4];
+            const int row = 16 * mt + (m8 & 1) * 8 + r8, col = 16 * ks + (m8 >> 1) * 8;
+            ldsm_x4(swz1024(ahi, row, col), ah[0], ah[1], ah[2], ah[3]);
+            ldsm_x4(swz1024(alo, row, col), al[0], al[1], al[2], al[3]);
+            mma16816(acc[mt][0], ah, b00, b01);
+            mma16816(acc[mt][0], al, b00, b01);
+            mma16816(acc[mt][1], ah, b10, b11);
+            mma16816(acc[mt][1], al, b10, b11);
         }
     }
+    // The thread holds v, v + 1 of requests 16 mt + g (acc[..][0..1]) and 16 mt + g + 8 (acc[..][2..3]).
     const int v_base = q * Sh::kVRows;
-    if (xmode) {  // fp32 y = W_UV o_c / L of this shard, to every rank
 #pragma unroll
-        for (int d = 0; d < kMaxRanks; ++d) {
-            if (d >= p.world) break;
-            char* buf = ex_buf(p, d);
+    for (int mt = 0; mt < kMt; ++mt)
 #pragma unroll
-            for (int n = 0; n < 2; ++n) {
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int r = 16 * mt + g + 8 * hf;
+                if (r >= nreq) continue;
                 const int v = v_base + 16 * warp + 8 * n + 2 * t4;
-                if (g < nreq)
-                    st_line(ex_lines(buf, ex, p.world, p.exchange_batch, step & 1u, p.rank, b0 + g, h) + v / 2,
-                            acc[n][0], acc[n][1], step);
-                if (g + 8 < nreq)
-                    st_line(ex_lines(buf, ex, p.world, p.exchange_batch, step & 1u, p.rank, b0 + g + 8, h) + v / 2,
-                            acc[n][2], acc[n][3], step);
+                const float y0 = acc[mt][n][2 * hf], y1 = acc[mt][n][2 * hf + 1];
+                if (xmode) {  // fp32 y = W_UV o_c / L of this shard, to every rank
+#pragma unroll
+                    for (int d = 0; d < kMaxRanks; ++d) {
+                        if (d >= p.world) break;
+                        st_line(ex_lines(ex_buf(p, d), ex, p.world, p.exchange_batch, step & 1u, p.rank, b0 + r, h) +
+                                    v / 2,
+                                y0, y1, step);
+                    }
+                } else if (p.shard_out) {  // sequence-sharded step: fp32 y = W_UV o_c / L of this shard
+                    *reinterpret_cast<float2*>(p.shard_out + ((int64_t)(b0 + r) * kHeads + h) * MLA_SHARD_STRIDE + v) =
+                        make_float2(y0, y1);
+                } else {
+                    *reinterpret_cast<uint32_t*>(out + (int64_t)(b0 + r) * p.out_stride + h * kV + v) =
+                        pack_bf16(y0, y1);
+                }
             }
-        }
-        return;
-    }
-    if (p.shard_out) {  // sequence-sharded step: fp32 y = W_UV o_c / L of this shard
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-            const int v = v_base + 16 * warp + 8 * n + 2 * t4;
-            if (g < nreq)
-                *reinterpret_cast<float2*>(p.shard_out + ((int64_t)(b0 + g) * kHeads + h) * MLA_SHARD_STRIDE + v) =
-                    make_float2(acc[n][0], acc[n][1]);
-            if (g + 8 < nreq)
-                *reinterpret_cast<float2*>(p.shard_out + ((int64_t)(b0 + g + 8) * kHeads + h) * MLA_SHARD_STRIDE + v) =
-                    make_float2(acc[n][2], acc[n][3]);
-        }
-        return;
-    }
-#pragma unroll
-    for (int n = 0; n < 2; ++n) {
-        const int v = v_base + 16 * warp + 8 * n + 2 * t4;
-        if (g < nreq)
-            *reinterpret_cast<uint32_t*>(out + (int64_t)(b0 + g) * p.out_stride + h * kV + v) =
-                pack_bf16(acc[n][0], acc[n][1]);
-        if (g + 8 < nreq)
-            *reinterpret_cast<uint32_t*>(out + (int64_t)(b0 + g + 8) * p.out_stride + h * kV + v) =
-                pack_bf16(acc[n][2], acc[n][3]);
-    }
 }
 
 // Cross-shard combine of one (request, head): out[128h + v] = bf16( sum_r w_r y_r[v] /
@@ -555,25 +550,38 @@ cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, v
 }
 
 cudaError_t k3_configure() {
-    cudaError_t e = cudaFuncSetAttribute(k3_merge_uv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k3_merge_uv<1, k3::kReq>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          k3::Shape<1>::kSmemBytes);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k3_merge_uv<k3::kClusterCtas>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(k3_merge_uv<1, 2 * k3::kReq>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             k3::Shape<1, 2 * k3::kReq>::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k3_merge_uv<k3::kClusterCtas, k3::kReq>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 k3::Shape<k3::kClusterCtas>::kSmemBytes);
 }
 
 // Rows of W_UV per CTA of the launch chosen by launch_merge_uv (its TMA box height).
 int k3_w_rows(int batch) { return k3_use_cluster(batch) ? k3::Shape<k3::kClusterCtas>::kVRows : kV; }
 
-cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, cudaStream_t stream) {
-    const int blocks = (p.batch + k3::kReq - 1) / k3::kReq;
-    if (!k3_use_cluster(p.batch))
-        return launch_pdl(k3_merge_uv<1>, dim3(kHeads, blocks), dim3(k3::kThreads), k3::Shape<1>::kSmemBytes, stream,
-                          p, tmap_kvb);
+cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, int sm_count,
+                            cudaStream_t stream) {
+    if (!k3_use_cluster(p.batch)) {
+        // One CTA per SM fits (W_UV[h] is 128 KB of shared memory). Blocks of 16
+        // requests while 16 heads x blocks fill at most one wave; beyond that, blocks
+        // of 32 (two m16 tiles on one staged W_UV[h]), which halves the waves.
+        const int blocks16 = (p.batch + k3::kReq - 1) / k3::kReq;
+        if (kHeads * blocks16 <= sm_count)
+            return launch_pdl(k3_merge_uv<1, k3::kReq>, dim3(kHeads, blocks16), dim3(k3::kThreads),
+                              k3::Shape<1>::kSmemBytes, stream, p, tmap_kvb);
+        const int blocks32 = (p.batch + 2 * k3::kReq - 1) / (2 * k3::kReq);
+        return launch_pdl(k3_merge_uv<1, 2 * k3::kReq>, dim3(kHeads, blocks32), dim3(k3::kThreads),
+                          k3::Shape<1, 2 * k3::kReq>::kSmemBytes, stream, p, tmap_kvb);
+    }
     // few request blocks: a cluster of kClusterCtas CTAs per (head, block), so that a
     // long run of partials (one long sequence split over every plan CTA) is folded by
     // kClusterCtas SMs and combined through distributed shared memory
     constexpr int kCl = k3::kClusterCtas;
+    const int blocks = (p.batch + k3::kReq - 1) / k3::kReq;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kHeads * kCl, blocks);
     cfg.blockDim = dim3(k3::kThreads);
@@ -588,7 +596,7 @@ cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kv
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl>, p, tmap_kvb);
+    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl, k3::kReq>, p, tmap_kvb);
 }
 
 }  // namespace mla

@@ -134,6 +134,22 @@ def test_ragged_paged_batch(cuda_device, num_ctas, kernel):
         np.testing.assert_allclose(r, rows[b], rtol=1e-2, atol=1e-6)
 
 
+@pytest.mark.parametrize("B", [150, 200, 300])
+def test_large_batch_merge_blocks(cuda_device, B):
+    """Batches past one wave of 16-request K3 blocks (16 heads x ceil(B/16) > 148 SMs)
+    run K3 in 32-request blocks, two m16 tiles on one staged W_UV[h]; partial last
+    blocks (B = 150: 22 requests, B = 200: 8) leave whole tiles empty."""
+    rng = np.random.default_rng(B)
+    lengths = [int(x) for x in rng.integers(0, 400, size=B)]
+    d = ragged_batch(cuda_device, lengths)
+    pages_np = d["cache"].pages.float().cpu().numpy()
+    bt = d["cache"].block_table.cpu().numpy()
+    want, _ = oracle_paged(bt, pages_np, d, fast=True)
+    got = run_gpu(d, cuda_device)
+    for b in range(B):
+        assert_close(got[b], want[b], f"request {b} of {B} (T={lengths[b]})")
+
+
 def test_tensor_core_kernels_vs_check_kernel(cuda_device):
     d = ragged_batch(cuda_device, EDGE_LENGTHS)
     a = run_gpu(d, cuda_device, num_ctas=5)
