@@ -521,6 +521,13 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
         dist.barrier()
         torch.cuda.synchronize()
         stage_ms.append(timer(stage(name), max(5, args.steps // 2)))
+    if ex is not None:  # the same step with the exchange as K3 + K4 instead of the fused K3
+        names.append("step_k3_k4_split")
+        runner.flags |= native.FLAG_EXCHANGE_SPLIT
+        dist.barrier()
+        torch.cuda.synchronize()
+        stage_ms.append(timer(step, max(5, args.steps // 2)))
+        runner.flags &= ~native.FLAG_EXCHANGE_SPLIT
     step()  # a whole step last: the peer protocol's step counter advances again
     torch.cuda.synchronize()
     runner.check_errors()

@@ -18,8 +18,9 @@ cudaError_t launch_prologue(const MlaDecodeParams& p, const CUtensorMap& tmap_kv
 cudaError_t launch_attention_tc(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, const CUtensorMap& tmap_q,
                                 float scale_log2, cudaStream_t stream);
 cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, cudaStream_t stream);
-cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, int sm_count,
+cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, int sm_count, bool fused,
                             cudaStream_t stream);
+bool k3_fused_fits(int batch, int sm_count);
 cudaError_t k1_configure();
 cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,
                                   cudaStream_t stream);
@@ -182,14 +183,38 @@ int run_prologue(const MlaDecodeParams& q, cudaStream_t s) {
     return launch_prologue(q, t, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
-int run_merge(const MlaDecodeParams& q, cudaStream_t s) {
+int run_merge(const MlaDecodeParams& q, cudaStream_t s, bool fused = false) {
     CUtensorMap t;
     int st = make_tmap_kvb(&t, q.kv_b, k3_w_rows(q.batch), 8);
     if (st != MLA_OK) return st;
     int sms = 0;
     st = device_info(&sms);
     if (st != MLA_OK) return st;
-    return launch_merge_uv(q, t, sms, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+    return launch_merge_uv(q, t, sms, fused, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
+// Whether this step's peer exchange runs fused into K3 (no K4): the whole K3 grid
+// must be resident at once. The answer depends only on the batch and the device;
+// the last one is kept per device.
+struct FusedCache {
+    std::mutex mu;
+    int batch = -1;
+    bool fits = false;
+};
+FusedCache g_fused[kMaxDevices];
+
+bool exchange_fused(const MlaDecodeParams& q) {
+    if (q.world <= 0 || (q.flags & MLA_FLAG_EXCHANGE_SPLIT)) return false;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || device_info(&sms) != MLA_OK)
+        return false;
+    FusedCache& c = g_fused[dev];
+    std::lock_guard<std::mutex> lock(c.mu);
+    if (c.batch != q.batch) {
+        c.fits = k3_fused_fits(q.batch, sms);
+        c.batch = q.batch;
+    }
+    return c.fits;
 }
 
 bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }
@@ -240,7 +265,8 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         if (p->x_stride < MLA_HIDDEN) return MLA_E_INVALID_ARG;
         if (!aligned(p->x_n, 16) || (p->x_stride & 7) || !aligned(p->w_qkv, 16)) return MLA_E_MISALIGNED;
     }
-    if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW)) return MLA_E_INVALID_ARG;
+    if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW | MLA_FLAG_EXCHANGE_SPLIT))
+        return MLA_E_INVALID_ARG;
     if (p->world < 0 || p->world > MLA_MAX_RANKS) return MLA_E_INVALID_ARG;
     if (p->world > 0) {  // peer exchange: K3 writes every rank's buffer, K4 combines into out
         if (p->rank < 0 || p->rank >= p->world || p->shard_out || !p->out || p->exchange_timeout_us < 0)
@@ -479,9 +505,10 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream) {
     if (st != MLA_OK) return st;
     st = run_attention(q, s);
     if (st != MLA_OK) return st;
-    st = run_merge(q, s);
+    const bool fused = exchange_fused(q);
+    st = run_merge(q, s, fused);
     if (st != MLA_OK) return st;
-    if (q.world > 0) {
+    if (q.world > 0 && !fused) {
         st = run_exchange_combine(q, s);
         if (st != MLA_OK) return st;
     }

@@ -137,6 +137,14 @@ __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const u
                                                __nv_bfloat16* __restrict__ out);
 
 template <int kCl, int kRq>
+__device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const ExLayout& ex, uint32_t step,
+                                                 int q, int h, int b0, int nreq, __nv_bfloat16* __restrict__ out);
+
+// kFuse (peer exchange only, launched only when the whole grid is resident at
+// once on every rank): after storing its lines to every rank, the CTA waits for
+// the other ranks' lines of its own (requests, head, rows of v) and writes the
+// combined R(out) itself, so the step needs no K4.
+template <int kCl, int kRq, bool kFuse>
 __global__ void __launch_bounds__(k3::kThreads, 1)
     k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb) {
     using namespace k3;
@@ -338,15 +346,80 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         cluster_sync_all();  // no rank reuses or releases its exchange buffer while others read it
     }
     __syncthreads();
+    bool w_ok;
     {
         int dummy = 0;
-        if (!mbar_wait(bar, 0, &dummy, p.error_word)) return;
+        w_ok = mbar_wait(bar, 0, &dummy, p.error_word);
     }
 
     // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] for this CTA's kVRows rows of v;
     // warp w owns v in [16w, 16w+16) ----
-    if (warp * 16 >= Sh::kVRows) return;
-    k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, xmode, ex, xmode ? step_s : 0u, out);
+    if (!kFuse) {
+        if (!w_ok || warp * 16 >= Sh::kVRows) return;
+        k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, xmode, ex, xmode ? step_s : 0u, out);
+        return;
+    }
+    if (w_ok && warp * 16 < Sh::kVRows)
+        k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, true, ex, step_s, out);
+    k3_fused_combine<kCl, kRq>(p, ex, step_s, q, h, b0, nreq, out);
+    if (threadIdx.x == 0) {  // the last CTA to finish (every CTA's thread 0 has read the counter) advances it
+        uint32_t* ctl = reinterpret_cast<uint32_t*>(ex_buf(p, p.rank) + ex.ctl);
+        __threadfence();
+        if (atomicAdd(ctl + 1, 1u) == gridDim.x * gridDim.y - 1) {
+            ctl[1] = 0;
+            __threadfence();
+            atomicExch(ctl, step_s);
+        }
+    }
+}
+
+// The combine of a fused K3 CTA: for each of its requests and line pairs of v, the
+// rank-ordered fold of combine_head over the world shards' lines (this rank's own
+// included), polled until they carry this step (bounded by exchange_timeout_us; on
+// timeout MLA_DEV_PEER_TIMEOUT and zeros). One line (two values of v) per task.
+template <int kCl, int kRq>
+__device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const ExLayout& ex, uint32_t step,
+                                                 int q, int h, int b0, int nreq, __nv_bfloat16* __restrict__ out) {
+    using Sh = k3::Shape<kCl, kRq>;
+    constexpr int kLines = Sh::kVRows / 2;  // lines of this CTA's rows of v, per request
+    char* own = ex_buf(p, p.rank);
+    const uint64_t limit_ns = (uint64_t)(p.exchange_timeout_us > 0 ? p.exchange_timeout_us : 2000000) * 1000ull;
+    const uint64_t t0 = globaltimer_ns();
+    bool ok = true;
+    for (int task = threadIdx.x; task < nreq * kLines; task += k3::kThreads) {
+        const int b = b0 + task / kLines;
+        const int line = q * kLines + task % kLines;  // v = 2 line, 2 line + 1
+        float m[kMaxRanks], L[kMaxRanks];
+        float gm = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+            m[r] = -INFINITY;
+            L[r] = 0.f;
+            if (r < p.world && ok) {
+                ok = poll_line(ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h) + kV / 2, step, m[r],
+                               L[r], t0, limit_ns);
+                gm = fmaxf(gm, m[r]);
+            }
+        }
+        float a0 = 0.f, a1 = 0.f, W = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+            if (r >= p.world || !ok || !(L[r] > 0.f)) continue;  // an empty shard contributes nothing
+            float y0, y1;
+            ok = poll_line(ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h) + line, step, y0, y1, t0,
+                           limit_ns);
+            if (!ok) continue;
+            const float w = L[r] * exp2f(m[r] - gm);
+            W += w;
+            a0 = fmaf(w, y0, a0);
+            a1 = fmaf(w, y1, a1);
+        }
+        const float inv = W > 0.f ? 1.f / W : 0.f;
+        // after a timeout the remaining tasks poll nothing and write zeros
+        *reinterpret_cast<uint32_t*>(out + (int64_t)b * p.out_stride + h * kV + 2 * line) =
+            ok ? pack_bf16(a0 * inv, a1 * inv) : 0u;
+    }
+    if (!ok) record_error(p.error_word, MLA_DEV_PEER_TIMEOUT);
 }
 
 // The W_UV MMA and the epilogue of one K3 warp (its 16 rows of v, all kRq
@@ -549,43 +622,52 @@ cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, v
     return cudaGetLastError();
 }
 
+template <int kCl, int kRq, bool kFuse>
+static cudaError_t k3_set_smem() {
+    return cudaFuncSetAttribute(k3_merge_uv<kCl, kRq, kFuse>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                k3::Shape<kCl, kRq>::kSmemBytes);
+}
+
 cudaError_t k3_configure() {
-    cudaError_t e = cudaFuncSetAttribute(k3_merge_uv<1, k3::kReq>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         k3::Shape<1>::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(k3_merge_uv<1, 2 * k3::kReq>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             k3::Shape<1, 2 * k3::kReq>::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k3_merge_uv<k3::kClusterCtas, k3::kReq>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                k3::Shape<k3::kClusterCtas>::kSmemBytes);
+    constexpr int kCl = k3::kClusterCtas, kR = k3::kReq;
+    cudaError_t e;
+    if ((e = k3_set_smem<1, kR, false>()) != cudaSuccess || (e = k3_set_smem<1, kR, true>()) != cudaSuccess ||
+        (e = k3_set_smem<1, 2 * kR, false>()) != cudaSuccess || (e = k3_set_smem<1, 2 * kR, true>()) != cudaSuccess ||
+        (e = k3_set_smem<kCl, kR, false>()) != cudaSuccess || (e = k3_set_smem<kCl, kR, true>()) != cudaSuccess)
+        return e;
+    return cudaSuccess;
 }
 
 // Rows of W_UV per CTA of the launch chosen by launch_merge_uv (its TMA box height).
 int k3_w_rows(int batch) { return k3_use_cluster(batch) ? k3::Shape<k3::kClusterCtas>::kVRows : kV; }
 
-cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, int sm_count,
-                            cudaStream_t stream) {
-    if (!k3_use_cluster(p.batch)) {
-        // One CTA per SM fits (W_UV[h] is 128 KB of shared memory). Blocks of 16
-        // requests while 16 heads x blocks fill at most one wave; beyond that, blocks
-        // of 32 (two m16 tiles on one staged W_UV[h]), which halves the waves.
-        const int blocks16 = (p.batch + k3::kReq - 1) / k3::kReq;
-        if (kHeads * blocks16 <= sm_count)
-            return launch_pdl(k3_merge_uv<1, k3::kReq>, dim3(kHeads, blocks16), dim3(k3::kThreads),
-                              k3::Shape<1>::kSmemBytes, stream, p, tmap_kvb);
-        const int blocks32 = (p.batch + 2 * k3::kReq - 1) / (2 * k3::kReq);
-        return launch_pdl(k3_merge_uv<1, 2 * k3::kReq>, dim3(kHeads, blocks32), dim3(k3::kThreads),
-                          k3::Shape<1, 2 * k3::kReq>::kSmemBytes, stream, p, tmap_kvb);
-    }
-    // few request blocks: a cluster of kClusterCtas CTAs per (head, block), so that a
-    // long run of partials (one long sequence split over every plan CTA) is folded by
-    // kClusterCtas SMs and combined through distributed shared memory
-    constexpr int kCl = k3::kClusterCtas;
-    const int blocks = (p.batch + k3::kReq - 1) / k3::kReq;
+namespace {
+
+// The K3 launch for a batch: cluster form (4 CTAs per (head, 16 requests)) for
+// batches of at most 4 blocks of 16; else the plain form in blocks of 16 while 16
+// heads x blocks fill at most one wave of SMs (one CTA per SM: W_UV[h] is 128 KB of
+// shared memory), beyond that in blocks of 32 (two m16 tiles on one staged W_UV[h]),
+// which halves the waves.
+struct K3Launch {
+    int cl, rq;
+    dim3 grid;
+};
+
+K3Launch k3_launch(int batch, int sm_count) {
+    if (k3_use_cluster(batch))
+        return {k3::kClusterCtas, k3::kReq, dim3(kHeads * k3::kClusterCtas, (batch + k3::kReq - 1) / k3::kReq)};
+    const int blocks16 = (batch + k3::kReq - 1) / k3::kReq;
+    if (kHeads * blocks16 <= sm_count) return {1, k3::kReq, dim3(kHeads, blocks16)};
+    return {1, 2 * k3::kReq, dim3(kHeads, (batch + 2 * k3::kReq - 1) / (2 * k3::kReq))};
+}
+
+template <int kCl, int kRq, bool kFuse>
+cudaError_t k3_launch_form(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, dim3 grid, cudaStream_t stream,
+                           bool query_only, bool* resident) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kHeads * kCl, blocks);
+    cfg.gridDim = grid;
     cfg.blockDim = dim3(k3::kThreads);
-    cfg.dynamicSmemBytes = k3::Shape<kCl>::kSmemBytes;
+    cfg.dynamicSmemBytes = k3::Shape<kCl, kRq>::kSmemBytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -595,8 +677,54 @@ cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kv
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl, k3::kReq>, p, tmap_kvb);
+    cfg.numAttrs = kCl > 1 ? 2 : 1;
+    if (query_only) {  // can every CTA (cluster) of the grid be resident at once?
+        int n = 0;
+        cudaError_t e;
+        if (kCl > 1) {
+            e = cudaOccupancyMaxActiveClusters(&n, k3_merge_uv<kCl, kRq, kFuse>, &cfg);
+            *resident = e == cudaSuccess && (int64_t)n * kCl >= (int64_t)grid.x * grid.y;
+        } else {
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k3_merge_uv<kCl, kRq, kFuse>, k3::kThreads,
+                                                              k3::Shape<kCl, kRq>::kSmemBytes);
+            int dev = 0, sms = 0;
+            if (e == cudaSuccess) e = cudaGetDevice(&dev);
+            if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            *resident = e == cudaSuccess && (int64_t)n * sms >= (int64_t)grid.x * grid.y;
+        }
+        return e;
+    }
+    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl, kRq, kFuse>, p, tmap_kvb);
+}
+
+template <bool kFuse>
+cudaError_t k3_dispatch(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, const K3Launch& l,
+                        cudaStream_t stream, bool query_only, bool* resident) {
+    if (l.cl > 1) return k3_launch_form<k3::kClusterCtas, k3::kReq, kFuse>(p, tmap_kvb, l.grid, stream, query_only,
+                                                                          resident);
+    if (l.rq == k3::kReq)
+        return k3_launch_form<1, k3::kReq, kFuse>(p, tmap_kvb, l.grid, stream, query_only, resident);
+    return k3_launch_form<1, 2 * k3::kReq, kFuse>(p, tmap_kvb, l.grid, stream, query_only, resident);
+}
+
+}  // namespace
+
+// Whether the fused K3 (exchange and combine in the same kernel) may run for this
+// batch: every CTA of its grid must be resident at the same time, since each one
+// waits for the same CTA of the other ranks. Pure host query.
+bool k3_fused_fits(int batch, int sm_count) {
+    const K3Launch l = k3_launch(batch, sm_count);
+    bool resident = false;
+    MlaDecodeParams dummy{};
+    CUtensorMap t{};
+    return k3_dispatch<true>(dummy, t, l, nullptr, true, &resident) == cudaSuccess && resident;
+}
+
+cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, int sm_count, bool fused,
+                            cudaStream_t stream) {
+    const K3Launch l = k3_launch(p.batch, sm_count);
+    return fused ? k3_dispatch<true>(p, tmap_kvb, l, stream, false, nullptr)
+                 : k3_dispatch<false>(p, tmap_kvb, l, stream, false, nullptr);
 }
 
 }  // namespace mla

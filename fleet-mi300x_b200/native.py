@@ -21,6 +21,7 @@ MAX_BATCH = 65536
 FLAG_CHECK_KERNEL = 0x2
 FLAG_TCGEN05 = 0x4
 FLAG_NO_NEW_ROW = 0x8
+FLAG_EXCHANGE_SPLIT = 0x10  # peer exchange as K3 + K4 even where the fused K3 applies
 SHARD_STRIDE = 132
 MAX_PROJECT_BATCH = 64  # MLA_MAX_PROJECT_BATCH: batch limit of the in-library q|kv_a projection
 STATIC_SCRATCH_BYTES = 32 << 20  # MLA_STATIC_SCRATCH_BYTES, the workspace of mla_decode_step_static

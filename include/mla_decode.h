@@ -99,6 +99,8 @@ typedef enum {
                                      m16n8k16 kernel (heads on M); same plan and partial layout */
 #define MLA_FLAG_NO_NEW_ROW 0x8   /* sequence-sharded decode, a shard that does not own the new token:
                                      store no row and attend over cache rows 0..seq_lens[b]-1 only */
+#define MLA_FLAG_EXCHANGE_SPLIT 0x10 /* peer exchange (world > 0): run it as K3 + K4 even where the fused
+                                        form (K3 waits for the other ranks and combines, no K4) applies */
 
 typedef struct MlaDecodeParams {
     uint32_t struct_size; /* sizeof(MlaDecodeParams) */
@@ -166,7 +168,11 @@ typedef struct MlaDecodeParams {
      * the same 64-bit store; a last kernel (K4) waits until the values of all
      * `world` shards carry this step, bounded by exchange_timeout_us, and combines
      * them in rank order into `out` with the arithmetic of mla_combine_shards. No
-     * flag, fence or collective library call is on the path.
+     * flag, fence or collective library call is on the path. Where the whole K3
+     * grid can be resident at once (small batches), mla_decode_step runs the
+     * fused form instead: each K3 CTA waits for the other ranks' values of its own
+     * slice and writes `out` itself, with the same arithmetic, and no K4 runs
+     * (MLA_FLAG_EXCHANGE_SPLIT keeps K3 + K4).
      * shard_out must be NULL; w_o (K5) may follow. Every rank must run the same
      * sequence of steps with the same batch. world = 0: no exchange. */
     void* exchange[MLA_MAX_RANKS]; /* every rank's exchange buffer as mapped in this process

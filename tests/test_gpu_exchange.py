@@ -112,10 +112,18 @@ def test_exchange_matches_oracle(cuda_device):
         ex[0].close()
 
 
-def test_world1_exchange_step_equals_local_combine(cuda_device):
-    """One shard: the whole step in one call (K1-K4) equals shard_out + combine."""
+@pytest.mark.parametrize("split", [False, True], ids=["fused", "split"])
+@pytest.mark.parametrize("lengths", [[700, 1, 64, 4000], [int(x) for x in np.random.default_rng(5).integers(0, 300, 150)],
+                                     [int(x) for x in np.random.default_rng(6).integers(0, 300, 300)]],
+                         ids=["cluster-form", "b150-32-blocks", "b300-not-resident"])
+def test_world1_exchange_step_equals_local_combine(cuda_device, lengths, split):
+    """One shard, the whole step in one call: K3 fused with the combine where its grid
+    is resident at once (4 requests: 64 cluster CTAs; 150: 80 CTAs of 32 requests),
+    else, or with MLA_FLAG_EXCHANGE_SPLIT, K3 + K4 (300 requests: 160 CTAs). Either
+    equals shard_out + mla_combine_shards bit for bit."""
     runner, *_ = _runner(cuda_device)
-    lengths = [700, 1, 64, 4000]
+    if split:
+        runner.flags |= native.FLAG_EXCHANGE_SPLIT
     caches, _ = _sharded_caches(lengths, 1, cuda_device, seed=21)
     q, kv_a = _inputs(len(lengths), cuda_device, seed=22)
     part = torch.empty(len(lengths), 16, native.SHARD_STRIDE, dtype=torch.float32, device=cuda_device)
@@ -123,7 +131,7 @@ def test_world1_exchange_step_equals_local_combine(cuda_device):
     want = fleet.combine_shards(part[None])
     ex = dist_mod.ExchangeBuffers.local(1, max_batch=len(lengths))
     try:
-        for _ in range(2):
+        for _ in range(3):
             got = runner.attend(q, kv_a, caches[0], exchange=ex[0])
             runner.check_errors()
             assert torch.equal(got, want)
@@ -163,10 +171,14 @@ def test_exchange_step_in_cuda_graph(cuda_device):
         ex[0].close()
 
 
-def test_missing_peer_times_out_with_error(cuda_device):
-    """Rank 1 never runs: rank 0's K4 waits for flags nothing sets, gives up after the
-    limit, records MLA_DEV_PEER_TIMEOUT and writes zeros. The context stays usable."""
+@pytest.mark.parametrize("split", [False, True], ids=["fused", "split"])
+def test_missing_peer_times_out_with_error(cuda_device, split):
+    """Rank 1 never runs: rank 0's combine (the fused K3, or K4) waits for lines nothing
+    writes, gives up after the limit, records MLA_DEV_PEER_TIMEOUT and writes zeros.
+    The context stays usable."""
     runner, *_ = _runner(cuda_device)
+    if split:
+        runner.flags |= native.FLAG_EXCHANGE_SPLIT
     caches, _ = _sharded_caches([500], 2, cuda_device, seed=41)
     q, kv_a = _inputs(1, cuda_device, seed=42)
     pos = torch.tensor([500], dtype=torch.int32, device=cuda_device)
@@ -229,7 +241,12 @@ def _peer_worker(rank, world, port, T, q_out):
         ex = dist_mod.ExchangeBuffers.create(rank, world, max_batch=1)
         step = dist_mod.SequenceShardedAttention(runner, rank, world, exchange=ex)
         runner.project = lambda x: (q, kv_a)
-        outs = [step.step(torch.zeros(1, 2048, dtype=BF, device=dev), caches[rank], pos).clone() for _ in range(3)]
+        x0 = torch.zeros(1, 2048, dtype=BF, device=dev)
+        outs = [step.step(x0, caches[rank], pos).clone() for _ in range(3)]  # fused K3 (grid resident)
+        runner.flags |= native.FLAG_EXCHANGE_SPLIT
+        outs += [step.step(x0, caches[rank], pos).clone() for _ in range(2)]  # K3 + K4
+        runner.flags &= ~native.FLAG_EXCHANGE_SPLIT
+        outs += [step.step(x0, caches[rank], pos).clone()]  # and back: the step counter is shared
         torch.cuda.synchronize()
         runner.check_errors()
         # the same step on this GPU alone, all ranks emulated, gathered combine
