@@ -56,8 +56,8 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Pa
         "-o", str(lib) + ".tmp",
         *[str(s) for s in sources()],
     ]
-    if trace:
-        cmd.insert(1, "-DMLA_TRACE")
+    if trace:  # the timeline array is shared by the kernels of several files: relocatable device code
+        cmd[1:1] = ["-DMLA_TRACE", "-rdc=true"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     proc = subprocess.run(cmd, capture_output=True, text=True)

@@ -549,6 +549,24 @@ cudaError_t launch_attention_check(const MlaDecodeParams& p, float scale_log2, c
 }  // namespace mla
 
 #ifdef MLA_TRACE
+namespace mla {
+__device__ unsigned long long g_mla_timeline[kTlKernels * kTlCtas * kTlEvents];
+}  // namespace mla
+
+// Trace build only (not part of include/mla_decode.h): copy the kernel timeline
+// [5 kernels][512 CTAs][4: entry, after pdl_wait, exit (%globaltimer ns, 0 = not
+// stamped), SM id + 1] to `host` and clear it.
+extern "C" int mla_timeline_read(unsigned long long* host, uint64_t n) {
+    using namespace mla;
+    const uint64_t total = (uint64_t)kTlKernels * kTlCtas * kTlEvents;
+    if (!host || n < total) return MLA_E_INVALID_ARG;
+    if (cudaMemcpyFromSymbol(host, g_mla_timeline, total * sizeof(unsigned long long)) != cudaSuccess)
+        return MLA_E_LAUNCH;
+    static unsigned long long zeros[kTlKernels * kTlCtas * kTlEvents];
+    if (cudaMemcpyToSymbol(g_mla_timeline, zeros, sizeof(zeros)) != cudaSuccess) return MLA_E_LAUNCH;
+    return MLA_OK;
+}
+
 // Trace build only (not part of include/mla_decode.h): copy the attention
 // kernel's per-tile stamps [160 CTAs][96 tiles][8 events] (SM clocks) to `host`
 // and clear them.

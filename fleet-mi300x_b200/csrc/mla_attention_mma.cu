@@ -87,6 +87,7 @@ __device__ __forceinline__ int p_offset(int head, int u) { return head * 64 + ((
 __global__ void __launch_bounds__(mmak::kThreads, 1)
     k2_attention_mma(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kv, float scale_log2) {
     using namespace mmak;
+    MLA_TL_SCOPE(1);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -106,6 +107,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
 
     pdl_trigger();
     pdl_wait();  // the plan, absorbed queries and new rows come from K1
+    MLA_TL_WAITED(1);
     const int64_t U = cum[p.batch];
     const int G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
     const int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan

@@ -484,4 +484,44 @@ constexpr int kTraceCtas = 160, kTraceTiles = 96, kTraceEvents = 8;
     } while (0)
 #endif
 
+// Optional kernel timeline (trace build only): per kernel and CTA, %globaltimer at
+// entry (thread 0), after pdl_wait (thread 0) and at exit (the last warp of the CTA
+// to return), and the SM id; read back by mla_timeline_read(). Kernels:
+// 0 = K1, 1 = K2, 2 = K3, 3 = K4, 4 = K0 / K5 (weight stream).
+#ifdef MLA_TRACE
+constexpr int kTlKernels = 5, kTlCtas = 512, kTlEvents = 4;
+extern __device__ unsigned long long g_mla_timeline[kTlKernels * kTlCtas * kTlEvents];
+__device__ __forceinline__ void tl_stamp(int k, int ev) {
+    const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+    if (cta >= kTlCtas) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    unsigned long long* slot = &g_mla_timeline[(k * kTlCtas + cta) * kTlEvents];
+    if (ev == 2) {
+        if ((threadIdx.x & 31) == 0) atomicMax(slot + 2, t);
+    } else if (threadIdx.x == 0) {
+        slot[ev] = t;
+        if (ev == 0) {
+            unsigned sm;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+            slot[3] = sm + 1;
+        }
+    }
+}
+struct TlScope {  // entry stamp now, exit stamp on every return path
+    int k;
+    __device__ explicit TlScope(int kernel) : k(kernel) { tl_stamp(k, 0); }
+    __device__ ~TlScope() { tl_stamp(k, 2); }
+};
+#define MLA_TL_SCOPE(k) ::mla::TlScope mla_tl_scope_(k)
+#define MLA_TL_WAITED(k) ::mla::tl_stamp(k, 1)
+#else
+#define MLA_TL_SCOPE(k) \
+    do {                \
+    } while (0)
+#define MLA_TL_WAITED(k) \
+    do {                 \
+    } while (0)
+#endif
+
 }  // namespace mla

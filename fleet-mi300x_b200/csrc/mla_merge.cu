@@ -148,6 +148,7 @@ template <int kCl, int kRq, bool kFuse>
 __global__ void __launch_bounds__(k3::kThreads, 1)
     k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb) {
     using namespace k3;
+    MLA_TL_SCOPE(2);
     using Sh = Shape<kCl, kRq>;
     constexpr int kABytes = Sh::kABytes;
     extern __shared__ uint8_t smem_raw[];
@@ -179,6 +180,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     }
     pdl_trigger();
     pdl_wait();  // partials from K2, plan from K1
+    MLA_TL_WAITED(2);
     const int64_t U = cum[p.batch];
     const int G = (int)(U < 1 ? 1 : (U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas));
 
@@ -543,10 +545,12 @@ __global__ void __launch_bounds__(256) k4_combine_shards(const float* __restrict
 // timeout the block records MLA_DEV_PEER_TIMEOUT and writes zeros). The last block
 // to finish advances the buffer's step counter.
 __global__ void __launch_bounds__(256) k4_exchange_combine(const MlaDecodeParams p) {
+    MLA_TL_SCOPE(3);
     const int b = blockIdx.x;
     const int h = threadIdx.x >> 4, v0 = (threadIdx.x & 15) * 8;
     pdl_trigger();
     pdl_wait();  // this rank's K3 has completed (and read the step counter)
+    MLA_TL_WAITED(3);
     const ExLayout ex = ex_layout(p.world, p.exchange_batch);
     char* own = ex_buf(p, p.rank);
     uint32_t* ctl = reinterpret_cast<uint32_t*>(own + ex.ctl);

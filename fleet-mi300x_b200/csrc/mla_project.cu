@@ -53,6 +53,7 @@ template <int kRows, int kEpi>
 __global__ void __launch_bounds__(128, 1)
     k_weight_stream(const StreamArgs a, const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_x) {
+    MLA_TL_SCOPE(4);
     using S = WStream<kRows>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -74,6 +75,7 @@ __global__ void __launch_bounds__(128, 1)
         }
     }
     pdl_wait();  // x (and the residual) come from earlier work on the stream
+    MLA_TL_WAITED(4);
     pdl_trigger();
     __syncthreads();  // barriers initialised
 

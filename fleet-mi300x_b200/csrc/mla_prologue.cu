@@ -124,12 +124,14 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
 
 __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p,
                                                             const __grid_constant__ CUtensorMap tmap_wuk) {
+    MLA_TL_SCOPE(0);
     const WsLayout ws = ws_layout(p);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     __nv_bfloat16* qa = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
     const K1Grid g(p.batch);
     const int cta = blockIdx.x;
     pdl_wait();     // q, kv_a and the cache come from earlier work on the stream
+    MLA_TL_WAITED(0);
     pdl_trigger();  // K2 may become resident now; it waits for this grid before reading its output
 
     if (cta == g.total - 1) {
