@@ -554,8 +554,8 @@ __device__ unsigned long long g_mla_timeline[kTlKernels * kTlCtas * kTlEvents];
 }  // namespace mla
 
 // Trace build only (not part of include/mla_decode.h): copy the kernel timeline
-// [5 kernels][512 CTAs][4: entry, after pdl_wait, exit (%globaltimer ns, 0 = not
-// stamped), SM id + 1] to `host` and clear it.
+// [5 kernels][512 CTAs][6: entry, after pdl_wait, exit (%globaltimer ns, 0 = not
+// stamped), SM id + 1, mark 1, mark 2] to `host` and clear it.
 extern "C" int mla_timeline_read(unsigned long long* host, uint64_t n) {
     using namespace mla;
     const uint64_t total = (uint64_t)kTlKernels * kTlCtas * kTlEvents;

@@ -486,10 +486,10 @@ constexpr int kTraceCtas = 160, kTraceTiles = 96, kTraceEvents = 8;
 
 // Optional kernel timeline (trace build only): per kernel and CTA, %globaltimer at
 // entry (thread 0), after pdl_wait (thread 0) and at exit (the last warp of the CTA
-// to return), and the SM id; read back by mla_timeline_read(). Kernels:
-// 0 = K1, 1 = K2, 2 = K3, 3 = K4, 4 = K0 / K5 (weight stream).
+// to return), the SM id, and two kernel-specific marks (latest writer wins); read
+// back by mla_timeline_read(). Kernels: 0 = K1, 1 = K2, 2 = K3, 3 = K4, 4 = K0 / K5.
 #ifdef MLA_TRACE
-constexpr int kTlKernels = 5, kTlCtas = 512, kTlEvents = 4;
+constexpr int kTlKernels = 5, kTlCtas = 512, kTlEvents = 6;
 extern __device__ unsigned long long g_mla_timeline[kTlKernels * kTlCtas * kTlEvents];
 __device__ __forceinline__ void tl_stamp(int k, int ev) {
     const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x);
@@ -513,9 +513,20 @@ struct TlScope {  // entry stamp now, exit stamp on every return path
     __device__ explicit TlScope(int kernel) : k(kernel) { tl_stamp(k, 0); }
     __device__ ~TlScope() { tl_stamp(k, 2); }
 };
+__device__ __forceinline__ void tl_mark(int k, int slot) {  // slot 4 or 5; lane 0 of the calling warp
+    const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+    if (cta >= kTlCtas || (threadIdx.x & 31) != 0) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    atomicMax(&g_mla_timeline[(k * kTlCtas + cta) * kTlEvents + slot], t);
+}
 #define MLA_TL_SCOPE(k) ::mla::TlScope mla_tl_scope_(k)
 #define MLA_TL_WAITED(k) ::mla::tl_stamp(k, 1)
+#define MLA_TL_MARK(k, slot) ::mla::tl_mark(k, slot)
 #else
+#define MLA_TL_MARK(k, slot) \
+    do {                     \
+    } while (0)
 #define MLA_TL_SCOPE(k) \
     do {                \
     } while (0)

@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         cluster_sync_all();  // no rank reuses or releases its exchange buffer while others read it
     }
     __syncthreads();
+    MLA_TL_MARK(2, 4);  // merge done
     bool w_ok;
     {
         int dummy = 0;
@@ -462,6 +463,7 @@ __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const u
             mma16816(acc[mt][1], al, b10, b11);
         }
     }
+    MLA_TL_MARK(2, 5);  // W_UV MMAs done
     // The thread holds v, v + 1 of requests 16 mt + g (acc[..][0..1]) and 16 mt + g + 8 (acc[..][2..3]).
     const int v_base = q * Sh::kVRows;
 #pragma unroll

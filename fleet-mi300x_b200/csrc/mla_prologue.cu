@@ -87,33 +87,42 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum) {
 // One warp: q_pe RoPE of request b, then (unless the call stores no row)
 // kv_post + the cache append at local row seq_lens[b].
 __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b, int lane) {
-    if (!request_ok(p, b)) return;  // recorded by the planner
+    // Two dependent rounds of loads: first everything that depends on b alone (the
+    // row counts, q_pe of all heads, the raw kv_a row and gamma), then what depends
+    // on the position (the RoPE tables, the block-table entry of the new row).
     const int pos = p.seq_lens[b];
-    const int rp = rope_position(p, b);
-    const float* cs = p.rope_cos + (int64_t)rp * kRope;
-    const float* sn = p.rope_sin + (int64_t)rp * kRope;
+    const int rp = p.rope_pos ? p.rope_pos[b] : pos;
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q) + (int64_t)b * p.q_stride;
-    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride;
-    const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w);
-
-    // q_pe of all 16 heads: lane j rotates pair j (all 16 loads issued first)
-    __nv_bfloat16* qrow = qa + (int64_t)b * kQRows * kRow;
     __nv_bfloat162 xq[kHeads];
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) xq[h] = reinterpret_cast<const __nv_bfloat162*>(q + h * kQHead + kNope)[lane];
+    const bool append = new_row_count(p) != 0;
+    KvPostIn kin;
+    if (append)
+        kv_post_load(reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride,
+                     reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w), lane, kin);
+    // request_ok, on the values already loaded (an invalid request is recorded by the planner)
+    if (!(pos >= 0 && rp >= 0 && rp < p.max_pos && pos + new_row_count(p) <= p.max_blocks * kPage)) return;
+
+    const float* cs = p.rope_cos + (int64_t)rp * kRope;
+    const float* sn = p.rope_sin + (int64_t)rp * kRope;
+    const float c0 = cs[lane], c1 = cs[32 + lane], s0 = sn[lane], s1 = sn[32 + lane];
+    const int page = append ? p.block_table[(int64_t)b * p.max_blocks + pos / kPage] : 0;
+
+    // q_pe of all 16 heads: lane j rotates pair j
+    __nv_bfloat16* qrow = qa + (int64_t)b * kQRows * kRow;
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) {
         float lo, hi;
-        rope_pair(__low2float(xq[h]), __high2float(xq[h]), cs, sn, lane, lo, hi);
+        rope_pair_r(__low2float(xq[h]), __high2float(xq[h]), c0, s0, c1, s1, lo, hi);
         qrow[h * kRow + kLora + lane] = __float2bfloat16_rn(lo);
         qrow[h * kRow + kLora + 32 + lane] = __float2bfloat16_rn(hi);
     }
-    if (!new_row_count(p)) return;
+    if (!append) return;
 
     __align__(16) __nv_bfloat16 outc[16];
     float lo, hi;
-    kv_post_compute(src, gam, p.rms_eps, cs, sn, lane, outc, lo, hi);
-    const int page = p.block_table[(int64_t)b * p.max_blocks + pos / kPage];
+    kv_post_finish(kin, p.rms_eps, cs, sn, lane, outc, lo, hi);
     if (page < 0 || page >= p.n_pages) {
         if (lane == 0) record_error(p.error_word, MLA_DEV_BAD_PAGE);
         return;
@@ -130,6 +139,19 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
     __nv_bfloat16* qa = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
     const K1Grid g(p.batch);
     const int cta = blockIdx.x;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* w_s = smem;
+    uint8_t* q_s = smem + kWukBytes;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(q_s + kQnBytes);
+    const int rb = cta / (kHeads * kQuarters), c_in = cta % (kHeads * kQuarters);
+    const int h = c_in / kQuarters, j = c_in % kQuarters;
+    if (cta != g.total - 1 && threadIdx.x == 0) {  // W_UK is a weight: no kernel writes it, so before pdl_wait
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(bar, kWukBytes);
+        tma_load_3d(w_s, &tmap_wuk, bar, 0, h * kKvbHead, kK1WukBlocks * j, kCacheEvictLast);
+    }
     pdl_wait();     // q, kv_a and the cache come from earlier work on the stream
     MLA_TL_WAITED(0);
     pdl_trigger();  // K2 may become resident now; it waits for this grid before reading its output
@@ -140,24 +162,12 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
     }
 
     // ---- absorb CTA: q_c[b][h][128j + l] = q_nope[b][h] @ W_UK[h][:, 128j + l] ----
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* w_s = smem;
-    uint8_t* q_s = smem + kWukBytes;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(q_s + kQnBytes);
-    const int rb = cta / (kHeads * kQuarters), c_in = cta % (kHeads * kQuarters);
-    const int h = c_in / kQuarters, j = c_in % kQuarters;
     const int b0 = rb * kReqBlock;
     const int nreq = min(kReqBlock, p.batch - b0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        mbar_init(bar, 1);
-        fence_mbar_init();
-        mbar_arrive_expect_tx(bar, kWukBytes);
-        tma_load_3d(w_s, &tmap_wuk, bar, 0, h * kKvbHead, kK1WukBlocks * j, kCacheEvictLast);
-    }
     if (warp == kK1MmaWarps) {  // the per-request work of request b0 + c_in; joins no barrier
         if (c_in < nreq) request_rows(p, qa, b0 + c_in, lane);
+        MLA_TL_MARK(0, 5);
         return;
     }
     // q_nope [64][128] -> shared, 256-byte rows with 16-byte units XOR (row & 7)
@@ -242,6 +252,7 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
                     pack_bf16(acc[mt][n][2], acc[mt][n][3]);
         }
     }
+    MLA_TL_MARK(0, 4);
 }
 
 cudaError_t k1_configure() {

@@ -6,6 +6,7 @@ device's free memory or torch's allocation count. The file name makes pytest col
 it last, so it runs both after every other GPU test in one process and alone.
 """
 import ctypes
+import gc
 import importlib
 
 import pytest
@@ -44,16 +45,24 @@ def test_static_step_equals_decode_step_on_two_calls(cuda_device):
         out = torch.full_like(want, float("nan"))
         p = runner.params(q, kv_a, cache, out)
         p.workspace, p.workspace_bytes = None, 0  # ignored by the static entry point
-        torch.cuda.synchronize(cuda_device)
-        free0, _ = torch.cuda.mem_get_info(cuda_device)
-        alloc0 = torch.cuda.memory_allocated(cuda_device)
-        native.check(runner.lib.mla_decode_step_static(ctypes.byref(p), stream), "mla_decode_step_static", p)
-        torch.cuda.synchronize(cuda_device)
+        # earlier tests' garbage must not be freed inside the measured window
+        gc.collect()
+        gc.disable()
+        try:
+            torch.cuda.synchronize(cuda_device)
+            free0, _ = torch.cuda.mem_get_info(cuda_device)
+            alloc0 = torch.cuda.memory_allocated(cuda_device)
+            native.check(runner.lib.mla_decode_step_static(ctypes.byref(p), stream), "mla_decode_step_static", p)
+            torch.cuda.synchronize(cuda_device)
+            alloc1 = torch.cuda.memory_allocated(cuda_device)
+            free1, _ = torch.cuda.mem_get_info(cuda_device)
+        finally:
+            gc.enable()
         runner.check_errors()
         assert torch.equal(out, want), f"call {call}: static-scratch output differs from mla_decode_step's"
-        assert torch.cuda.memory_allocated(cuda_device) == alloc0
+        assert alloc1 == alloc0
         if call == 1:  # the first call may load the library's device image, which holds the scratch
-            assert torch.cuda.mem_get_info(cuda_device)[0] == free0, "the static step allocated device memory"
+            assert free1 == free0, "the static step allocated device memory"
 
 
 def test_static_step_refuses_batches_beyond_its_scratch(cuda_device):
