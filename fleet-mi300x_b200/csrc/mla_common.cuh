@@ -242,22 +242,31 @@ __device__ __forceinline__ void st_line(ulonglong2* line, float a, float b, uint
     asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(line), "l"(x), "l"(y) : "memory");
 }
 
-// Poll a line until both halves carry `step` (true, values in a, b) or until
-// limit_ns have passed since t0 (false).
-__device__ __forceinline__ bool poll_line(const ulonglong2* line, uint32_t step, float& a, float& b, uint64_t t0,
+// One load of a line (both halves in one 128-bit access of two 64-bit elements).
+__device__ __forceinline__ ulonglong2 ld_line(const ulonglong2* line) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(line) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool line_ready(const ulonglong2& v, uint32_t step) {
+    return (uint32_t)(v.x >> 32) == step && (uint32_t)(v.y >> 32) == step;
+}
+
+// Wait until a line carries `step`, starting from an already loaded value v
+// (true; v then holds the line) or until limit_ns have passed since t0 (false).
+// Callers load all the lines they need first, so that one round trip serves them
+// all when the data is already there.
+__device__ __forceinline__ bool wait_line(const ulonglong2* line, uint32_t step, ulonglong2& v, uint64_t t0,
                                           uint64_t limit_ns) {
-    for (uint32_t k = 1;; ++k) {
-        unsigned long long x, y;
-        asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(line) : "memory");
-        if ((uint32_t)(x >> 32) == step && (uint32_t)(y >> 32) == step) {
-            a = __uint_as_float((uint32_t)x);
-            b = __uint_as_float((uint32_t)y);
-            return true;
-        }
+    for (uint32_t k = 1; !line_ready(v, step); ++k) {
         if ((k & 31) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
         __nanosleep(32);
+        v = ld_line(line);
     }
+    return true;
 }
+__device__ __forceinline__ float line_lo(const ulonglong2& v) { return __uint_as_float((uint32_t)v.x); }
+__device__ __forceinline__ float line_hi(const ulonglong2& v) { return __uint_as_float((uint32_t)v.y); }
 
 // A wait on one phase of an mbarrier that gives up after `kWaitLimitNs` or
 // when another role raised `*abort`. On giving up it records

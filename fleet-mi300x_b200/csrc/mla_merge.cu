@@ -36,8 +36,8 @@ struct Shape {
     static constexpr int kVRows = kV / kCl;                    // W_UV rows (v) of this CTA
     static constexpr int kWBytes = kVRows * kLora * 2;         // [8 column blocks][kVRows rows][128 B], swizzled
     static constexpr int kABytes = kRq * kLora * 2;            // [kRq requests][512] bf16, 1024-byte rows, swizzled
-    static constexpr int kXBytes = kCl > 1 ? kRq * (kLora + 4) * 4 : 0;  // cluster exchange: per request
-                                                                        // acc[512], m, L (fp32)
+    static constexpr int kXBytes = kCl > 1 ? kCl * kRq * (kLora + 4) * 4 : 0;  // cluster exchange: per rank
+                                                                              // and request acc[512], m, L
     static constexpr int kSmemBytes = kWBytes + 2 * kABytes + kRedBytes + kXBytes + 64 + 1024;
 };
 constexpr int kClusterCtas = kK3ClusterCtas;  // cluster form: CTAs per (head, request block)
@@ -74,6 +74,16 @@ __device__ __forceinline__ float2 dsmem_ld2(uint32_t addr) {
     asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
     return v;
 }
+// Stores into a peer CTA's shared memory that complete their bytes on an mbarrier
+// there (cluster addresses from dsmem_addr).
+__device__ __forceinline__ void dsmem_push4(uint32_t addr, float4 v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ void dsmem_push2(uint32_t addr, float2 v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
+                 ::"r"(addr), "f"(v.x), "f"(v.y), "r"(remote_bar) : "memory");
+}
 
 // Partial slot s = (c + b) * heads + h: its (m, L) pair and the lane's four
 // float4 of acc (latent l = 4 lane + 128 k, k < 4).
@@ -103,7 +113,8 @@ __device__ __forceinline__ void fold_partial(float2 ml, const float4 (&a)[4], fl
 
 // Fold of the partials c = first, first + stride, ... <= last of (request b,
 // head h), in order. Loads are issued kDepth partials (kDepth x 2 KB per warp)
-// at a time. (Eight at a time measured no faster than four.)
+// at a time. (Six or eight at a time measured no faster than four: at one request
+// the fold is bound by the bytes each of the 64 cluster SMs pulls, not by rounds.)
 template <int kDepth = 4>
 __device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
                                                int b, int h, int first, int last, int stride, int lane, float& m,
@@ -157,7 +168,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     uint8_t* a_hi = smem + Sh::kWBytes;
     uint8_t* a_lo = a_hi + kABytes;
     float* red_acc = reinterpret_cast<float*>(a_lo + kABytes);           // [kWarps][512]
-    float* xch = reinterpret_cast<float*>(a_lo + kABytes + kRedBytes);     // [16][512 + 4]: acc, m, L
+    float* xch = reinterpret_cast<float*>(a_lo + kABytes + kRedBytes);     // [kCl][kRq][512 + 4]: acc, m, L
     uint64_t* bar = reinterpret_cast<uint64_t*>(a_lo + kABytes + kRedBytes + Sh::kXBytes);
 
     const WsLayout ws = ws_layout(p);
@@ -172,12 +183,17 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     const int b0 = blockIdx.y * kRq;
     const int nreq = min(kRq, p.batch - b0);
 
+    // cluster form: bar[1] counts the bytes of the other ranks' folds pushed into xch
+    constexpr uint32_t kPushBytes = (kLora + 2) * 4;  // one request's acc[512], m, L
     if (threadIdx.x == 0) {  // W_UV is a weight: no kernel writes it, so it may load before pdl_wait
         mbar_init(bar, 1);
+        if (kCl > 1) mbar_init(bar + 1, 1);
         fence_mbar_init();
         mbar_arrive_expect_tx(bar, Sh::kWBytes);
         tma_load_3d(w_s, &tmap_kvb, bar, 0, h * kKvbHead + kNope + q * Sh::kVRows, 0, kCacheEvictLast);
+        if (kCl > 1) mbar_arrive_expect_tx(bar + 1, (uint32_t)(kCl - 1) * (uint32_t)nreq * kPushBytes);
     }
+    if (kCl > 1) cluster_sync_all();  // every rank's bar[1] is initialised before any rank pushes into it
     pdl_trigger();
     pdl_wait();  // partials from K2, plan from K1
     MLA_TL_WAITED(2);
@@ -248,11 +264,20 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         if (kCl == 1) {
             store_ml(r, m, L);
             store_oc(r, acc, L > 0.f ? 1.f / L : 0.f);
-        } else {
-            float* x = xch + r * (kLora + 4);
+        } else {  // into slot [q][r] of xch in this CTA and in every other rank of the cluster
+            float* x = xch + (q * kRq + r) * (kLora + 4);
 #pragma unroll
             for (int k = 0; k < 4; ++k) *reinterpret_cast<float4*>(x + 4 * lane + 128 * k) = acc[k];
             if (lane == 0) { x[kLora] = m; x[kLora + 1] = L; }
+            const uint32_t xl = smem_u32(x), bl = smem_u32(bar + 1);
+#pragma unroll
+            for (int c = 0; c < kCl; ++c) {
+                if (c == q) continue;
+                const uint32_t xr = dsmem_addr(xl, (uint32_t)c), br = dsmem_addr(bl, (uint32_t)c);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) dsmem_push4(xr + (uint32_t)(4 * lane + 128 * k) * 4u, acc[k], br);
+                if (lane == 0) dsmem_push2(xr + (uint32_t)kLora * 4u, make_float2(m, L), br);
+            }
         }
     };
 
@@ -310,22 +335,32 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
 
     if (kCl > 1) {
         // The cluster's kCl folds of each request, combined in rank order: every CTA
-        // reads all ranks' (acc, m, L) from distributed shared memory, so each holds the
-        // whole o_c for its slice of W_UV. Warp w combines requests w and w + 8.
-        cluster_sync_all();  // every rank has published
-        const uint32_t xbase = smem_u32(xch);
+        // holds all ranks' (acc, m, L) in its own xch once the other ranks' pushes have
+        // landed (bar[1]), so each has the whole o_c for its slice of W_UV. Warp w
+        // combines requests w and w + 8.
+        __syncthreads();  // this CTA's own slot, written by its warps
+        MLA_TL_MARK(2, 4);
+        {
+            int dummy = 0;
+            if (!mbar_wait(bar + 1, 0, &dummy, p.error_word)) return;
+        }
 #pragma unroll 1
         for (int rr = 0; rr < 2; ++rr) {
             const int r = warp + kWarps * rr;
             if (r >= nreq) continue;
-            const uint32_t off = (uint32_t)(r * (kLora + 4)) * 4u;
             float2 ml[kCl];
-            float gm = -INFINITY;
+            float4 xs[kCl][4];
 #pragma unroll
             for (int c = 0; c < kCl; ++c) {
-                ml[c] = dsmem_ld2(dsmem_addr(xbase + off + kLora * 4u, (uint32_t)c));
-                if (ml[c].y > 0.f) gm = fmaxf(gm, ml[c].x);
+                const float* x = xch + (c * kRq + r) * (kLora + 4);
+                ml[c] = make_float2(x[kLora], x[kLora + 1]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) xs[c][k] = *reinterpret_cast<const float4*>(x + 4 * lane + 128 * k);
             }
+            float gm = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kCl; ++c)
+                if (ml[c].y > 0.f) gm = fmaxf(gm, ml[c].x);
             float Lt = 0.f;
             float4 tot[4];
 #pragma unroll
@@ -334,10 +369,9 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
             for (int c = 0; c < kCl; ++c) {
                 const float wv = ml[c].y > 0.f ? exp2f(ml[c].x - gm) : 0.f;
                 Lt = fmaf(wv, ml[c].y, Lt);
-                const uint32_t src = dsmem_addr(xbase + off, (uint32_t)c);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    const float4 x = dsmem_ld4(src + (uint32_t)(4 * lane + 128 * k) * 4u);
+                    const float4 x = xs[c][k];
                     tot[k].x = fmaf(wv, x.x, tot[k].x); tot[k].y = fmaf(wv, x.y, tot[k].y);
                     tot[k].z = fmaf(wv, x.z, tot[k].z); tot[k].w = fmaf(wv, x.w, tot[k].w);
                 }
@@ -345,10 +379,9 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
             store_ml(r, gm, Lt);
             store_oc(r, tot, Lt > 0.f ? 1.f / Lt : 0.f);
         }
-        cluster_sync_all();  // no rank reuses or releases its exchange buffer while others read it
     }
     __syncthreads();
-    MLA_TL_MARK(2, 4);  // merge done
+    MLA_TL_MARK(2, 5);  // merge done
     bool w_ok;
     {
         int dummy = 0;
@@ -392,30 +425,34 @@ __device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const
     for (int task = threadIdx.x; task < nreq * kLines; task += k3::kThreads) {
         const int b = b0 + task / kLines;
         const int line = q * kLines + task % kLines;  // v = 2 line, 2 line + 1
-        float m[kMaxRanks], L[kMaxRanks];
+        // every shard's (m, L) line and y line, loaded together, then waited on
+        const ulonglong2* base[kMaxRanks];
+        ulonglong2 mlv[kMaxRanks], yv[kMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r) {
+            if (r >= p.world) break;
+            base[r] = ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h);
+            mlv[r] = ld_line(base[r] + kV / 2);
+            yv[r] = ld_line(base[r] + line);
+        }
         float gm = -INFINITY;
 #pragma unroll
         for (int r = 0; r < kMaxRanks; ++r) {
-            m[r] = -INFINITY;
-            L[r] = 0.f;
-            if (r < p.world && ok) {
-                ok = poll_line(ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h) + kV / 2, step, m[r],
-                               L[r], t0, limit_ns);
-                gm = fmaxf(gm, m[r]);
-            }
+            if (r >= p.world) break;
+            if (ok) ok = wait_line(base[r] + kV / 2, step, mlv[r], t0, limit_ns) &&
+                         wait_line(base[r] + line, step, yv[r], t0, limit_ns);
+            gm = fmaxf(gm, line_lo(mlv[r]));
         }
         float a0 = 0.f, a1 = 0.f, W = 0.f;
 #pragma unroll
         for (int r = 0; r < kMaxRanks; ++r) {
-            if (r >= p.world || !ok || !(L[r] > 0.f)) continue;  // an empty shard contributes nothing
-            float y0, y1;
-            ok = poll_line(ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h) + line, step, y0, y1, t0,
-                           limit_ns);
-            if (!ok) continue;
-            const float w = L[r] * exp2f(m[r] - gm);
+            if (r >= p.world || !ok) break;
+            const float Lr = line_hi(mlv[r]);
+            if (!(Lr > 0.f)) continue;  // an empty shard contributes nothing
+            const float w = Lr * exp2f(line_lo(mlv[r]) - gm);
             W += w;
-            a0 = fmaf(w, y0, a0);
-            a1 = fmaf(w, y1, a1);
+            a0 = fmaf(w, line_lo(yv[r]), a0);
+            a1 = fmaf(w, line_hi(yv[r]), a1);
         }
         const float inv = W > 0.f ? 1.f / W : 0.f;
         // after a timeout the remaining tasks poll nothing and write zeros
@@ -463,7 +500,6 @@ __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const u
             mma16816(acc[mt][1], al, b10, b11);
         }
     }
-    MLA_TL_MARK(2, 5);  // W_UV MMAs done
     // The thread holds v, v + 1 of requests 16 mt + g (acc[..][0..1]) and 16 mt + g + 8 (acc[..][2..3]).
     const int v_base = q * Sh::kVRows;
 #pragma unroll
@@ -546,6 +582,7 @@ __global__ void __launch_bounds__(256) k4_combine_shards(const float* __restrict
 // needs until they carry this step's number (bounded by exchange_timeout_us; on
 // timeout the block records MLA_DEV_PEER_TIMEOUT and writes zeros). The last block
 // to finish advances the buffer's step counter.
+template <int kW>  // an upper bound on p.world (2, 4 or 8): sizes the per-thread line arrays
 __global__ void __launch_bounds__(256) k4_exchange_combine(const MlaDecodeParams p) {
     MLA_TL_SCOPE(3);
     const int b = blockIdx.x;
@@ -567,34 +604,42 @@ __global__ void __launch_bounds__(256) k4_exchange_combine(const MlaDecodeParams
     const uint64_t limit_ns = (uint64_t)(p.exchange_timeout_us > 0 ? p.exchange_timeout_us : 2000000) * 1000ull;
     const uint64_t t0 = globaltimer_ns();
     bool ok = true;
-    float m[kMaxRanks], L[kMaxRanks];
+    // every shard's (m, L) line and the four y lines of this thread, loaded together,
+    // then waited on
+    const ulonglong2* base[kW];
+    ulonglong2 mlv[kW], yv[kW][4];
+#pragma unroll
+    for (int r = 0; r < kW; ++r) {
+        if (r >= p.world) break;
+        base[r] = ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h);
+        mlv[r] = ld_line(base[r] + kV / 2);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) yv[r][k] = ld_line(base[r] + v0 / 2 + k);
+    }
     float gm = -INFINITY;
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-        m[r] = -INFINITY;
-        L[r] = 0.f;
-        if (r < p.world && ok) {
-            const ulonglong2* ln = ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h);
-            ok = poll_line(ln + kV / 2, step, m[r], L[r], t0, limit_ns);
-            gm = fmaxf(gm, m[r]);
-        }
+    for (int r = 0; r < kW; ++r) {
+        if (r >= p.world) break;
+        if (ok) ok = wait_line(base[r] + kV / 2, step, mlv[r], t0, limit_ns);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (ok) ok = wait_line(base[r] + v0 / 2 + k, step, yv[r][k], t0, limit_ns);
+        gm = fmaxf(gm, line_lo(mlv[r]));
     }
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float W = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r) {
-        if (r >= p.world || !ok) continue;
-        if (!(L[r] > 0.f)) continue;  // an empty shard contributes nothing
-        const ulonglong2* ln = ex_lines(own, ex, p.world, p.exchange_batch, step & 1u, r, b, h) + v0 / 2;
-        float y[8];
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-            if (ok) ok = poll_line(ln + k, step, y[2 * k], y[2 * k + 1], t0, limit_ns);
-        if (!ok) continue;
-        const float w = L[r] * exp2f(m[r] - gm);
+    for (int r = 0; r < kW; ++r) {
+        if (r >= p.world || !ok) break;
+        const float Lr = line_hi(mlv[r]);
+        if (!(Lr > 0.f)) continue;  // an empty shard contributes nothing
+        const float w = Lr * exp2f(line_lo(mlv[r]) - gm);
         W += w;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] = fmaf(w, y[k], acc[k]);
+        for (int k = 0; k < 4; ++k) {
+            acc[2 * k] = fmaf(w, line_lo(yv[r][k]), acc[2 * k]);
+            acc[2 * k + 1] = fmaf(w, line_hi(yv[r][k]), acc[2 * k + 1]);
+        }
     }
     if (!ok) {
         record_error(p.error_word, MLA_DEV_PEER_TIMEOUT);
@@ -618,7 +663,9 @@ __global__ void __launch_bounds__(256) k4_exchange_combine(const MlaDecodeParams
 }
 
 cudaError_t launch_exchange_combine(const MlaDecodeParams& p, cudaStream_t stream) {
-    return launch_pdl(k4_exchange_combine, dim3(p.batch), dim3(256), 0, stream, p);
+    if (p.world <= 2) return launch_pdl(k4_exchange_combine<2>, dim3(p.batch), dim3(256), 0, stream, p);
+    if (p.world <= 4) return launch_pdl(k4_exchange_combine<4>, dim3(p.batch), dim3(256), 0, stream, p);
+    return launch_pdl(k4_exchange_combine<kMaxRanks>, dim3(p.batch), dim3(256), 0, stream, p);
 }
 
 cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, void* out, int64_t out_stride,
