@@ -266,18 +266,22 @@ def _peer_worker(rank, world, port, T, q_out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_exchange_two_gpus():
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange_gpus(world):
+    """One process per GPU (2, and 4 where the box has them), buffers mapped through IPC."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     qq = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, 9000, qq)) for r in range(2)]
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, 9000, qq)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted([qq.get(timeout=300) for _ in range(2)], key=lambda x: x[0])
+    res = sorted([qq.get(timeout=300) for _ in range(world)], key=lambda x: x[0])
     for p in procs:
         p.join(timeout=120)
     assert all(same is True for _, same, _ in res), [(r, s) for r, s, _ in res]
     assert all(p.exitcode == 0 for p in procs)
-    assert np.array_equal(res[0][2], res[1][2])
+    assert all(np.array_equal(res[0][2], x[2]) for x in res[1:])
