@@ -116,13 +116,9 @@ __device__ __forceinline__ void fold_partial(float2 ml, const float4 (&a)[4], fl
 // at a time. (Six or eight at a time measured no faster than four: at one request
 // the fold is bound by the bytes each of the 64 cluster SMs pulls, not by rounds.)
 template <int kDepth = 4>
-__device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
-                                               int b, int h, int first, int last, int stride, int lane, float& m,
-                                               float& L, float4 (&acc)[4]) {
-    m = -INFINITY;
-    L = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+__device__ __forceinline__ void fold_range(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
+                                           int b, int h, int first, int last, int stride, int lane, float& m, float& L,
+                                           float4 (&acc)[4]) {
     for (int cc = first; cc <= last; cc += kDepth * stride) {
         float2 ml[kDepth];
         float4 a[kDepth][4];
@@ -133,6 +129,17 @@ __device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml
         for (int j = 0; j < kDepth; ++j)
             if (cc + j * stride <= last) fold_partial(ml[j], a[j], m, L, acc);
     }
+}
+
+template <int kDepth = 4>
+__device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
+                                               int b, int h, int first, int last, int stride, int lane, float& m,
+                                               float& L, float4 (&acc)[4]) {
+    m = -INFINITY;
+    L = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    fold_range<kDepth>(part_ml, part_acc, b, h, first, last, stride, lane, m, L, acc);
 }
 
 // Address of element (row, col) of a [rows][512] bf16 matrix stored as 1024-byte
@@ -289,6 +296,46 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     const int wpr = nreq == 1 ? 8 : nreq == 2 ? 4 : nreq <= 4 ? 2 : 1;
     const int groups = kWarps / wpr, gi = warp / wpr, wi = warp % wpr;
     const int iters = (nreq + groups - 1) / groups;
+    if (wpr == 1) {
+        // One warp per request (5 or more requests): two requests per pass, the first
+        // two partials of both loaded together, so that a warp's requests do not each
+        // wait for their own round trip in turn. Each request still folds its partials
+        // in plan order. (Three per request measured the same: the merge is bound by
+        // the L2 lines an SM keeps in flight, ~30 GB/s per SM, not by round trips.)
+        const int first = q, stride = kCl;
+#pragma unroll 1
+        for (int it = 0; it < iters; it += 2) {
+            int r2[2], c0[2] = {0, 0}, c1[2] = {-1, -1};
+            bool v[2];
+            float2 ml[2][2];
+            float4 a[2][2][4];
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+                r2[x] = gi + (it + x) * groups;
+                v[x] = it + x < iters && part_range(r2[x], c0[x], c1[x]) && c0[x] + first <= c1[x];
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+                    if (v[x] && c0[x] + first + j * stride <= c1[x])
+                        load_partial(part_ml, part_acc, b0 + r2[x], h, c0[x] + first + j * stride, lane, ml[x][j],
+                                     a[x][j]);
+            }
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+                float m = -INFINITY, L = 0.f;
+                float4 acc[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (v[x]) {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        if (c0[x] + first + j * stride <= c1[x]) fold_partial(ml[x][j], a[x][j], m, L, acc);
+                    fold_range(part_ml, part_acc, b0 + r2[x], h, c0[x] + first + 2 * stride, c1[x], stride, lane, m,
+                               L, acc);
+                }
+                if (r2[x] < nreq && it + x < iters) publish(r2[x], m, L, acc);
+            }
+        }
+    } else {
 #pragma unroll 1
     for (int it = 0; it < iters; ++it) {  // uniform trip count: the barriers below are CTA-wide
         const int r = gi + it * groups;
@@ -300,10 +347,6 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
             merge_partials(part_ml, part_acc, b0 + r, h, c0 + first, c1, kCl * wpr, lane, m, L, acc);
         else
             for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (wpr == 1) {
-            if (r < nreq) publish(r, m, L, acc);
-            continue;
-        }
         if (lane == 0) { red_ml[warp][0] = m; red_ml[warp][1] = L; }
 #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -333,6 +376,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         __syncthreads();
     }
 
+    }
     if (kCl > 1) {
         // The cluster's kCl folds of each request, combined in rank order: every CTA
         // holds all ranks' (acc, m, L) in its own xch once the other ranks' pushes have
