@@ -260,8 +260,11 @@ class MlaDecodeAttention:
             raise ValueError(f"the in-library projection takes at most {native.MAX_PROJECT_BATCH} requests")
 
     def project(self, x_n: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """q = R(W_q x_n), kv_a = R(W_kv_a x_n) as views of one bf16 GEMM output."""
-        qkv = torch.nn.functional.linear(x_n, self.w_qkv)
+        """q = R(W_q x_n), kv_a = R(W_kv_a x_n) as views of one bf16 GEMM output.
+        (torch.mm against the transposed view: at B = 256 with cold weights cuBLAS runs
+        it in 13.3 us against 17.1 us for F.linear; inside the pipelined decode loop the
+        two measured the same within run-to-run noise.)"""
+        qkv = torch.mm(x_n, self.w_qkv.t())
         nq = self.cfg.heads * self.cfg.q_head_dim
         return qkv[:, :nq], qkv[:, nq:]
 
