@@ -200,7 +200,7 @@ def cpu_oracle_sample(name: str, budget_s: float, faithful: bool) -> dict:
     cos, sin = cfg.cos_sin(max(lengths) + 8)
     done_bytes, done_req, t_total = 0, 0, 0.0
     i = 0
-    while t_total < budget_s and done_req < 4 * len(lengths):
+    while t_total < budget_s and done_req < 64 * len(lengths):
         b = i % len(lengths)
         T = lengths[b]
         rows = O.bf16_round(rng.standard_normal((T, 576), dtype=np.float32))
@@ -611,7 +611,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="config5a", choices=sorted(workloads.WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="CPU baseline sample: seconds of oracle work on the host cores (about 10-30 s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="config5b on N > 1 GPUs: how the shard partials move (peer memory or NCCL)")
