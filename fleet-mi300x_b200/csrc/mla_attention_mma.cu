@@ -108,14 +108,14 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     pdl_trigger();
     pdl_wait();  // the plan, absorbed queries and new rows come from K1
     MLA_TL_WAITED(1);
-    const int64_t U = cum[p.batch];
-    const int G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
     const int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan
                                                   // has more CTAs than the grid)
+    const int G = reinterpret_cast<const PlanHeader*>(wsb + ws.plan)->G;
+    const PlanEntry pe = reinterpret_cast<const PlanEntry*>(wsb + ws.plan + sizeof(PlanHeader))[
+        vc < p.num_ctas ? vc : 0];  // loaded with G: one round trip to the plan
     const bool leader = w == 0 && lane == 0;
 
     if (vc < G) {
-        const int64_t u_begin = plan_begin(vc, U, G), u_end = plan_begin(vc + 1, U, G);
         if (leader) {
             for (int i = 0; i < kNSlot; ++i) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], kGroupWarps); }
             S.abort = 0;
@@ -141,13 +141,14 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         };
         if (leader) {
             prefetch_tmap(&tmap_kv);
-            la.init(cum, p.seq_lens, p.batch, u_begin, u_end, new_row_count(p));
+            la.init_at(cum, p.seq_lens, p.batch, pe, new_row_count(p));
             while (issued < kNSlot && la.valid()) issue_next();
+            MLA_TL_MARK(1, 4);  // first half pages requested
         }
         __syncwarp();  // the leader's warp reconverges before its first .aligned MMA
 
         TileCursor cur;
-        cur.init(cum, p.seq_lens, p.batch, u_begin, u_end, new_row_count(p));
+        cur.init_at(cum, p.seq_lens, p.batch, pe, new_row_count(p));
         const int g = lane >> 2, t4 = lane & 3;
         const int m8 = lane >> 3, r8 = lane & 7;  // ldmatrix: matrix index, row in matrix
         const uint32_t tile_addr = smem_u32(tile_s), p_addr = smem_u32(p_s);
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 const bool tile_first = first && hh == 0;
                 const uint32_t slot = i % kNSlot;
                 if (!mbar_wait(&S.full[slot], (i / kNSlot) & 1, abort, p.error_word)) { ok = false; break; }
+                if (i == 0 && w == 0) MLA_TL_MARK(1, 5);  // first half page landed
                 const uint32_t tbase = tile_addr + slot * kTileBytes;
 
                 // ---- partial scores over this warp's 144 columns, the 32 tokens ----

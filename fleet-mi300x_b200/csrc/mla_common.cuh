@@ -33,14 +33,28 @@ constexpr float kLog2e = 1.4426950408889634f;
 // ---------------------------------------------------------------------------
 // Workspace layout (bytes, each region 256-byte aligned).
 //   tiles_cum  int32 [batch + 1]          prefix sum of 64-token tiles per request (split plan)
+//   plan       PlanHeader, PlanEntry [num_ctas]   the split plan per CTA, ready to use (K1 writes it)
 //   qa         bf16  [batch][16][576]     absorbed query q_c (512) | roped q_pe (64), per head
 //   part_ml    f32   [slots][16][2]       split partial: running max (log2 domain), sum of exps
 //   part_acc   f32   [slots][16][512]     split partial: unnormalised sum_t p_t * c_t
 // slots = num_ctas + batch: CTA c writes the partial of request b at slot c + b.
 // ---------------------------------------------------------------------------
 struct WsLayout {
-    uint64_t tiles_cum, qa, part_ml, part_acc, qkv, total;
+    uint64_t tiles_cum, plan, qa, part_ml, part_acc, qkv, total;
     int32_t slots;
+};
+
+// The split plan as K1's planner leaves it for the split-KV kernel: the total tile
+// count U, the number of CTAs with work G = min(U, num_ctas), and per plan CTA its
+// tile range, its first request b (the largest b with cum[b] <= u_begin) and that
+// request's cum[b], cum[b + 1], so that the kernel starts without a search.
+struct PlanHeader {
+    int64_t U;
+    int32_t G, pad;
+};
+struct PlanEntry {
+    int64_t u_begin, u_end;
+    int32_t b, cb0, cb1, pad;
 };
 
 __host__ __device__ inline uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
@@ -52,6 +66,7 @@ __host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with
     w.slots = num_ctas + batch;
     uint64_t off = 0;
     w.tiles_cum = off; off = align256(off + uint64_t(batch + 1) * 4);
+    w.plan = off;      off = align256(off + sizeof(PlanHeader) + uint64_t(num_ctas) * sizeof(PlanEntry));
     w.qa = off;        off = align256(off + uint64_t(batch) * kQRows * kRow * 2);
     w.part_ml = off;   off = align256(off + uint64_t(w.slots) * kHeads * 2 * 4);
     w.part_acc = off;  off = align256(off + uint64_t(w.slots) * kHeads * kLora * 4);

@@ -53,9 +53,12 @@ __device__ __forceinline__ bool request_ok(const MlaDecodeParams& p, int b) {
 
 // Prefix sum of tiles per request (one CTA). Invalid positions are recorded
 // and given zero tiles, so no later kernel reads outside the block table.
-__device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum) {
+// cum_s (kCumSmem entries of shared memory) receives a copy when batch + 1 fits.
+constexpr int kCumSmem = (kK1SmemBytes - 1024) / 4;  // what is left after aligning the base to 1024 bytes
+__device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum, int32_t* cum_s) {
     __shared__ int32_t warp_tot[kK1Threads / 32];
     __shared__ int32_t carry;
+    const bool stage = p.batch + 1 <= kCumSmem;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
     for (int base = 0; base < p.batch; base += kK1Threads) {
@@ -76,12 +79,51 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum) {
         __syncthreads();
         int before = carry;
         for (int w = 0; w < warp; ++w) before += warp_tot[w];
-        if (b < p.batch) cum[b] = before + incl - n;
+        if (b < p.batch) {
+            cum[b] = before + incl - n;
+            if (stage) cum_s[b] = before + incl - n;
+        }
         __syncthreads();
         if (threadIdx.x == kK1Threads - 1) carry = before + incl;
         __syncthreads();
     }
-    if (threadIdx.x == 0) cum[p.batch] = carry;
+    if (threadIdx.x == 0) {
+        cum[p.batch] = carry;
+        if (stage) cum_s[p.batch] = carry;
+    }
+}
+
+// Per plan CTA of the split-KV kernel: its tile range and first request (the same
+// search TileCursor::init does, here once per CTA instead of in every thread of
+// the split-KV kernel after its grid-dependency wait).
+__device__ void plan_entries(const MlaDecodeParams& p, const int32_t* cum, const int32_t* cum_s, char* plan) {
+    __syncthreads();  // cum / cum_s complete
+    const bool staged = p.batch + 1 <= kCumSmem;
+    const int32_t* c = staged ? cum_s : cum;
+    const int64_t U = c[p.batch];
+    const int G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
+    if (threadIdx.x == 0) {
+        PlanHeader* hdr = reinterpret_cast<PlanHeader*>(plan);
+        hdr->U = U;
+        hdr->G = G;
+        hdr->pad = 0;
+    }
+    PlanEntry* ent = reinterpret_cast<PlanEntry*>(plan + sizeof(PlanHeader));
+    for (int vc = threadIdx.x; vc < G; vc += blockDim.x) {
+        PlanEntry e;
+        e.u_begin = plan_begin(vc, U, G);
+        e.u_end = plan_begin(vc + 1, U, G);
+        int lo = 0, hi = p.batch;  // largest b with cum[b] <= u_begin (skips empty requests)
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (c[mid] <= e.u_begin) lo = mid; else hi = mid;
+        }
+        e.b = lo;
+        e.cb0 = c[lo];
+        e.cb1 = c[lo + 1];
+        e.pad = 0;
+        ent[vc] = e;
+    }
 }
 
 // One warp: q_pe RoPE of request b, then (unless the call stores no row)
@@ -157,7 +199,10 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
     pdl_trigger();  // K2 may become resident now; it waits for this grid before reading its output
 
     if (cta == g.total - 1) {
-        plan_scan(p, reinterpret_cast<int32_t*>(wsb + ws.tiles_cum));
+        int32_t* cum = reinterpret_cast<int32_t*>(wsb + ws.tiles_cum);
+        int32_t* cum_s = reinterpret_cast<int32_t*>(smem);
+        plan_scan(p, cum, cum_s);
+        plan_entries(p, cum, cum_s, wsb + ws.plan);
         return;
     }
 

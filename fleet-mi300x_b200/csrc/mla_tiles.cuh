@@ -27,6 +27,12 @@ struct TileCursor {
         }
         b = lo; cb0 = cum[b]; cb1 = cum[b + 1];
     }
+    // The same start from a plan entry (no search).
+    __device__ void init_at(const int32_t* cum_, const int32_t* sl, int B, const PlanEntry& e, int extra_ = 1) {
+        cum = cum_; seq_lens = sl; batch = B; u = e.u_begin; u_begin = e.u_begin; u_end = e.u_end; seg = 0;
+        extra = extra_;
+        b = e.b; cb0 = e.cb0; cb1 = e.cb1;
+    }
     __device__ bool valid() const { return u < u_end; }
     __device__ int page_index() const { return (int)(u - cb0); }
     __device__ int tokens() const {  // valid tokens in this 64-token tile

@@ -51,6 +51,7 @@ def test_params_struct_layout(lib):
 def expected_workspace(batch: int, ctas: int) -> int:
     a = lambda x: (x + 255) // 256 * 256
     off = a((batch + 1) * 4)
+    off = a(off + 16 + ctas * 32)  # the split plan: header (U, G) and one 32-byte entry per CTA
     off = a(off + batch * 16 * 576 * 2)
     off = a(off + (ctas + batch) * 16 * 2 * 4)
     off = a(off + (ctas + batch) * 16 * 512 * 4)
