@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         volatile int* abort = &S.abort;
 
         // The leader's look-ahead over half pages (loads run two half pages ahead).
-        TileCursor la;
+        TileCursor la{};
         int la_half = 0;
         uint32_t issued = 0;
         auto issue_next = [&]() {
