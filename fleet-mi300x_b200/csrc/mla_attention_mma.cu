@@ -54,6 +54,8 @@ constexpr int kSPitch = 40;                           // floats per head row of 
                                                       // (64-bit accesses by a half-warp hit 32 banks)
 constexpr int kSPartBytes = kGroupWarps * kHeads * kSPitch * 4;  // 10,240
 constexpr int kPBytes = kHeads * 64;                  // [16 heads][32 tokens] bf16, 64-byte rows, swizzled
+constexpr int kPrePlan = kThreads;                    // batches up to this plan before the K1 wait
+constexpr int kPreSlots = 1;                          // half pages a group requests before the K1 wait
 
 struct GroupSmem {
     uint64_t full[kNSlot], empty[kNSlot];
@@ -106,49 +108,108 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     float* part_acc = reinterpret_cast<float*>(wsb + ws.part_acc);
 
     pdl_trigger();
-    pdl_wait();  // the plan, absorbed queries and new rows come from K1
-    MLA_TL_WAITED(1);
     const int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan
                                                   // has more CTAs than the grid)
-    const int G = reinterpret_cast<const PlanHeader*>(wsb + ws.plan)->G;
-    const PlanEntry pe = reinterpret_cast<const PlanEntry*>(wsb + ws.plan + sizeof(PlanHeader))[
-        vc < p.num_ctas ? vc : 0];  // loaded with G: one round trip to the plan
     const bool leader = w == 0 && lane == 0;
 
-    if (vc < G) {
-        if (leader) {
-            for (int i = 0; i < kNSlot; ++i) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], kGroupWarps); }
-            S.abort = 0;
-            fence_mbar_init();
+    // The leader's look-ahead over half pages (loads run two half pages ahead).
+    TileCursor la{};
+    int la_half = 0;
+    uint32_t issued = 0;
+    auto issue_next = [&]() {
+        int page = p.block_table[(int64_t)la.b * p.max_blocks + la.page_index()];
+        if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
+        const uint32_t slot = issued % kNSlot;
+        mbar_arrive_expect_tx(&S.full[slot], kTileBytes);
+        tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.full[slot], 0, kHalf * la_half, 0, page,
+                    kCacheEvictFirst);
+        ++issued;
+        if (la_half == 0 && la.tokens() > kHalf) la_half = 1;
+        else { la_half = 0; la.next(); }
+    };
+    // Would the half page the leader loads next hold the row K1 appends in this step?
+    auto holds_new_row = [&]() -> bool {
+        if (!new_row_count(p)) return false;
+        const int row0 = la.page_index() * kPage + kHalf * la_half, nr = p.seq_lens[la.b];
+        return nr >= row0 && nr < row0 + kHalf;
+    };
+    auto init_group = [&]() {
+        for (int i = 0; i < kNSlot; ++i) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], kGroupWarps); }
+        S.abort = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmap_kv);
+    };
+
+    // Batches of at most kPrePlan requests: the split plan from the step's inputs
+    // (row counts, positions, limits; complete before K1 started) before the wait
+    // on K1. It equals K1's plan (the same rule, plan_tiles), and the leader already
+    // requests its first half pages, except one that holds the row K1 appends, so
+    // that those copies overlap K1. Larger batches read K1's plan after the wait.
+    __shared__ int32_t pre_cum[kPrePlan + 1];
+    __shared__ int32_t pre_tot[kThreads / 32];
+    const bool pre = p.batch <= kPrePlan;
+    PlanEntry pe{};
+    int G = 0;
+    const int32_t* cumv = cum;  // the prefix sums the cursors walk
+    if (pre) {
+        const int b = threadIdx.x;
+        const int n = b < p.batch ? plan_tiles(p, b) : 0;
+        int incl = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
         }
-        named_bar_sync(bar_id, kGroupWarps * 32);
+        if (lane == 31) pre_tot[warp] = incl;
+        __syncthreads();
+        int before = 0;
+        for (int v = 0; v < warp; ++v) before += pre_tot[v];
+        if (b < p.batch) pre_cum[b] = before + incl - n;
+        if (threadIdx.x == kThreads - 1) pre_cum[p.batch] = before + incl;
+        __syncthreads();
+        cumv = pre_cum;
+        const int64_t U = pre_cum[p.batch];
+        G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
+        if (vc < G) {
+            pe.u_begin = plan_begin(vc, U, G);
+            pe.u_end = plan_begin(vc + 1, U, G);
+            int lo = 0, hi = p.batch;  // largest b with cum[b] <= u_begin (skips empty requests)
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (pre_cum[mid] <= pe.u_begin) lo = mid; else hi = mid;
+            }
+            pe.b = lo;
+            pe.cb0 = pre_cum[lo];
+            pe.cb1 = pre_cum[lo + 1];
+            if (leader) {
+                init_group();
+                la.init_at(cumv, p.seq_lens, p.batch, pe, new_row_count(p));
+                while (issued < kPreSlots && la.valid() && !holds_new_row()) issue_next();
+            }
+        }
+    }
+    pdl_wait();  // the plan, absorbed queries and new rows come from K1
+    MLA_TL_WAITED(1);
+    if (!pre) {
+        G = reinterpret_cast<const PlanHeader*>(wsb + ws.plan)->G;
+        pe = reinterpret_cast<const PlanEntry*>(wsb + ws.plan + sizeof(PlanHeader))[
+            vc < p.num_ctas ? vc : 0];  // loaded with G: one round trip to the plan
+    }
+
+    if (vc < G) {
+        if (leader && !pre) init_group();
+        named_bar_sync(bar_id, kGroupWarps * 32);  // barriers initialised
         volatile int* abort = &S.abort;
 
-        // The leader's look-ahead over half pages (loads run two half pages ahead).
-        TileCursor la{};
-        int la_half = 0;
-        uint32_t issued = 0;
-        auto issue_next = [&]() {
-            int page = p.block_table[(int64_t)la.b * p.max_blocks + la.page_index()];
-            if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
-            const uint32_t slot = issued % kNSlot;
-            mbar_arrive_expect_tx(&S.full[slot], kTileBytes);
-            tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.full[slot], 0, kHalf * la_half, 0, page,
-                        kCacheEvictFirst);
-            ++issued;
-            if (la_half == 0 && la.tokens() > kHalf) la_half = 1;
-            else { la_half = 0; la.next(); }
-        };
         if (leader) {
-            prefetch_tmap(&tmap_kv);
-            la.init_at(cum, p.seq_lens, p.batch, pe, new_row_count(p));
+            if (!pre) la.init_at(cumv, p.seq_lens, p.batch, pe, new_row_count(p));
             while (issued < kNSlot && la.valid()) issue_next();
             MLA_TL_MARK(1, 4);  // first half pages requested
         }
         __syncwarp();  // the leader's warp reconverges before its first .aligned MMA
 
         TileCursor cur;
-        cur.init_at(cum, p.seq_lens, p.batch, pe, new_row_count(p));
+        cur.init_at(cumv, p.seq_lens, p.batch, pe, new_row_count(p));
         const int g = lane >> 2, t4 = lane & 3;
         const int m8 = lane >> 3, r8 = lane & 7;  // ldmatrix: matrix index, row in matrix
         const uint32_t tile_addr = smem_u32(tile_s), p_addr = smem_u32(p_s);

@@ -129,6 +129,19 @@ __device__ __forceinline__ int rope_position(const MlaDecodeParams& p, int b) {
     return p.rope_pos ? p.rope_pos[b] : p.seq_lens[b];
 }
 
+// Request b is valid if its RoPE position lies in the tables and its rows
+// (cached + the new one, if this call stores it) fit its block-table row.
+__device__ __forceinline__ bool request_ok(const MlaDecodeParams& p, int b) {
+    const int rows = p.seq_lens[b], rp = rope_position(p, b);
+    return rows >= 0 && rp >= 0 && rp < p.max_pos && rows + new_row_count(p) <= p.max_blocks * kPage;
+}
+
+// 64-token tiles request b attends in the split plan: 0 for an invalid request
+// (K1's planner records it), so that no kernel reads outside the block table.
+__device__ __forceinline__ int plan_tiles(const MlaDecodeParams& p, int b) {
+    return request_ok(p, b) ? (p.seq_lens[b] + new_row_count(p) + kPage - 1) / kPage : 0;
+}
+
 // ---------------------------------------------------------------------------
 // Error word: first error wins.
 // ---------------------------------------------------------------------------

@@ -44,13 +44,6 @@ struct K1Grid {
     }
 };
 
-// Request b is valid if its RoPE position lies in the tables and its rows
-// (cached + the new one, if this call stores it) fit its block-table row.
-__device__ __forceinline__ bool request_ok(const MlaDecodeParams& p, int b) {
-    const int rows = p.seq_lens[b], rp = rope_position(p, b);
-    return rows >= 0 && rp >= 0 && rp < p.max_pos && rows + new_row_count(p) <= p.max_blocks * kPage;
-}
-
 // Prefix sum of tiles per request (one CTA). Invalid positions are recorded
 // and given zero tiles, so no later kernel reads outside the block table.
 // cum_s (kCumSmem entries of shared memory) receives a copy when batch + 1 fits.
@@ -66,7 +59,7 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum, int32_t* cum_s
         int n = 0;
         if (b < p.batch) {
             if (!request_ok(p, b)) record_error(p.error_word, MLA_DEV_BAD_POSITION);
-            else n = (p.seq_lens[b] + new_row_count(p) + kPage - 1) / kPage;
+            else n = plan_tiles(p, b);
         }
         int incl = n;
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
