@@ -33,6 +33,9 @@
 // page j as soon as all four warps have released it (mbarrier, bounded wait).
 // A page whose valid tokens fit in its first half is loaded and computed as
 // that half only.
+// Start: batches of up to 256 requests derive the split plan from the step's
+// inputs before the wait on K1 and request their first half page early (except
+// one holding the row K1 appends); larger batches read K1's per-CTA plan entry.
 #include <cuda.h>
 
 #include "mla_common.cuh"

@@ -6,13 +6,20 @@
 // (reference_decode.py:252-256). Partials are merged in CTA order, so the
 // result is bitwise reproducible for a fixed split plan.
 //
-// Grid: x = head, y = block of 16 requests; 256 threads. The CTA stages
-// W_UV[h] (kv_b rows [256h+128, 256h+256), 128 x 512 bf16) with one 128 KB
-// TMA box while it merges the partials of its requests into o_c (fp32), then
-// runs out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] as m16n8k16 MMAs with the 16
+// Grid: x = head (x cluster rank), y = block of requests; 256 threads. A CTA
+// stages its rows of W_UV[h] (kv_b rows [256h+128, 256h+256), 512 columns) with
+// one TMA box while it merges the partials of its requests into o_c (fp32), then
+// runs out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] as m16n8k16 MMAs with the
 // requests on M. o_c enters the MMA as a bf16 hi/lo pair (hi = bf16(o_c),
 // lo = bf16(o_c - hi)), two MMAs per step, so the product keeps ~16 mantissa
-// bits of o_c, as the reference's fp32 GEMV does.
+// bits of o_c, as the reference's fp32 GEMV does. Three forms (k3_launch):
+//   * cluster form, batches of at most 4 blocks of 16: a thread-block cluster of 4
+//     CTAs per (head, block), each folding a quarter of the partials and owning 32
+//     rows of W_UV; the folds meet through distributed shared memory;
+//   * plain form, one CTA per (head, block of 16), while that grid fits one wave;
+//   * plain form in blocks of 32 (two m16 tiles on one staged W_UV[h]) beyond.
+// Sequence-sharded steps end here too: shard_out (fp32 partials for a gather) or
+// the peer exchange (stores to every rank's buffer; the fused form also combines).
 #include <cuda.h>
 
 #include "mla_common.cuh"
@@ -48,8 +55,8 @@ constexpr int kClusterCtas = kK3ClusterCtas;  // cluster form: CTAs per (head, r
 __host__ __device__ inline bool k3_use_cluster(int batch) { return (batch + k3::kReq - 1) / k3::kReq <= 4; }
 
 // Thread-block cluster primitives (sm_90+): this CTA's rank, a cluster-wide
-// barrier with release/acquire ordering of shared memory, and loads from a
-// peer CTA's shared memory.
+// barrier with release/acquire ordering of shared memory, the cluster address of
+// a shared-memory location in a peer CTA, and stores into it.
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -62,17 +69,6 @@ __device__ __forceinline__ uint32_t dsmem_addr(uint32_t smem_addr, uint32_t rank
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
     return r;
-}
-__device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr) : "memory");
-    return v;
-}
-__device__ __forceinline__ float2 dsmem_ld2(uint32_t addr) {
-    float2 v;
-    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
-    return v;
 }
 // Stores into a peer CTA's shared memory that complete their bytes on an mbarrier
 // there (cluster addresses from dsmem_addr).
