@@ -127,3 +127,47 @@ class HostPipeline:
         """Block until every submitted step's R(out) is in host memory."""
         for st in (self.h2d, self.compute, self.d2h):
             st.synchronize()
+
+
+class HostStepGraph:
+    """One decode step of a layer from pinned host memory to pinned host memory as a
+    single CUDA graph: the copy of x_n in, the step (the kernels DecodeGraph runs) and
+    the copy of R(out) back, in order on one stream.
+
+    For latency-bound use (one request or a few), where HostPipeline's overlap of
+    neighbouring steps buys nothing and its hand-offs between three streams cost
+    more than the copies themselves. Write the next input into `x_host`, call
+    `replay()` on the current stream, synchronise, read `out_host`. The copies are
+    real copies on every replay (graph memcpy nodes from and to pinned memory).
+    """
+
+    def __init__(self, runner: MlaDecodeAttention, cache: PagedLatentCache, *, advance: bool = False):
+        cfg, dev, B = runner.cfg, runner.device, cache.batch
+        bf = torch.bfloat16
+        self.runner, self.cache = runner, cache
+        self.x_host = torch.zeros(B, cfg.hidden, dtype=bf).pin_memory()
+        self.out_host = torch.empty(B, cfg.heads * cfg.v_head, dtype=bf).pin_memory()
+        self.x_dev = torch.zeros(B, cfg.hidden, dtype=bf, device=dev)
+        self.out_dev = torch.empty(B, cfg.heads * cfg.v_head, dtype=bf, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            self._step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+            if advance:
+                cache.seq_lens.add_(1)
+
+    def _step(self) -> None:
+        self.x_dev.copy_(self.x_host, non_blocking=True)
+        self.runner(self.x_dev, self.cache, self.out_dev)
+        self.out_host.copy_(self.out_dev, non_blocking=True)
+
+    def replay(self) -> torch.Tensor:
+        """Queue the step on the current stream; returns `out_host` (valid once the
+        stream has reached this point)."""
+        self.graph.replay()
+        return self.out_host

@@ -83,3 +83,24 @@ def test_host_pipeline_matches_eager_loop(cuda_device):
     runner.check_errors()
     assert torch.equal(cache_p.seq_lens, cache_e.seq_lens)
     assert torch.equal(cache_p.pages, cache_e.pages)
+
+
+def test_host_step_graph_matches_eager_loop(cuda_device):
+    """The one-graph host step (copy in, step, copy out): every replay copies the new
+    host input and returns the eager step's output, and with advance=True the cache
+    grows as the eager loop's does."""
+    runner, cache_e = _runner_and_cache(cuda_device, seed=29)
+    cache_h = _clone(cache_e)
+    hsg = fleet.HostStepGraph(runner, cache_h, advance=True)
+    g = torch.Generator().manual_seed(9)
+    for k in range(4):
+        x = torch.randn(len(LENS), 2048, generator=g).to(torch.bfloat16)
+        hsg.x_host.copy_(x)
+        got = hsg.replay()
+        torch.cuda.synchronize(cuda_device)
+        want = runner(x.to(cuda_device), cache_e).cpu()
+        cache_e.advance()
+        assert torch.equal(got, want), f"step {k}"
+    runner.check_errors()
+    assert torch.equal(cache_h.seq_lens, cache_e.seq_lens)
+    assert torch.equal(cache_h.pages, cache_e.pages)
