@@ -33,7 +33,7 @@
 // page j as soon as all four warps have released it (mbarrier, bounded wait).
 // A page whose valid tokens fit in its first half is loaded and computed as
 // that half only.
-// Start: batches of up to 256 requests derive the split plan from the step's
+// Start: batches of up to 64 requests derive the split plan from the step's
 // inputs before the wait on K1 and request their first half page early (except
 // one holding the row K1 appends); larger batches read K1's per-CTA plan entry.
 #include <cuda.h>
@@ -57,7 +57,9 @@ constexpr int kSPitch = 40;                           // floats per head row of 
                                                       // (64-bit accesses by a half-warp hit 32 banks)
 constexpr int kSPartBytes = kGroupWarps * kHeads * kSPitch * 4;  // 10,240
 constexpr int kPBytes = kHeads * 64;                  // [16 heads][32 tokens] bf16, 64-byte rows, swizzled
-constexpr int kPrePlan = kThreads;                    // batches up to this plan before the K1 wait
+constexpr int kPrePlan = 64;                          // batches up to this plan before the K1 wait (larger
+                                                      // batches fill the SMs with K1, so K2 becomes resident
+                                                      // only as K1 ends, and the early scan would delay it)
 constexpr int kPreSlots = 1;                          // half pages a group requests before the K1 wait
 
 struct GroupSmem {
