@@ -198,9 +198,46 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     }
     if (kCl > 1) cluster_sync_all();  // every rank's bar[1] is initialised before any rank pushes into it
     pdl_trigger();
+
+    // The split plan's prefix sums of this block (cum_s) and the tile total. Batches
+    // of at most 64 requests derive them from the step's inputs before the wait (the
+    // rule K1's planner and K2 use, plan_tiles), so the first partial loads follow the
+    // wait directly; larger batches read K1's prefix sums after it.
+    __shared__ int32_t cum_s[kRq + 1];
+    __shared__ int32_t pre_tot[2];
+    __shared__ int64_t U_s;
+    constexpr int kPrePlan = 64;
+    const bool pre = p.batch <= kPrePlan;
+    if (pre) {
+        int n = 0, incl = 0;
+        if (threadIdx.x < kPrePlan) {
+            n = (int)threadIdx.x < p.batch ? plan_tiles(p, threadIdx.x) : 0;
+            incl = n;
+            const int ln = threadIdx.x & 31;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (ln >= o) incl += t;
+            }
+            if (ln == 31) pre_tot[threadIdx.x >> 5] = incl;
+        }
+        __syncthreads();
+        if (threadIdx.x < kPrePlan) {
+            const int before = (threadIdx.x >> 5) ? pre_tot[0] : 0;
+            const int b = (int)threadIdx.x;  // cum[b] = before + incl - n (the total for b >= batch)
+            if (b >= b0 && b <= b0 + kRq) cum_s[b - b0] = before + incl - n;
+            if (b == kPrePlan - 1 && b0 + kRq >= kPrePlan) cum_s[kPrePlan - b0] = before + incl;
+            if (b == 0) U_s = pre_tot[0] + pre_tot[1];
+        }
+    }
     pdl_wait();  // partials from K2, plan from K1
     MLA_TL_WAITED(2);
-    const int64_t U = cum[p.batch];
+    if (!pre) {
+        if (threadIdx.x == 0) U_s = cum[p.batch];
+        if (threadIdx.x <= kRq) cum_s[threadIdx.x] = cum[min(b0 + (int)threadIdx.x, p.batch)];
+    }
+    __syncthreads();
+    const int64_t U = U_s;
     const int G = (int)(U < 1 ? 1 : (U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas));
 
     // Peer exchange (p.world > 0): this step's number = steps completed + 1. The
@@ -215,9 +252,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     // ---- merge: o_c[r][l] = sum_c w_c acc_c[l] / sum_c w_c l_c ----
     // Every fold visits partials in plan-CTA order; requests without tiles (invalid
     // position) get a zero o_c.
-    __shared__ int32_t cum_s[kRq + 1];
     __shared__ float red_ml[kWarps][2];
-    if (threadIdx.x <= kRq) cum_s[threadIdx.x] = cum[min(b0 + (int)threadIdx.x, p.batch)];
     for (int i = threadIdx.x; i < (kRq - nreq) * (kLora / 8); i += kThreads) {  // rows past nreq: zero operands
         const int r = nreq + i / (kLora / 8), col = (i % (kLora / 8)) * 8;
         const uint32_t ahi0 = smem_u32(a_hi), alo0 = smem_u32(a_lo);
