@@ -462,6 +462,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         int dummy = 0;
         w_ok = mbar_wait(bar, 0, &dummy, p.error_word);
     }
+    if (kCl == 1) MLA_TL_MARK(2, 4);  // W_UV staged (the cluster form marks its published folds)
 
     // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] for this CTA's kVRows rows of v;
     // warp w owns v in [16w, 16w+16) ----

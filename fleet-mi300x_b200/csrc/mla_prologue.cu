@@ -6,10 +6,11 @@
 //    src/kernels/attention.h:62-90);
 //  * q_pe RoPE, bf16-rounded (reference_decode.py:235);
 //  * q-absorb q_c[h] = q_nope[h] @ W_UK[h] with fp32 accumulation
-//    (reference_decode.py:250, attention.h:171-216): per head an m16n8k16 GEMM
-//    [16 requests x 128] x [128 x 512] with W_UK[h] staged by one 128 KB TMA
-//    box; q_nope and W_UK are bf16 already, so the products are exact; q_c is
-//    stored bf16 as an operand of the attention kernel's score contraction;
+//    (reference_decode.py:250, attention.h:171-216): per (block of 64 requests,
+//    head, quarter of the latent) an m16n8k16 GEMM [64 requests x 128] x
+//    [128 x 128] against a 32 KB slice of W_UK[h] staged by one TMA box; q_nope
+//    and W_UK are bf16 already, so the products are exact; q_c is stored bf16 as
+//    an operand of the attention kernel's score contraction;
 //  * the split plan: prefix sum of 64-token tiles per request, consumed by K2/K3.
 //
 // One 1-D grid with two kinds of CTA:

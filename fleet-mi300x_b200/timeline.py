@@ -5,8 +5,8 @@ stamp `%globaltimer` per CTA at entry, after `griddepcontrol.wait` and at exit (
 warp to return), record the SM id, and set two kernel-specific marks:
 
     K1: mark1 = absorb MMAs stored, mark2 = per-request work (q_pe RoPE, new row) done
-    K3: mark1 = this CTA's folds published (cluster form: before waiting for the other
-        ranks' pushes), mark2 = o_c of the block complete
+    K3: mark1 = cluster form: this CTA's folds published (before waiting for the other
+        ranks' pushes); plain form: W_UV staged; mark2 = o_c of the block complete
 
 `python -m fleet-mi300x_b200.timeline config5b` (from the repository root, on a GPU)
 replays one workload's step as a CUDA graph with the L2 flushed before each replay and
