@@ -146,8 +146,8 @@ __device__ __forceinline__ uint32_t swz1024(uint32_t base, int row, int col) {
 
 template <int kCl, int kRq>
 __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const uint8_t* w_s, uint32_t ahi,
-                                               uint32_t alo, int warp, int lane, int q, int h, int b0, int nreq,
-                                               bool xmode, const ExLayout& ex, uint32_t step,
+                                               uint32_t alo, float* red, bool w_ok, int warp, int lane, int q, int h,
+                                               int b0, int nreq, bool xmode, const ExLayout& ex, uint32_t step,
                                                __nv_bfloat16* __restrict__ out);
 
 template <int kCl, int kRq>
@@ -467,12 +467,11 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     // ---- out[r][v] = sum_l o_c[r][l] W_UV[h][v][l] for this CTA's kVRows rows of v;
     // warp w owns v in [16w, 16w+16) ----
     if (!kFuse) {
-        if (!w_ok || warp * 16 >= Sh::kVRows) return;
-        k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, xmode, ex, xmode ? step_s : 0u, out);
+        k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, red_acc, w_ok, warp, lane, q, h, b0, nreq, xmode, ex,
+                                 xmode ? step_s : 0u, out);
         return;
     }
-    if (w_ok && warp * 16 < Sh::kVRows)
-        k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, warp, lane, q, h, b0, nreq, true, ex, step_s, out);
+    k3_uv_epilogue<kCl, kRq>(p, w_s, ahi, alo, red_acc, w_ok, warp, lane, q, h, b0, nreq, true, ex, step_s, out);
     k3_fused_combine<kCl, kRq>(p, ex, step_s, q, h, b0, nreq, out);
     if (threadIdx.x == 0) {  // the last CTA to finish (every CTA's thread 0 has read the counter) advances it
         uint32_t* ctl = reinterpret_cast<uint32_t*>(ex_buf(p, p.rank) + ex.ctl);
@@ -538,31 +537,59 @@ __device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const
     if (!ok) record_error(p.error_word, MLA_DEV_PEER_TIMEOUT);
 }
 
-// The W_UV MMA and the epilogue of one K3 warp (its 16 rows of v, all kRq
-// requests of the block as kRq / 16 m16 tiles): R(out) in bf16, or the fp32 shard
-// partial y (into shard_out, or in exchange mode into slot p.rank of every rank's
-// exchange buffer).
+// The W_UV MMA and its epilogue, by all eight warps of a K3 CTA: warp w takes the
+// 16 rows of v of group w % kGroups over the 512 / kKp latent columns of part
+// w / kGroups, for all kRq requests (kRq / 16 m16 tiles); the hi and lo halves of
+// o_c accumulate separately (independent MMA chains). The plain form's 128 rows
+// give every warp its own group (kKp = 1). The cluster form's 32 rows are two
+// groups, so its warps split the latent columns four ways: the parts meet in
+// shared memory (red, the merge's reduction area, free by now) in part order. The
+// part-0 warps write R(out) in bf16, or the fp32 shard partial y (into shard_out,
+// or in exchange mode into slot p.rank of every rank's exchange buffer). (Splitting
+// the plain form into 4 groups x 2 parts of 32 rows measured 1.5 us slower at 32
+// requests.) !w_ok (the W_UV load gave up): every warp still meets any barrier,
+// and nothing is written.
+template <int kCl, int kRq>
+struct UvSplit {
+    static constexpr int kVRows = k3::Shape<kCl, kRq>::kVRows;
+    static constexpr int kVg = 16;                            // rows of v per warp
+    static constexpr int kGroups = kVRows / kVg;              // v groups
+    static constexpr int kKp = k3::kWarps / kGroups;          // latent parts
+    static constexpr int kKs = kLora / 16 / kKp;              // k-steps of 16 per part
+    static constexpr int kNt = kVg / 8;                       // n8 tiles per warp
+    static constexpr int kFrag = k3::Shape<kCl, kRq>::kMt * kNt * 4;  // accumulators per lane
+    static_assert(kGroups * kKp == k3::kWarps && kKs * kKp * 16 == kLora, "warps = v groups x latent parts");
+    static_assert((kKp - 1) * kGroups * kFrag * 32 * 4 <= k3::kRedBytes, "part sums fit the reduction area");
+};
+
 template <int kCl, int kRq>
 __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const uint8_t* w_s, uint32_t ahi,
-                                               uint32_t alo, int warp, int lane, int q, int h, int b0, int nreq,
-                                               bool xmode, const ExLayout& ex, uint32_t step,
+                                               uint32_t alo, float* red, bool w_ok, int warp, int lane, int q, int h,
+                                               int b0, int nreq, bool xmode, const ExLayout& ex, uint32_t step,
                                                __nv_bfloat16* __restrict__ out) {
     using Sh = k3::Shape<kCl, kRq>;
-    constexpr int kMt = Sh::kMt;
+    using Sp = UvSplit<kCl, kRq>;
+    constexpr int kMt = Sh::kMt, kNt = Sp::kNt;
     const int g = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;
+    const int vg = warp % Sp::kGroups, kp = warp / Sp::kGroups;
     const uint32_t wb = smem_u32(w_s);
-    float acc[kMt][2][4];
+    float acc[kMt][kNt][4], acl[kMt][kNt][4];
 #pragma unroll
     for (int mt = 0; mt < kMt; ++mt)
 #pragma unroll
-        for (int n = 0; n < 2; ++n) acc[mt][n][0] = acc[mt][n][1] = acc[mt][n][2] = acc[mt][n][3] = 0.f;
+        for (int n = 0; n < kNt; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][n][e] = acl[mt][n][e] = 0.f;
 #pragma unroll 4
-    for (int ks = 0; ks < kLora / 16; ++ks) {
-        uint32_t b00, b01, b10, b11;  // v tiles 0, 1 of this warp
-        {
-            const int v = 16 * warp + (m8 >> 1) * 8 + r8;
+    for (int kk = 0; kk < Sp::kKs; ++kk) {
+        const int ks = kp * Sp::kKs + kk;
+        uint32_t bf[kNt][2];  // B fragments of this warp's n8 tiles of v
+#pragma unroll
+        for (int np = 0; np < kNt / 2; ++np) {
+            const int v = Sp::kVg * vg + 16 * np + (m8 >> 1) * 8 + r8;
             const int l = 16 * ks + (m8 & 1) * 8;
-            ldsm_x4(wb + (l >> 6) * (Sh::kVRows * 128) + v * 128 + ((((l & 63) >> 3) ^ r8) << 4), b00, b01, b10, b11);
+            ldsm_x4(wb + (l >> 6) * (Sh::kVRows * 128) + v * 128 + ((((l & 63) >> 3) ^ r8) << 4), bf[2 * np][0],
+                    bf[2 * np][1], bf[2 * np + 1][0], bf[2 * np + 1][1]);
         }
 #pragma unroll
         for (int mt = 0; mt < kMt; ++mt) {
@@ -570,23 +597,56 @@ __device__ __forceinline__ void k3_uv_epilogue(const MlaDecodeParams& p, const u
             const int row = 16 * mt + (m8 & 1) * 8 + r8, col = 16 * ks + (m8 >> 1) * 8;
             ldsm_x4(swz1024(ahi, row, col), ah[0], ah[1], ah[2], ah[3]);
             ldsm_x4(swz1024(alo, row, col), al[0], al[1], al[2], al[3]);
-            mma16816(acc[mt][0], ah, b00, b01);
-            mma16816(acc[mt][0], al, b00, b01);
-            mma16816(acc[mt][1], ah, b10, b11);
-            mma16816(acc[mt][1], al, b10, b11);
+#pragma unroll
+            for (int n = 0; n < kNt; ++n) {
+                mma16816(acc[mt][n], ah, bf[n][0], bf[n][1]);
+                mma16816(acl[mt][n], al, bf[n][0], bf[n][1]);
+            }
         }
     }
+#pragma unroll
+    for (int mt = 0; mt < kMt; ++mt)
+#pragma unroll
+        for (int n = 0; n < kNt; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][n][e] += acl[mt][n][e];
+    if (Sp::kKp > 1) {  // part sums of parts 1.. -> red, added by the part-0 warp of the group in part order
+        float4* slot = reinterpret_cast<float4*>(red) + (size_t)((kp - 1) * Sp::kGroups + vg) * (Sp::kFrag / 4) * 32;
+        if (kp > 0) {
+#pragma unroll
+            for (int mt = 0; mt < kMt; ++mt)
+#pragma unroll
+                for (int n = 0; n < kNt; ++n)
+                    slot[(mt * kNt + n) * 32 + lane] = make_float4(acc[mt][n][0], acc[mt][n][1], acc[mt][n][2],
+                                                                   acc[mt][n][3]);
+        }
+        __syncthreads();
+        if (kp > 0) return;
+#pragma unroll 1
+        for (int k2 = 1; k2 < Sp::kKp; ++k2) {
+            const float4* src = reinterpret_cast<const float4*>(red) + (size_t)((k2 - 1) * Sp::kGroups + vg) *
+                                                                        (Sp::kFrag / 4) * 32;
+#pragma unroll
+            for (int mt = 0; mt < kMt; ++mt)
+#pragma unroll
+                for (int n = 0; n < kNt; ++n) {
+                    const float4 x = src[(mt * kNt + n) * 32 + lane];
+                    acc[mt][n][0] += x.x; acc[mt][n][1] += x.y; acc[mt][n][2] += x.z; acc[mt][n][3] += x.w;
+                }
+        }
+    }
+    if (!w_ok) return;
     // The thread holds v, v + 1 of requests 16 mt + g (acc[..][0..1]) and 16 mt + g + 8 (acc[..][2..3]).
     const int v_base = q * Sh::kVRows;
 #pragma unroll
     for (int mt = 0; mt < kMt; ++mt)
 #pragma unroll
-        for (int n = 0; n < 2; ++n)
+        for (int n = 0; n < kNt; ++n)
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 const int r = 16 * mt + g + 8 * hf;
                 if (r >= nreq) continue;
-                const int v = v_base + 16 * warp + 8 * n + 2 * t4;
+                const int v = v_base + Sp::kVg * vg + 8 * n + 2 * t4;
                 const float y0 = acc[mt][n][2 * hf], y1 = acc[mt][n][2 * hf + 1];
                 if (xmode) {  // fp32 y = W_UV o_c / L of this shard, to every rank
 #pragma unroll
