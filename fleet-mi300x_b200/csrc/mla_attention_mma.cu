@@ -36,6 +36,8 @@
 // Start: batches of up to 64 requests derive the split plan from the step's
 // inputs before the wait on K1 and request their first half page early (except
 // one holding the row K1 appends); larger batches read K1's per-CTA plan entry.
+// End (pairs, one request with G = num_ctas): the two groups hold adjacent plan
+// CTAs and merge their partials into one slot per CTA (k2_pairs).
 #include <cuda.h>
 
 #include "mla_common.cuh"
@@ -92,7 +94,8 @@ __device__ __forceinline__ int p_offset(int head, int u) { return head * 64 + ((
 }  // namespace mmak
 
 __global__ void __launch_bounds__(mmak::kThreads, 1)
-    k2_attention_mma(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kv, float scale_log2) {
+    k2_attention_mma(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kv, float scale_log2,
+                     int pairs) {
     using namespace mmak;
     MLA_TL_SCOPE(1);
     extern __shared__ uint8_t smem_raw[];
@@ -113,8 +116,9 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     float* part_acc = reinterpret_cast<float*>(wsb + ws.part_acc);
 
     pdl_trigger();
-    const int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan
-                                                  // has more CTAs than the grid)
+    int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan has
+                                            // more CTAs than the grid; adjacent to group 0's when paired)
+    bool paired = false;                    // the two groups merge their partials (k2_pairs, G = num_ctas)
     const bool leader = w == 0 && lane == 0;
 
     // The leader's look-ahead over half pages (loads run two half pages ahead).
@@ -175,6 +179,8 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         cumv = pre_cum;
         const int64_t U = pre_cum[p.batch];
         G = (int)(U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas);
+        paired = pairs && G == p.num_ctas;
+        if (paired) vc = 2 * blockIdx.x + grp;
         if (vc < G) {
             pe.u_begin = plan_begin(vc, U, G);
             pe.u_end = plan_begin(vc + 1, U, G);
@@ -225,6 +231,22 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         int rows_b = 0;                        // rows attended by the current request
         uint32_t i = 0;                        // half pages consumed
         bool ok = true;
+        float seg_L[2] = {0.f, 0.f};           // row sums of the last segment, heads g, g+8
+        // The partial (m, L, unnormalised O) of this group's segment into slot s.
+        auto write_partial = [&](int64_t s) {
+            if (w == 0 && t4 == 0) {
+                part_ml[(s * kHeads + g) * 2 + 0] = m_run[0];
+                part_ml[(s * kHeads + g) * 2 + 1] = seg_L[0];
+                part_ml[(s * kHeads + g + 8) * 2 + 0] = m_run[1];
+                part_ml[(s * kHeads + g + 8) * 2 + 1] = seg_L[1];
+            }
+            float* acc = part_acc + s * kHeads * kLora + 128 * w + 2 * t4;
+#pragma unroll
+            for (int n = 0; n < 16; ++n) {
+                *reinterpret_cast<float2*>(acc + g * kLora + 8 * n) = make_float2(o[n][0], o[n][1]);
+                *reinterpret_cast<float2*>(acc + (g + 8) * kLora + 8 * n) = make_float2(o[n][2], o[n][3]);
+            }
+        };
         for (; ok && cur.valid(); cur.next()) {
             const bool first = cur.first(), last = cur.last();
             if (first) rows_b = p.seq_lens[cur.b] + new_row_count(p);
@@ -385,23 +407,47 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
                 if (t4 == 0) { S.lsum[w][g] = l0; S.lsum[w][g + 8] = l1; }
                 named_bar_sync(bar_id, kGroupWarps * 32);
-                const int64_t slot_idx = (int64_t)vc + cur.b;
-                if (w == 0 && t4 == 0) {
-                    const float L0 = (S.lsum[0][g] + S.lsum[1][g]) + (S.lsum[2][g] + S.lsum[3][g]);
-                    const float L1 = (S.lsum[0][g + 8] + S.lsum[1][g + 8]) + (S.lsum[2][g + 8] + S.lsum[3][g + 8]);
-                    part_ml[(slot_idx * kHeads + g) * 2 + 0] = m_run[0];
-                    part_ml[(slot_idx * kHeads + g) * 2 + 1] = L0;
-                    part_ml[(slot_idx * kHeads + g + 8) * 2 + 0] = m_run[1];
-                    part_ml[(slot_idx * kHeads + g + 8) * 2 + 1] = L1;
-                }
-                float* acc = part_acc + slot_idx * kHeads * kLora + 128 * w + 2 * t4;
-#pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    *reinterpret_cast<float2*>(acc + g * kLora + 8 * n) = make_float2(o[n][0], o[n][1]);
-                    *reinterpret_cast<float2*>(acc + (g + 8) * kLora + 8 * n) = make_float2(o[n][2], o[n][3]);
-                }
+                seg_L[0] = (S.lsum[0][g] + S.lsum[1][g]) + (S.lsum[2][g] + S.lsum[3][g]);
+                seg_L[1] = (S.lsum[0][g + 8] + S.lsum[1][g + 8]) + (S.lsum[2][g + 8] + S.lsum[3][g + 8]);
+                if (!paired) write_partial((int64_t)vc + cur.b);  // paired: merged after the loop
                 // the lsum buffer is reused by the next segment's epilogue only after
                 // at least one more half page's barriers, which every warp passes after this read
+            }
+        }
+        if (paired) {
+            // Group 1 leaves its (m, L, O) in its own ring (free: its last half page is consumed
+            // and nothing more was requested); group 0 merges it into its own, rescaled to the
+            // larger max, and writes the pair's partial into slot CTA. Both groups meet here
+            // on every path out of the loop.
+            float4* xo = reinterpret_cast<float4*>(smem + kOffTile + kNSlot * kTileBytes);  // [4 w][16 n][32 lanes]
+            float2* xml = reinterpret_cast<float2*>(xo + kGroupWarps * 16 * 32);              // [16 heads]
+            if (grp == 1 && ok) {
+#pragma unroll
+                for (int n = 0; n < 16; ++n) xo[(w * 16 + n) * 32 + lane] = make_float4(o[n][0], o[n][1], o[n][2], o[n][3]);
+                if (w == 0 && t4 == 0) {
+                    xml[g] = make_float2(m_run[0], seg_L[0]);
+                    xml[g + 8] = make_float2(m_run[1], seg_L[1]);
+                }
+            }
+            named_bar_sync(3, kThreads);
+            if (grp == 0) {
+                const float2 p0 = xml[g], p1 = xml[g + 8];
+                const float n0 = fmaxf(m_run[0], p0.x), n1 = fmaxf(m_run[1], p1.x);
+                const float a0 = exp2f(m_run[0] - n0), b0 = exp2f(p0.x - n0);
+                const float a1 = exp2f(m_run[1] - n1), b1 = exp2f(p1.x - n1);
+#pragma unroll
+                for (int n = 0; n < 16; ++n) {
+                    const float4 x = xo[(w * 16 + n) * 32 + lane];
+                    o[n][0] = o[n][0] * a0 + x.x * b0;
+                    o[n][1] = o[n][1] * a0 + x.y * b0;
+                    o[n][2] = o[n][2] * a1 + x.z * b1;
+                    o[n][3] = o[n][3] * a1 + x.w * b1;
+                }
+                seg_L[0] = seg_L[0] * a0 + p0.y * b0;
+                seg_L[1] = seg_L[1] * a1 + p1.y * b1;
+                m_run[0] = n0;
+                m_run[1] = n1;
+                write_partial(blockIdx.x);  // the one request: b = 0
             }
         }
         // Drain: every copy the leader issued must land before the CTA's shared memory is released.
@@ -423,12 +469,10 @@ cudaError_t k2_mma_configure() {
 
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
                                  int sm_count, cudaStream_t stream) {
-    // Plan CTAs are warp groups: up to one CTA per SM with one group each, then a second group
-    // in the same CTAs; beyond two per SM, CTAs of two groups each.
-    const int paired = (p.num_ctas + mmak::kGroups - 1) / mmak::kGroups;
-    const int grid = p.num_ctas <= sm_count ? p.num_ctas : (paired > sm_count ? paired : sm_count);
+    static_assert(mmak::kGroups == 2, "k2_grid assumes two plan CTAs per CTA");
+    const int grid = k2_grid(p.num_ctas, sm_count);
     const cudaError_t e = launch_pdl(k2_attention_mma, dim3(grid), dim3(mmak::kThreads), mmak::kSmemBytes,
-                                     stream, p, tmap_kv, scale_log2);
+                                     stream, p, tmap_kv, scale_log2, k2_pairs(p, sm_count) ? 1 : 0);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

@@ -80,6 +80,25 @@ __host__ __device__ inline WsLayout ws_layout(const MlaDecodeParams& p) {
 }
 
 
+// The split-KV kernel's grid for num_ctas plan CTAs (two warp groups per CTA, each
+// one plan CTA): up to one CTA per SM with one group each, then a second group in
+// the same CTAs; beyond two per SM, CTAs of two groups each.
+inline int k2_grid(int num_ctas, int sm_count) {
+    const int two = (num_ctas + 1) / 2;
+    return num_ctas <= sm_count ? num_ctas : (two > sm_count ? two : sm_count);
+}
+
+// Pair merge of single-request plans. When the batch is one request and every CTA
+// of the split-KV kernel runs two plan CTAs, those are made adjacent (2 CTA, 2 CTA
+// + 1) and, once the request has at least num_ctas tiles (G = num_ctas), the CTA
+// merges its two partials in shared memory into slot CTA: K3 then folds num_ctas / 2
+// partials, in the same tile order. Both kernels take this flag from the host and
+// test G themselves. Only the default (mma) split-KV kernel pairs.
+inline bool k2_pairs(const MlaDecodeParams& p, int sm_count) {
+    return p.batch == 1 && (p.flags & (MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05)) == 0 &&
+           p.num_ctas % 2 == 0 && 2 * k2_grid(p.num_ctas, sm_count) == p.num_ctas;
+}
+
 // Programmatic dependent launch. A kernel launched with launch_pdl may start
 // while the kernel before it on the stream is still running; pdl_wait() returns
 // once that kernel has completed and its writes are visible, so it must come

@@ -158,9 +158,13 @@ __device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const
 // once on every rank): after storing its lines to every rank, the CTA waits for
 // the other ranks' lines of its own (requests, head, rows of v) and writes the
 // combined R(out) itself, so the step needs no K4.
+//
+// pairs (k2_pairs): when the plan has num_ctas CTAs, the split-KV kernel merged
+// plan CTAs 2c and 2c + 1 of the one request into slot c, so the fold runs over
+// c = 0 .. num_ctas / 2 - 1.
 template <int kCl, int kRq, bool kFuse>
 __global__ void __launch_bounds__(k3::kThreads, 1)
-    k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb) {
+    k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb, int pairs) {
     using namespace k3;
     MLA_TL_SCOPE(2);
     using Sh = Shape<kCl, kRq>;
@@ -239,6 +243,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     __syncthreads();
     const int64_t U = U_s;
     const int G = (int)(U < 1 ? 1 : (U < (int64_t)p.num_ctas ? U : (int64_t)p.num_ctas));
+    const bool paired = pairs && G == p.num_ctas;
 
     // Peer exchange (p.world > 0): this step's number = steps completed + 1. The
     // counter was last written by the previous step's K4, which completed before
@@ -266,6 +271,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         if (r >= nreq || cum_s[r + 1] <= cum_s[r]) return false;  // invalid position: no tiles
         c0 = plan_cta_of(cum_s[r], U, G);
         c1 = plan_cta_of(cum_s[r + 1] - 1, U, G);
+        if (paired) { c0 >>= 1; c1 >>= 1; }  // slot c holds plan CTAs 2c, 2c + 1
         return true;
     };
     // o_c -> bf16 hi/lo operands of request r; lane owns l = 4 lane + 128 k
@@ -851,8 +857,8 @@ K3Launch k3_launch(int batch, int sm_count) {
 }
 
 template <int kCl, int kRq, bool kFuse>
-cudaError_t k3_launch_form(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, dim3 grid, cudaStream_t stream,
-                           bool query_only, bool* resident) {
+cudaError_t k3_launch_form(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, dim3 grid, int pairs,
+                           cudaStream_t stream, bool query_only, bool* resident) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(k3::kThreads);
@@ -883,17 +889,18 @@ cudaError_t k3_launch_form(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb
         }
         return e;
     }
-    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl, kRq, kFuse>, p, tmap_kvb);
+    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl, kRq, kFuse>, p, tmap_kvb, pairs);
 }
 
 template <bool kFuse>
-cudaError_t k3_dispatch(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, const K3Launch& l,
+cudaError_t k3_dispatch(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, const K3Launch& l, int pairs,
                         cudaStream_t stream, bool query_only, bool* resident) {
-    if (l.cl > 1) return k3_launch_form<k3::kClusterCtas, k3::kReq, kFuse>(p, tmap_kvb, l.grid, stream, query_only,
-                                                                          resident);
+    if (l.cl > 1)
+        return k3_launch_form<k3::kClusterCtas, k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, stream, query_only,
+                                                                resident);
     if (l.rq == k3::kReq)
-        return k3_launch_form<1, k3::kReq, kFuse>(p, tmap_kvb, l.grid, stream, query_only, resident);
-    return k3_launch_form<1, 2 * k3::kReq, kFuse>(p, tmap_kvb, l.grid, stream, query_only, resident);
+        return k3_launch_form<1, k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, stream, query_only, resident);
+    return k3_launch_form<1, 2 * k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, stream, query_only, resident);
 }
 
 }  // namespace
@@ -906,14 +913,15 @@ bool k3_fused_fits(int batch, int sm_count) {
     bool resident = false;
     MlaDecodeParams dummy{};
     CUtensorMap t{};
-    return k3_dispatch<true>(dummy, t, l, nullptr, true, &resident) == cudaSuccess && resident;
+    return k3_dispatch<true>(dummy, t, l, 0, nullptr, true, &resident) == cudaSuccess && resident;
 }
 
 cudaError_t launch_merge_uv(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, int sm_count, bool fused,
                             cudaStream_t stream) {
     const K3Launch l = k3_launch(p.batch, sm_count);
-    return fused ? k3_dispatch<true>(p, tmap_kvb, l, stream, false, nullptr)
-                 : k3_dispatch<false>(p, tmap_kvb, l, stream, false, nullptr);
+    const int pairs = k2_pairs(p, sm_count) ? 1 : 0;  // as the split-KV kernel of these params ran
+    return fused ? k3_dispatch<true>(p, tmap_kvb, l, pairs, stream, false, nullptr)
+                 : k3_dispatch<false>(p, tmap_kvb, l, pairs, stream, false, nullptr);
 }
 
 }  // namespace mla

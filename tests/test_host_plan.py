@@ -76,6 +76,46 @@ def test_plan_baseline_configs():
     assert G == 148 and len(seg) <= 148 + 256
 
 
+def k2_grid(num_ctas, sm_count):
+    """mla_common.cuh:k2_grid."""
+    two = (num_ctas + 1) // 2
+    return num_ctas if num_ctas <= sm_count else max(two, sm_count)
+
+
+def k2_pairs(batch, num_ctas, sm_count):
+    """mla_common.cuh:k2_pairs (default split-KV kernel)."""
+    return batch == 1 and num_ctas % 2 == 0 and 2 * k2_grid(num_ctas, sm_count) == num_ctas
+
+
+@pytest.mark.parametrize("T,num_ctas,sms,expect", [
+    (131071, 296, 148, True), (65535, 296, 148, True), (18880, 296, 148, True),  # 296 tiles: G = num_ctas
+    (18879, 296, 148, False),  # 295 tiles: G < num_ctas
+    (1023, 296, 148, False), (131071, 148, 148, False), (131071, 200, 148, False), (131071, 400, 148, True),
+    (9000, 296, 148, False)])
+def test_pair_merge_plan(T, num_ctas, sms, expect):
+    """Pair merge: with one request and two plan CTAs per kernel CTA, CTA k runs plan CTAs
+    2k and 2k + 1 (adjacent tile ranges) and, when G = num_ctas, writes their merge into
+    slot k; K3 then folds slots plan_cta_of(first) / 2 .. plan_cta_of(last) / 2, which are
+    exactly the slots written, in tile order. Otherwise nothing changes."""
+    G, seg = simulate([T], num_ctas)
+    grid = k2_grid(num_ctas, sms)
+    paired = k2_pairs(1, num_ctas, sms) and G == num_ctas
+    if paired:
+        assert grid * 2 == num_ctas
+        vcs = sorted(2 * k + g for k in range(grid) for g in range(2))
+        assert vcs == list(range(G)), "every plan CTA runs, in adjacent pairs"
+        assert all(b == 0 for _, b in seg) and len(seg) == G  # one segment per plan CTA
+        written = sorted({c // 2 for c, _ in seg})
+        U = (T + 1 + 63) // 64
+        c0, c1 = plan_cta_of(0, U, G) >> 1, plan_cta_of(U - 1, U, G) >> 1
+        assert written == list(range(c0, c1 + 1)) == list(range(grid))
+    else:
+        # group 1 of a CTA takes plan CTA CTA + grid, as without pairing
+        vcs = sorted(k + grid * g for k in range(grid) for g in range(2) if k + grid * g < G)
+        assert vcs == list(range(G))
+    assert paired == expect
+
+
 def test_paged_cache_helpers_cpu():
     lengths = [0, 63, 64, 130]
     cache = fleet.PagedLatentCache.for_lengths(lengths, spare_pages=2, permute=True,
