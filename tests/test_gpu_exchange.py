@@ -62,9 +62,10 @@ def _inputs(B, dev, seed):
 
 
 @pytest.mark.parametrize("lengths,world", [([5000], 3), ([130], 4), ([64], 2), ([4095], 8), ([300] * 5, 2),
-                                           ([37 * i + 5 for i in range(70)], 3)])
+                                           ([37 * i + 5 for i in range(70)], 3),
+                                           ([40000], 2)])  # shards of 313 tiles: pair-merged partials
 def test_emulated_exchange_equals_gathered_combine(cuda_device, lengths, world):
-    runner, *_ = _runner(cuda_device)
+    runner, *_ = _runner(cuda_device, max_pos=max(8192, max(lengths) + 8))
     B = len(lengths)
     caches, _ = _sharded_caches(lengths, world, cuda_device, seed=11)
     q, kv_a = _inputs(B, cuda_device, seed=12)
@@ -82,9 +83,10 @@ def test_emulated_exchange_equals_gathered_combine(cuda_device, lengths, world):
         ex[0].close()
 
 
-def test_exchange_matches_oracle(cuda_device):
-    T, world = 6000, 2
-    runner, lw, cfg, cos, sin = _runner(cuda_device, seed=5)
+@pytest.mark.parametrize("T", [6000, 40000])  # 40000: each shard's split plan is pair-merged (k2_pairs)
+def test_exchange_matches_oracle(cuda_device, T):
+    world = 2
+    runner, lw, cfg, cos, sin = _runner(cuda_device, seed=5, max_pos=max(8192, T + 8))
     w = oracle_weights(lw)
     rows = workloads.make_cache_rows(6, T, torch.from_numpy(cos), torch.from_numpy(sin))
     x_n = workloads.make_hidden(7, 1).float().numpy()[0]
