@@ -36,8 +36,9 @@
 // Start: batches of up to 64 requests derive the split plan from the step's
 // inputs before the wait on K1 and request their first half page early (except
 // one holding the row K1 appends); larger batches read K1's per-CTA plan entry.
-// End (pairs, one request with G = num_ctas): the two groups hold adjacent plan
-// CTAs and merge their partials into one slot per CTA (k2_pairs).
+// Pairs (k2_pairs, G = num_ctas): the two groups hold adjacent plan CTAs 2k, 2k + 1;
+// where their boundary falls inside a request, group 1's first partial is merged
+// into group 0's last one in shared memory (slot 2k + b), so K3 folds fewer.
 #include <cuda.h>
 
 #include "mla_common.cuh"
@@ -75,7 +76,12 @@ constexpr int kOffTile = 0;                                      // [group][slot
 constexpr int kOffS = kOffTile + kGroups * kNSlot * kTileBytes;  // [group]
 constexpr int kOffP = kOffS + kGroups * kSPartBytes;             // [group][2]
 constexpr int kOffMisc = kOffP + kGroups * 2 * kPBytes;          // [group]
-constexpr int kSmemBytes = kOffMisc + kGroups * (int)sizeof(GroupSmem) + 1024;
+// Pair merge: group 1's first partial, left for group 0 ([4 w][16 n][32 lanes] float4 of O,
+// then (m, L) of the 16 heads, then the mbarrier that group 1 arrives on).
+constexpr int kOffStash = (kOffMisc + kGroups * (int)sizeof(GroupSmem) + 15) & ~15;
+constexpr int kStashOBytes = kGroupWarps * 16 * 32 * 16;         // 32,768
+constexpr int kStashBytes = kStashOBytes + kHeads * 8 + 16;
+constexpr int kSmemBytes = kOffStash + kStashBytes + 1024;
 static_assert(kSmemBytes <= 232448, "K2 (mma) shared memory exceeds 227 KB");
 static_assert(kTileBytes % 1024 == 0 && kOffS % 1024 == 0, "TMA slots must stay 1024-byte aligned");
 
@@ -118,7 +124,15 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     pdl_trigger();
     int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan has
                                             // more CTAs than the grid; adjacent to group 0's when paired)
-    bool paired = false;                    // the two groups merge their partials (k2_pairs, G = num_ctas)
+    bool paired = false;                    // adjacent plan CTAs, merged across their boundary (k2_pairs)
+    float4* stash_o = reinterpret_cast<float4*>(smem + kOffStash);
+    float2* stash_ml = reinterpret_cast<float2*>(smem + kOffStash + kStashOBytes);
+    uint64_t* stash_bar = reinterpret_cast<uint64_t*>(smem + kOffStash + kStashOBytes + kHeads * 8);
+    if (threadIdx.x == 0) {
+        mbar_init(stash_bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
     const bool leader = w == 0 && lane == 0;
 
     // The leader's look-ahead over half pages (loads run two half pages ahead).
@@ -202,9 +216,15 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     pdl_wait();  // the plan, absorbed queries and new rows come from K1
     MLA_TL_WAITED(1);
     if (!pre) {
+        // G, and both candidate entries (plain and paired numbering) in one round trip to the plan
+        const PlanEntry* ents = reinterpret_cast<const PlanEntry*>(wsb + ws.plan + sizeof(PlanHeader));
         G = reinterpret_cast<const PlanHeader*>(wsb + ws.plan)->G;
-        pe = reinterpret_cast<const PlanEntry*>(wsb + ws.plan + sizeof(PlanHeader))[
-            vc < p.num_ctas ? vc : 0];  // loaded with G: one round trip to the plan
+        pe = ents[vc < p.num_ctas ? vc : 0];
+        const int vp = 2 * (int)blockIdx.x + grp;
+        PlanEntry pp{};
+        if (pairs) pp = ents[vp < p.num_ctas ? vp : 0];
+        paired = pairs && G == p.num_ctas;
+        if (paired) { vc = vp; pe = pp; }
     }
 
     if (vc < G) {
@@ -409,45 +429,44 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 named_bar_sync(bar_id, kGroupWarps * 32);
                 seg_L[0] = (S.lsum[0][g] + S.lsum[1][g]) + (S.lsum[2][g] + S.lsum[3][g]);
                 seg_L[1] = (S.lsum[0][g + 8] + S.lsum[1][g + 8]) + (S.lsum[2][g + 8] + S.lsum[3][g + 8]);
-                if (!paired) write_partial((int64_t)vc + cur.b);  // paired: merged after the loop
+                // Pair merge: the boundary between plan CTAs 2k and 2k + 1 falls inside a request
+                // when group 1's first segment started before its range and group 0's last
+                // segment goes on past its range. Group 1 leaves that partial in shared memory;
+                // group 0 merges it into its own (rescaled to the larger max) and writes slot 2k + b.
+                if (paired && grp == 1 && cur.seg == 0 && cur.u_begin > cur.cb0) {
+#pragma unroll
+                    for (int n = 0; n < 16; ++n)
+                        stash_o[(w * 16 + n) * 32 + lane] = make_float4(o[n][0], o[n][1], o[n][2], o[n][3]);
+                    if (w == 0 && t4 == 0) {
+                        stash_ml[g] = make_float2(m_run[0], seg_L[0]);
+                        stash_ml[g + 8] = make_float2(m_run[1], seg_L[1]);
+                    }
+                    named_bar_sync(bar_id, kGroupWarps * 32);
+                    if (leader) mbar_arrive(stash_bar);
+                } else {
+                    if (paired && grp == 0 && cur.u == cur.u_end - 1 && cur.u_end < cur.cb1 &&
+                        mbar_wait(stash_bar, 0, abort, p.error_word)) {
+                        const float2 p0 = stash_ml[g], p1 = stash_ml[g + 8];
+                        const float n0 = fmaxf(m_run[0], p0.x), n1 = fmaxf(m_run[1], p1.x);
+                        const float a0 = exp2f(m_run[0] - n0), b0 = exp2f(p0.x - n0);
+                        const float a1 = exp2f(m_run[1] - n1), b1 = exp2f(p1.x - n1);
+#pragma unroll
+                        for (int n = 0; n < 16; ++n) {
+                            const float4 x = stash_o[(w * 16 + n) * 32 + lane];
+                            o[n][0] = o[n][0] * a0 + x.x * b0;
+                            o[n][1] = o[n][1] * a0 + x.y * b0;
+                            o[n][2] = o[n][2] * a1 + x.z * b1;
+                            o[n][3] = o[n][3] * a1 + x.w * b1;
+                        }
+                        seg_L[0] = seg_L[0] * a0 + p0.y * b0;
+                        seg_L[1] = seg_L[1] * a1 + p1.y * b1;
+                        m_run[0] = n0;
+                        m_run[1] = n1;
+                    }
+                    write_partial((int64_t)vc + cur.b);
+                }
                 // the lsum buffer is reused by the next segment's epilogue only after
                 // at least one more half page's barriers, which every warp passes after this read
-            }
-        }
-        if (paired) {
-            // Group 1 leaves its (m, L, O) in its own ring (free: its last half page is consumed
-            // and nothing more was requested); group 0 merges it into its own, rescaled to the
-            // larger max, and writes the pair's partial into slot CTA. Both groups meet here
-            // on every path out of the loop.
-            float4* xo = reinterpret_cast<float4*>(smem + kOffTile + kNSlot * kTileBytes);  // [4 w][16 n][32 lanes]
-            float2* xml = reinterpret_cast<float2*>(xo + kGroupWarps * 16 * 32);              // [16 heads]
-            if (grp == 1 && ok) {
-#pragma unroll
-                for (int n = 0; n < 16; ++n) xo[(w * 16 + n) * 32 + lane] = make_float4(o[n][0], o[n][1], o[n][2], o[n][3]);
-                if (w == 0 && t4 == 0) {
-                    xml[g] = make_float2(m_run[0], seg_L[0]);
-                    xml[g + 8] = make_float2(m_run[1], seg_L[1]);
-                }
-            }
-            named_bar_sync(3, kThreads);
-            if (grp == 0) {
-                const float2 p0 = xml[g], p1 = xml[g + 8];
-                const float n0 = fmaxf(m_run[0], p0.x), n1 = fmaxf(m_run[1], p1.x);
-                const float a0 = exp2f(m_run[0] - n0), b0 = exp2f(p0.x - n0);
-                const float a1 = exp2f(m_run[1] - n1), b1 = exp2f(p1.x - n1);
-#pragma unroll
-                for (int n = 0; n < 16; ++n) {
-                    const float4 x = xo[(w * 16 + n) * 32 + lane];
-                    o[n][0] = o[n][0] * a0 + x.x * b0;
-                    o[n][1] = o[n][1] * a0 + x.y * b0;
-                    o[n][2] = o[n][2] * a1 + x.z * b1;
-                    o[n][3] = o[n][3] * a1 + x.w * b1;
-                }
-                seg_L[0] = seg_L[0] * a0 + p0.y * b0;
-                seg_L[1] = seg_L[1] * a1 + p1.y * b1;
-                m_run[0] = n0;
-                m_run[1] = n1;
-                write_partial(blockIdx.x);  // the one request: b = 0
             }
         }
         // Drain: every copy the leader issued must land before the CTA's shared memory is released.

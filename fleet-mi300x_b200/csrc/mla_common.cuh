@@ -88,15 +88,17 @@ inline int k2_grid(int num_ctas, int sm_count) {
     return num_ctas <= sm_count ? num_ctas : (two > sm_count ? two : sm_count);
 }
 
-// Pair merge of single-request plans. When the batch is one request and every CTA
-// of the split-KV kernel runs two plan CTAs, those are made adjacent (2 CTA, 2 CTA
-// + 1) and, once the request has at least num_ctas tiles (G = num_ctas), the CTA
-// merges its two partials in shared memory into slot CTA: K3 then folds num_ctas / 2
-// partials, in the same tile order. Both kernels take this flag from the host and
-// test G themselves. Only the default (mma) split-KV kernel pairs.
+// Pair merge. When every CTA of the split-KV kernel runs two plan CTAs and the plan
+// has num_ctas CTAs (G = num_ctas: at least num_ctas tiles), the two are made
+// adjacent (2k, 2k + 1). Where their boundary falls inside a request, group 1's
+// first partial (that request's) is merged in shared memory into group 0's last one
+// (slot 2k + b), so that K3 folds fewer partials: a request's partials then sit at
+// its first plan CTA and at every even plan CTA after it. Both kernels take this
+// flag from the host and test G themselves. Only the default (mma) split-KV kernel
+// pairs.
 inline bool k2_pairs(const MlaDecodeParams& p, int sm_count) {
-    return p.batch == 1 && (p.flags & (MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05)) == 0 &&
-           p.num_ctas % 2 == 0 && 2 * k2_grid(p.num_ctas, sm_count) == p.num_ctas;
+    return (p.flags & (MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05)) == 0 && p.num_ctas % 2 == 0 &&
+           2 * k2_grid(p.num_ctas, sm_count) == p.num_ctas;
 }
 
 // Programmatic dependent launch. A kernel launched with launch_pdl may start

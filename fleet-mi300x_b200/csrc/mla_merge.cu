@@ -91,6 +91,17 @@ __device__ __forceinline__ void load_partial(const float* __restrict__ part_ml, 
     for (int k = 0; k < 4; ++k) a[k] = reinterpret_cast<const float4*>(part_acc + s * kLora)[lane + 32 * k];
 }
 
+// The partials of one request, in fold order: index e < n maps to the plan CTA
+// whose slot holds it. Unpaired: c0 + e. Paired (k2_pairs): the split-KV kernel
+// merged plan CTA 2k + 1's first partial into 2k's wherever their boundary falls
+// inside the request, so the request's partials sit at its first plan CTA c0 and at
+// every even plan CTA after it.
+struct PartIdx {
+    int c0;
+    bool paired;
+    __device__ __forceinline__ int c(int e) const { return !paired ? c0 + e : (e == 0 ? c0 : 2 * ((c0 >> 1) + e)); }
+};
+
 // One step of the online LSE merge: running max m (log2 domain), rescaled sum of
 // exps L and unnormalised acc absorb the partial (ml.x = its max, ml.y = its sum).
 __device__ __forceinline__ void fold_partial(float2 ml, const float4 (&a)[4], float& m, float& L, float4 (&acc)[4]) {
@@ -113,14 +124,14 @@ __device__ __forceinline__ void fold_partial(float2 ml, const float4 (&a)[4], fl
 // the fold is bound by the bytes each of the 64 cluster SMs pulls, not by rounds.)
 template <int kDepth = 4>
 __device__ __forceinline__ void fold_range(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
-                                           int b, int h, int first, int last, int stride, int lane, float& m, float& L,
-                                           float4 (&acc)[4]) {
+                                           int b, int h, const PartIdx& pi, int first, int last, int stride, int lane,
+                                           float& m, float& L, float4 (&acc)[4]) {
     for (int cc = first; cc <= last; cc += kDepth * stride) {
         float2 ml[kDepth];
         float4 a[kDepth][4];
 #pragma unroll
         for (int j = 0; j < kDepth; ++j)
-            if (cc + j * stride <= last) load_partial(part_ml, part_acc, b, h, cc + j * stride, lane, ml[j], a[j]);
+            if (cc + j * stride <= last) load_partial(part_ml, part_acc, b, h, pi.c(cc + j * stride), lane, ml[j], a[j]);
 #pragma unroll
         for (int j = 0; j < kDepth; ++j)
             if (cc + j * stride <= last) fold_partial(ml[j], a[j], m, L, acc);
@@ -129,13 +140,13 @@ __device__ __forceinline__ void fold_range(const float* __restrict__ part_ml, co
 
 template <int kDepth = 4>
 __device__ __forceinline__ void merge_partials(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
-                                               int b, int h, int first, int last, int stride, int lane, float& m,
-                                               float& L, float4 (&acc)[4]) {
+                                               int b, int h, const PartIdx& pi, int first, int last, int stride,
+                                               int lane, float& m, float& L, float4 (&acc)[4]) {
     m = -INFINITY;
     L = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    fold_range<kDepth>(part_ml, part_acc, b, h, first, last, stride, lane, m, L, acc);
+    fold_range<kDepth>(part_ml, part_acc, b, h, pi, first, last, stride, lane, m, L, acc);
 }
 
 // Address of element (row, col) of a [rows][512] bf16 matrix stored as 1024-byte
@@ -159,9 +170,9 @@ __device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const
 // the other ranks' lines of its own (requests, head, rows of v) and writes the
 // combined R(out) itself, so the step needs no K4.
 //
-// pairs (k2_pairs): when the plan has num_ctas CTAs, the split-KV kernel merged
-// plan CTAs 2c and 2c + 1 of the one request into slot c, so the fold runs over
-// c = 0 .. num_ctas / 2 - 1.
+// pairs (k2_pairs): when the plan has num_ctas CTAs, the split-KV kernel ran plan
+// CTAs 2k, 2k + 1 in one CTA and merged them across their boundary where it falls
+// inside a request (PartIdx).
 template <int kCl, int kRq, bool kFuse>
 __global__ void __launch_bounds__(k3::kThreads, 1)
     k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb, int pairs) {
@@ -267,11 +278,12 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     __syncthreads();
     const uint32_t ahi = smem_u32(a_hi), alo = smem_u32(a_lo);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto part_range = [&](int r, int& c0, int& c1) -> bool {
+    // request r's partials: n of them, at the plan CTAs pi.c(0 .. n - 1)
+    auto part_range = [&](int r, PartIdx& pi, int& n) -> bool {
         if (r >= nreq || cum_s[r + 1] <= cum_s[r]) return false;  // invalid position: no tiles
-        c0 = plan_cta_of(cum_s[r], U, G);
-        c1 = plan_cta_of(cum_s[r + 1] - 1, U, G);
-        if (paired) { c0 >>= 1; c1 >>= 1; }  // slot c holds plan CTAs 2c, 2c + 1
+        const int c0 = plan_cta_of(cum_s[r], U, G), c1 = plan_cta_of(cum_s[r + 1] - 1, U, G);
+        pi = PartIdx{c0, paired};
+        n = paired ? 1 + (c1 >> 1) - (c0 >> 1) : c1 - c0 + 1;
         return true;
     };
     // o_c -> bf16 hi/lo operands of request r; lane owns l = 4 lane + 128 k
@@ -342,18 +354,19 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         const int first = q, stride = kCl;
 #pragma unroll 1
         for (int it = 0; it < iters; it += 2) {
-            int r2[2], c0[2] = {0, 0}, c1[2] = {-1, -1};
+            int r2[2], n2[2] = {0, 0};
+            PartIdx pi[2] = {{0, false}, {0, false}};
             bool v[2];
             float2 ml[2][2];
             float4 a[2][2][4];
 #pragma unroll
             for (int x = 0; x < 2; ++x) {
                 r2[x] = gi + (it + x) * groups;
-                v[x] = it + x < iters && part_range(r2[x], c0[x], c1[x]) && c0[x] + first <= c1[x];
+                v[x] = it + x < iters && part_range(r2[x], pi[x], n2[x]) && first < n2[x];
 #pragma unroll
                 for (int j = 0; j < 2; ++j)
-                    if (v[x] && c0[x] + first + j * stride <= c1[x])
-                        load_partial(part_ml, part_acc, b0 + r2[x], h, c0[x] + first + j * stride, lane, ml[x][j],
+                    if (v[x] && first + j * stride < n2[x])
+                        load_partial(part_ml, part_acc, b0 + r2[x], h, pi[x].c(first + j * stride), lane, ml[x][j],
                                      a[x][j]);
             }
 #pragma unroll
@@ -365,9 +378,9 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
                 if (v[x]) {
 #pragma unroll
                     for (int j = 0; j < 2; ++j)
-                        if (c0[x] + first + j * stride <= c1[x]) fold_partial(ml[x][j], a[x][j], m, L, acc);
-                    fold_range(part_ml, part_acc, b0 + r2[x], h, c0[x] + first + 2 * stride, c1[x], stride, lane, m,
-                               L, acc);
+                        if (first + j * stride < n2[x]) fold_partial(ml[x][j], a[x][j], m, L, acc);
+                    fold_range(part_ml, part_acc, b0 + r2[x], h, pi[x], first + 2 * stride, n2[x] - 1, stride, lane,
+                               m, L, acc);
                 }
                 if (r2[x] < nreq && it + x < iters) publish(r2[x], m, L, acc);
             }
@@ -376,12 +389,13 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
 #pragma unroll 1
     for (int it = 0; it < iters; ++it) {  // uniform trip count: the barriers below are CTA-wide
         const int r = gi + it * groups;
-        int c0 = 0, c1 = -1;
+        PartIdx pi{0, false};
+        int n = 0;
         float4 acc[4];
         float m = -INFINITY, L = 0.f;
         const int first = q + kCl * wi;
-        if (part_range(r, c0, c1) && c0 + first <= c1)
-            merge_partials(part_ml, part_acc, b0 + r, h, c0 + first, c1, kCl * wpr, lane, m, L, acc);
+        if (part_range(r, pi, n) && first < n)
+            merge_partials(part_ml, part_acc, b0 + r, h, pi, first, n - 1, kCl * wpr, lane, m, L, acc);
         else
             for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (lane == 0) { red_ml[warp][0] = m; red_ml[warp][1] = L; }

@@ -150,14 +150,18 @@ def test_large_batch_merge_blocks(cuda_device, B):
         assert_close(got[b], want[b], f"request {b} of {B} (T={lengths[b]})")
 
 
-@pytest.mark.parametrize("T", [18880, 40000])
-def test_single_request_pair_merge(cuda_device, T):
-    """One request with at least 296 tiles (18,881 rows: exactly 296, the last holding only
-    the new row): with the default 296 plan CTAs every split-KV CTA merges its two
-    adjacent plan CTAs' partials before K3 (k2_pairs), and K3 folds 148. Checked against
-    the oracle, against plans that do not pair (148 CTAs, the check kernel), and for
-    repeatable bits."""
-    d = ragged_batch(cuda_device, [T])
+@pytest.mark.parametrize("lengths", [[18880], [40000], [9000, 20, 12000, 0, 3000, 64, 8000, 1],
+                                     [127] * 40 + [30000] + [5] * 30],
+                         ids=["one-296-tiles", "one-626-tiles", "ragged-8", "ragged-71"])
+def test_pair_merge(cuda_device, lengths):
+    """Plans of at least 296 tiles with the default 296 plan CTAs: each split-KV CTA runs two
+    adjacent plan CTAs and, where their boundary falls inside a request, merges the two
+    partials of that request in shared memory before K3 (k2_pairs). One request of exactly
+    296 tiles (the last holding only the new row) merges at every CTA; ragged batches merge
+    at some boundaries and not at others (empty requests, requests inside one plan CTA).
+    Checked against the oracle, against plans that do not pair (148 CTAs, the check kernel),
+    and for repeatable bits."""
+    d = ragged_batch(cuda_device, lengths)
     pages_np = d["cache"].pages.float().cpu().numpy()
     bt = d["cache"].block_table.cpu().numpy()
     want, _ = oracle_paged(bt, pages_np, d, fast=True)
@@ -165,9 +169,10 @@ def test_single_request_pair_merge(cuda_device, T):
     np.testing.assert_array_equal(got, run_gpu(d, cuda_device))
     unpaired = run_gpu(d, cuda_device, num_ctas=148)
     ck = run_gpu(d, cuda_device, check_kernel=True)
-    assert_close(got[0], want[0], f"T={T}, paired")
-    assert_close(unpaired[0], want[0], f"T={T}, 148 CTAs")
-    assert_close(got[0], ck[0], f"T={T}, paired vs check kernel")
+    for b, T in enumerate(lengths):
+        assert_close(got[b], want[b], f"request {b} (T={T}), paired")
+        assert_close(unpaired[b], want[b], f"request {b} (T={T}), 148 CTAs")
+        assert_close(got[b], ck[b], f"request {b} (T={T}), paired vs check kernel")
 
 
 def test_tensor_core_kernels_vs_check_kernel(cuda_device):

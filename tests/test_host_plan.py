@@ -82,9 +82,40 @@ def k2_grid(num_ctas, sm_count):
     return num_ctas if num_ctas <= sm_count else max(two, sm_count)
 
 
-def k2_pairs(batch, num_ctas, sm_count):
+def k2_pairs(num_ctas, sm_count):
     """mla_common.cuh:k2_pairs (default split-KV kernel)."""
-    return batch == 1 and num_ctas % 2 == 0 and 2 * k2_grid(num_ctas, sm_count) == num_ctas
+    return num_ctas % 2 == 0 and 2 * k2_grid(num_ctas, sm_count) == num_ctas
+
+
+def paired_slots(seq_lens, num_ctas):
+    """The pair merge of mla_attention_mma.cu: plan CTAs 2k, 2k + 1 run in kernel CTA k;
+    where their boundary falls inside a request, 2k + 1's first segment is merged into
+    2k's last one. Returns, per request, the slots written, in tile order."""
+    G, segments = simulate(seq_lens, num_ctas)
+    tiles = [(t + 1 + 63) // 64 for t in seq_lens]
+    cum = [0]
+    for n in tiles:
+        cum.append(cum[-1] + n)
+    U = cum[-1]
+    by_cta = {}
+    for c, b in segments:
+        by_cta.setdefault(c, []).append(b)
+    written = {b: [] for b in range(len(tiles))}
+    for c in range(G):
+        for i, b in enumerate(by_cta[c]):
+            mid = plan_begin(c, U, G)
+            merged_away = c % 2 == 1 and i == 0 and cum[b] < mid  # group 1's first segment, request started before
+            if not merged_away:
+                written[b].append(c)
+    return G, cum, written
+
+
+def part_idx(c0, c1, paired):
+    """mla_merge.cu:PartIdx over a request's plan CTAs [c0, c1]."""
+    if not paired:
+        return list(range(c0, c1 + 1))
+    n = 1 + (c1 >> 1) - (c0 >> 1)
+    return [c0 if e == 0 else 2 * ((c0 >> 1) + e) for e in range(n)]
 
 
 @pytest.mark.parametrize("T,num_ctas,sms,expect", [
@@ -92,28 +123,39 @@ def k2_pairs(batch, num_ctas, sm_count):
     (18879, 296, 148, False),  # 295 tiles: G < num_ctas
     (1023, 296, 148, False), (131071, 148, 148, False), (131071, 200, 148, False), (131071, 400, 148, True),
     (9000, 296, 148, False)])
-def test_pair_merge_plan(T, num_ctas, sms, expect):
-    """Pair merge: with one request and two plan CTAs per kernel CTA, CTA k runs plan CTAs
-    2k and 2k + 1 (adjacent tile ranges) and, when G = num_ctas, writes their merge into
-    slot k; K3 then folds slots plan_cta_of(first) / 2 .. plan_cta_of(last) / 2, which are
-    exactly the slots written, in tile order. Otherwise nothing changes."""
-    G, seg = simulate([T], num_ctas)
-    grid = k2_grid(num_ctas, sms)
-    paired = k2_pairs(1, num_ctas, sms) and G == num_ctas
-    if paired:
-        assert grid * 2 == num_ctas
-        vcs = sorted(2 * k + g for k in range(grid) for g in range(2))
-        assert vcs == list(range(G)), "every plan CTA runs, in adjacent pairs"
-        assert all(b == 0 for _, b in seg) and len(seg) == G  # one segment per plan CTA
-        written = sorted({c // 2 for c, _ in seg})
-        U = (T + 1 + 63) // 64
-        c0, c1 = plan_cta_of(0, U, G) >> 1, plan_cta_of(U - 1, U, G) >> 1
-        assert written == list(range(c0, c1 + 1)) == list(range(grid))
-    else:
-        # group 1 of a CTA takes plan CTA CTA + grid, as without pairing
-        vcs = sorted(k + grid * g for k in range(grid) for g in range(2) if k + grid * g < G)
-        assert vcs == list(range(G))
+def test_pair_merge_single_request(T, num_ctas, sms, expect):
+    """One request: every boundary between 2k and 2k + 1 is inside it, so the slots are 0, 2, 4, ..."""
+    G, cum, written = paired_slots([T], num_ctas)
+    paired = k2_pairs(num_ctas, sms) and G == num_ctas
     assert paired == expect
+    if paired:
+        U = cum[-1]
+        assert written[0] == part_idx(plan_cta_of(0, U, G), plan_cta_of(U - 1, U, G), True)
+        assert written[0] == list(range(0, G, 2))
+
+
+def test_pair_merge_random_batches():
+    """Ragged batches (empty requests, requests inside one plan CTA, requests across many): the
+    slots K3 enumerates with PartIdx are exactly those the pair-merged split-KV kernel writes,
+    in tile order, and each written slot is unique."""
+    rng = random.Random(7)
+    for _ in range(300):
+        B = rng.randint(1, 60)
+        lens = [rng.choice([0, 1, 63, 64, 127, rng.randint(0, 3000), rng.randint(0, 40000)]) for _ in range(B)]
+        num_ctas = rng.choice([2, 4, 16, 296, 400])
+        G, cum, written = paired_slots(lens, num_ctas)
+        if G != num_ctas:
+            continue
+        U = cum[-1]
+        slots = []
+        for b in range(B):
+            if cum[b + 1] == cum[b]:
+                assert written[b] == []
+                continue
+            c0, c1 = plan_cta_of(cum[b], U, G), plan_cta_of(cum[b + 1] - 1, U, G)
+            assert written[b] == part_idx(c0, c1, True), (lens, num_ctas, b)
+            slots += [c + b for c in written[b]]
+        assert len(set(slots)) == len(slots)
 
 
 def test_paged_cache_helpers_cpu():
