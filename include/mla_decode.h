@@ -322,7 +322,9 @@ int mla_rows_to_pages(const MlaRowsToPages* r, void* stream);
  * step writes everything it reads). The scratch is one per device and shared by
  * every call on that device: calls that overlap on the GPU (on streams not
  * ordered with one another, or from several host threads) race on it. Order
- * them on one stream or with events. */
+ * them on one stream or with events. The first call on a device, with that device
+ * current, looks up the scratch array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture on that device. */
 int mla_decode_step_static(const MlaDecodeParams* p, void* stream);
 
 #ifdef __cplusplus
