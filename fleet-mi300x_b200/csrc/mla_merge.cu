@@ -245,6 +245,13 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
             if (b == 0) U_s = pre_tot[0] + pre_tot[1];
         }
     }
+    // Rows of the W_UV operand past nreq are zero (shared memory only, so before the wait).
+    for (int i = threadIdx.x; i < (kRq - nreq) * (kLora / 8); i += kThreads) {
+        const int r = nreq + i / (kLora / 8), col = (i % (kLora / 8)) * 8;
+        const uint32_t ahi0 = smem_u32(a_hi), alo0 = smem_u32(a_lo);
+        *reinterpret_cast<uint4*>(a_hi + (swz1024(ahi0, r, col) - ahi0)) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(a_lo + (swz1024(alo0, r, col) - alo0)) = make_uint4(0u, 0u, 0u, 0u);
+    }
     pdl_wait();  // partials from K2, plan from K1
     MLA_TL_WAITED(2);
     if (!pre) {
@@ -269,13 +276,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     // Every fold visits partials in plan-CTA order; requests without tiles (invalid
     // position) get a zero o_c.
     __shared__ float red_ml[kWarps][2];
-    for (int i = threadIdx.x; i < (kRq - nreq) * (kLora / 8); i += kThreads) {  // rows past nreq: zero operands
-        const int r = nreq + i / (kLora / 8), col = (i % (kLora / 8)) * 8;
-        const uint32_t ahi0 = smem_u32(a_hi), alo0 = smem_u32(a_lo);
-        *reinterpret_cast<uint4*>(a_hi + (swz1024(ahi0, r, col) - ahi0)) = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(a_lo + (swz1024(alo0, r, col) - alo0)) = make_uint4(0u, 0u, 0u, 0u);
-    }
-    __syncthreads();
+    __syncthreads();  // step_s
     const uint32_t ahi = smem_u32(a_hi), alo = smem_u32(a_lo);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // request r's partials: n of them, at the plan CTAs pi.c(0 .. n - 1)
