@@ -185,60 +185,134 @@ class StepTimer:
                 "(the step reads %.1f MB of cache rows)" % (self.kv_bytes / 1e6))
 
 
-def cpu_oracle_sample(name: str, budget_s: float, faithful: bool) -> dict:
-    """Times the CPU oracle on a bounded sample of the workload's requests."""
+def host_threads() -> int:
+    """Host threads this process may run on (its CPU affinity), whatever OMP_NUM_THREADS says."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def use_all_host_threads() -> int:
+    """Give torch and NumPy's BLAS every host thread of this process. torchrun exports
+    OMP_NUM_THREADS=1 to its ranks, which would leave the CPU legs on one core."""
+    n = host_threads()
+    torch.set_num_threads(n)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    return n
+
+
+class CpuSample:
+    """The CPU oracle on a bounded sample of a workload's requests (the cpu_baseline leg
+    and the reference arm). Inputs are prepared once, outside any timing: the layer's
+    weights, q / kv_a of up to 64 requests and the cache rows of up to 4 distinct
+    requests (seeded N(0, 1) bf16 latents, reused round-robin), so that the timed work is
+    the task itself: the new row (kv_post) and the attention over the request's rows.
+    `faithful` runs the per-head loop of reference_decode.py:245-254 (oracle.attend_rows),
+    otherwise the all-heads vectorised form (oracle.attend_rows_fast)."""
+
+    def __init__(self, name: str):
+        from oracle import mla_oracle as O
+        self.O = O
+        self.name = name
+        self.wl = workloads.WORKLOADS[name]
+        self.lengths = self.wl.seq_lens()
+        self.cfg = O.Config()
+        lw = workloads.make_layer_weights(self.wl.seed)
+        f = lambda t: t.float().numpy()
+        self.w = O.Weights(f(lw.q_proj), f(lw.kv_a_proj_with_mqa), f(lw.kv_a_layernorm), f(lw.kv_b_proj))
+        self.cos, self.sin = self.cfg.cos_sin(max(self.lengths) + 8)
+        x_n = workloads.make_hidden(self.wl.seed + 1, min(len(self.lengths), 64)).float().numpy()
+        self.qkv = [O.project(self.cfg, self.w, x) for x in x_n]
+        rng = np.random.default_rng(self.wl.seed)
+        self.rows = {}
+        for b in range(min(len(self.lengths), 4)):
+            T = self.lengths[b]
+            if T not in self.rows:
+                self.rows[T] = O.bf16_round(rng.standard_normal((T + 1, 576), dtype=np.float32))
+        self.i = 0
+
+    def run(self, budget_s: float, faithful: bool, max_requests: int | None = None) -> dict:
+        O = self.O
+        attend = O.attend_rows if faithful else O.attend_rows_fast
+        done_bytes, done_req, t_total = 0, 0, 0.0
+        limit = max_requests or 64 * len(self.lengths)
+        while t_total < budget_s and done_req < limit:
+            b = self.i % len(self.lengths)
+            T = self.lengths[b]
+            allr = self.rows.get(T)
+            if allr is None:  # a ragged length without prepared rows: the nearest prepared one
+                T = min(self.rows, key=lambda t: abs(t - T))
+                allr = self.rows[T]
+            q, kv_a = self.qkv[b % len(self.qkv)]
+            t0 = time.perf_counter()
+            allr[T] = O.kv_post(self.cfg, self.w, kv_a, T, self.cos, self.sin)
+            attend(self.cfg, self.w, q, allr, T, self.cos, self.sin)
+            t_total += time.perf_counter() - t0
+            done_bytes += (T + 1) * 1152
+            done_req += 1
+            self.i += 1
+        return {"value": done_bytes / t_total / 1e9, "unit": "GB/s", "cores": host_threads(), "kind": "port",
+                "sample": f"{done_req} requests of {self.name} ({done_bytes / 1e6:.1f} MB of cache rows), "
+                          f"{'per-head loop (reference_decode.py:245-254)' if faithful else 'all-heads vectorised'} "
+                          f"NumPy/BLAS on {host_threads()} host threads, {t_total:.2f} s",
+                "seconds": t_total, "bytes": done_bytes, "requests": done_req}
+
+
+def check_sequence_sharded(inp: dict) -> dict:
+    """The CPU leg's check of the sequence-sharded step: its combined R(out) against the
+    oracle (all-heads form of reference_decode.py:239-254) over all rows of the sequence."""
     from oracle import mla_oracle as O
-    wl = workloads.WORKLOADS[name]
-    lengths = wl.seq_lens()
-    cfg = O.Config()
+    wl = workloads.WORKLOADS["config5b"]
     lw = workloads.make_layer_weights(wl.seed)
     f = lambda t: t.float().numpy()
     w = O.Weights(f(lw.q_proj), f(lw.kv_a_proj_with_mqa), f(lw.kv_a_layernorm), f(lw.kv_b_proj))
-    x_n = workloads.make_hidden(wl.seed + 1, min(len(lengths), 64)).float().numpy()
-    rng = np.random.default_rng(wl.seed)
-    attend = O.attend_rows if faithful else O.attend_rows_fast
-    cos, sin = cfg.cos_sin(max(lengths) + 8)
-    done_bytes, done_req, t_total = 0, 0, 0.0
-    i = 0
-    while t_total < budget_s and done_req < 64 * len(lengths):
-        b = i % len(lengths)
-        T = lengths[b]
-        rows = O.bf16_round(rng.standard_normal((T, 576), dtype=np.float32))
-        q, kv_a = O.project(cfg, w, x_n[b % len(x_n)])
-        t0 = time.perf_counter()
-        row = O.kv_post(cfg, w, kv_a, T, cos, sin)
-        allr = np.concatenate([rows, row[None]], 0)
-        attend(cfg, w, q, allr, T, cos, sin)
-        t_total += time.perf_counter() - t0
-        done_bytes += (T + 1) * 1152
-        done_req += 1
-        i += 1
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([x.get("num_threads", 1) for x in threadpool_info()] or [1])
-    except Exception:
-        cores = os.cpu_count() or 1
-    return {"value": done_bytes / t_total / 1e9, "unit": "GB/s", "cores": int(cores), "kind": "port",
-            "sample": f"{done_req} requests of {name} ({done_bytes / 1e6:.1f} MB of cache rows), "
-                      f"{'per-head loop (reference_decode.py:245-254)' if faithful else 'all-heads vectorised'} "
-                      f"NumPy/BLAS, {t_total:.2f} s",
-            "seconds": t_total}
+    cfg = O.Config()
+    T = inp["T"]
+    cos, sin = cfg.cos_sin(T + 8)
+    new_row = O.kv_post(cfg, w, inp["kv_a"][0], T, cos, sin)
+    want = O.attend_rows_fast(cfg, w, inp["q"].reshape(16, 192), np.concatenate([inp["rows"], new_row[None]]), T,
+                              cos, sin)
+    got = inp["out"][0]
+    rel = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+    cs = float(got @ want / (np.linalg.norm(got) * np.linalg.norm(want) + 1e-30))
+    return {"oracle": f"oracle.attend_rows_fast over all {T + 1} rows", "max_rel_vs_oracle": rel, "cos": cs,
+            "bar": 2e-2, "ok": bool(rel <= 2e-2)}
+
+
+def cpu_oracle_sample(name: str, budget_s: float, faithful: bool) -> dict:
+    """Times the CPU oracle on a bounded sample of the workload's requests (all host threads)."""
+    use_all_host_threads()
+    return CpuSample(name).run(budget_s, faithful)
 
 
 # ---------------------------------------------------------------------------- arms
+REFERENCE_TIMED_S = 100.0  # seconds of oracle work in the reference arm's timed steps, all of them together
+
+
 def run_reference_arm(args, rank: int, world: int) -> None:
+    """The reference's own algorithm for this path on the host cores: the oracle's
+    per-head loop, which restates reference_decode.py:245-254 and is pinned to the
+    reference's outputs (the reference itself is pure Python and cannot be installed
+    or shipped here). Rank 0 only. Each step is a bounded sample of the same workload;
+    the timed steps hold about REFERENCE_TIMED_S seconds of work together, so the arm
+    ends within a few minutes whatever --steps is."""
     if rank != 0:
         return
-    steps_out = []
-    per_step_budget = max(0.5, min(6.0, 120.0 / max(1, args.steps + args.warmup)))
+    threads = use_all_host_threads()
+    t_start = time.perf_counter()
+    sample = CpuSample(args.workload)
+    per_step = max(0.3, min(6.0, REFERENCE_TIMED_S / max(1, args.steps)))
     for _ in range(args.warmup):
-        cpu_oracle_sample(args.workload, per_step_budget / 4, faithful=True)
-    info = None
-    for _ in range(args.steps):
-        info = cpu_oracle_sample(args.workload, per_step_budget, faithful=True)
-        steps_out.append(info)
+        sample.run(min(0.5, per_step), faithful=True)
+    steps_out = [sample.run(per_step, faithful=True) for _ in range(args.steps)]
     total_s = sum(s["seconds"] for s in steps_out)
-    total_b = sum(s["value"] * s["seconds"] * 1e9 for s in steps_out)
+    total_b = sum(s["bytes"] for s in steps_out)
+    n_req = sum(s["requests"] for s in steps_out)
     value = total_b / total_s / 1e9
     wl = workloads.WORKLOADS[args.workload]
     line = {
@@ -247,8 +321,10 @@ def run_reference_arm(args, rank: int, world: int) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded)",
         "config": {"workload": args.workload, "batch_per_gpu": wl.batch, "parallelism": "cpu-host"},
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": info["cores"], "kind": "port",
-                         "sample": info["sample"] + " per step"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{n_req} requests of {args.workload} over {args.steps} steps of about "
+                                   f"{per_step:.1f} s each, per-head loop (reference_decode.py:245-254) "
+                                   f"NumPy/BLAS on {threads} host threads; wall {time.perf_counter() - t_start:.0f} s"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -410,10 +486,29 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         e2e_ms = float(t.item())
     e2e_value = world * kv_b / (e2e_ms * 1e-3) / 1e9
 
+    # ---- the sequence-sharded variant (config 5b) in the same processes at N > 1; the other
+    # configurations on this GPU at N = 1
+    seq = None
+    if world > 1 and not args.no_extra:
+        seq = sequence_sharded_block(args, rank, world, dev, dist)
+    others = None
+    if world == 1 and not args.no_extra:
+        peak0, _ = measured_peak()
+        oclocks = ClockSampler(local_rank)
+        with oclocks:
+            others = {n: other_config_summary(n, dev, max(10, args.steps), peak0)
+                      for n in ("config1", "config3", "config4", "config5b") if n != args.workload}
+        others["clocks"] = oclocks.summary()
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample(args.workload, args.cpu_seconds, faithful=False)
-        cpu.pop("seconds", None)
+        for k in ("seconds", "bytes", "requests"):
+            cpu.pop(k, None)
+    if seq is not None:
+        inp = seq.pop("_check_inputs")
+        if rank == 0:  # the CPU leg also checks the sequence-sharded output against the oracle
+            seq["check"] = check_sequence_sharded(inp)
 
     if dist:
         dist.barrier()
@@ -452,16 +547,27 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         "gpu_launches": native.load_library().mla_launches_per_step() * args.steps,
         "clocks": clocks.summary(),
     }
+    if seq is not None:
+        line["sequence_sharded"] = seq
+    if others is not None:
+        line["other_configs"] = others
     print(json.dumps(line), flush=True)
 
 
-def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torch.device, dist) -> None:
-    """Config 5b across `world` GPUs: one 131,072-token sequence split by page-aligned KV
-    ranges; per step K1+K2+K3 on each range and the fixed-order combine of the 8.4 KB
-    partials (distributed.py). --exchange peer (default): K3 stores the partials into
-    every rank's exchange buffer over NVLink and K4 combines, one library call per
-    step; --exchange nccl: an NCCL all-gather and mla_combine_shards. Total work is
-    fixed: strong scaling."""
+def sequence_sharded_block(args, rank: int, world: int, dev: torch.device, dist, exchange: str = "peer") -> dict:
+    """Config 5b across `world` GPUs, in the processes of the current run: one sequence of
+    131,072 cached rows split by page-aligned KV ranges (distributed.sequence_shards); per
+    step K1-K3 on each range and the fixed-order combine of the 8.4 KB shard partials.
+    exchange="peer": K3 stores the partials into every rank's exchange buffer over NVLink
+    and combines them itself where its grid is resident at once (else K4 does), one
+    library call per step; "nccl": an NCCL all-gather and mla_combine_shards.
+
+    Every rank draws the same 131,072 rows (one seeded generator), so the same rows are
+    also timed unsharded on each rank's own GPU (the N = 1 step, a CUDA graph of K1-K3):
+    strong-scaling efficiency = t(1) / (N t(N)), both measured in this run, max over
+    ranks. The combined output is compared with the one-GPU step's; rank 0 keeps the
+    inputs so that its CPU leg checks it against the oracle over all rows. Total work is
+    fixed: strong scaling. Collective: every rank calls this."""
     dmod = importlib.import_module("fleet-mi300x_b200.distributed")
     wl = workloads.WORKLOADS["config5b"]
     T = wl.seq_lens()[0]
@@ -470,110 +576,211 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
     w = fleet.LayerWeights(*(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm,
                                                    lw.kv_b_proj)))
     cos, sin = fleet.device_rope_tables(cfg, T + 8, dev)
+    rows = torch.randn(T, 576, generator=torch.Generator(device=dev).manual_seed(wl.seed), device=dev)
+    rows = rows.to(torch.bfloat16)
+    runner = fleet.MlaDecodeAttention(cfg, w, cos, sin)
+    x_n = workloads.make_hidden(wl.seed + 1, 1).to(dev)
+    q, kv_a = (t.contiguous() for t in runner.project(x_n))
+    if dist is not None:  # every shard must use the same q / kv_a bits
+        dist.broadcast(q, 0)
+        dist.broadcast(kv_a, 0)
+    pos = torch.tensor([T], dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    kv_b = workloads.kv_bytes([T])
+    steps = max(5, args.steps)
+
+    # ---- N = 1 on this rank's own GPU: the whole sequence, the same rows
+    full = fleet.PagedLatentCache.for_lengths([T], permute=True, zero=False,
+                                              generator=torch.Generator().manual_seed(wl.seed), device=dev)
+    full.write_rows(0, 0, rows)
+    one = torch.empty(1, 2048, dtype=torch.bfloat16, device=dev)
+    g1 = fleet.DecodeGraph(runner, full, inputs="qkv", q=q, kv_a=kv_a, out=one)
+    for _ in range(max(3, args.warmup)):
+        g1.replay()
+    g1.synchronize()
+    t1_timer = StepTimer(stream, kv_b, dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t1_ms = t1_timer(g1.replay, steps)
+    g1.synchronize()
+    del g1
+
+    # ---- N shards
     a, b = dmod.sequence_shards(T, world)[rank]
     last = rank == world - 1
     cache = fleet.PagedLatentCache.for_lengths([b - a], extra_tokens=1 if last else 0, permute=True, zero=False,
                                                generator=torch.Generator().manual_seed(wl.seed + rank), device=dev)
-    workloads.fill_pool_random(cache.pages, wl.seed + 1000 * rank)
-    runner = fleet.MlaDecodeAttention(cfg, w, cos, sin)
-    x_n = workloads.make_hidden(wl.seed + 1, 1).to(dev)
-    q, kv_a = (t.contiguous() for t in runner.project(x_n))
-    pos = torch.tensor([T], dtype=torch.int32, device=dev)
+    cache.write_rows(0, 0, rows[a:b])
+    out = torch.empty(1, 2048, dtype=torch.bfloat16, device=dev)
     local = torch.empty(1, 16, native.SHARD_STRIDE, dtype=torch.float32, device=dev)
     parts = torch.empty(world, 1, 16, native.SHARD_STRIDE, dtype=torch.float32, device=dev)
-    out = torch.empty(1, 2048, dtype=torch.bfloat16, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    ex = dmod.ExchangeBuffers.create(rank, world, max_batch=1) if args.exchange == "peer" else None
+    ex = None
+    if exchange == "peer":
+        ex = (dmod.ExchangeBuffers.create(rank, world, max_batch=1) if dist is not None
+              else dmod.ExchangeBuffers.local(1, max_batch=1)[0])
 
     def step():
         if ex is not None:
             runner.attend(q, kv_a, cache, out, rope_pos=pos, new_row=last, exchange=ex)
             return
         runner.attend(q, kv_a, cache, rope_pos=pos, shard_out=local, new_row=last)
-        dist.all_gather_into_tensor(parts, local)
-        fleet.combine_shards(parts, out)
+        if dist is not None:
+            dist.all_gather_into_tensor(parts, local)
+            fleet.combine_shards(parts, out)
+        else:
+            fleet.combine_shards(local[None], out)
 
     for _ in range(max(3, args.warmup)):
         step()
+    torch.cuda.synchronize()
     runner.check_errors()
-    kv_b = workloads.kv_bytes([T])
     timer = StepTimer(stream, kv_b // world, dev)
-    clocks = ClockSampler(local_rank)
-    with clocks:
+    if dist is not None:
         dist.barrier()
-        torch.cuda.synchronize()
-        ms = timer(step, args.steps)
-        torch.cuda.synchronize()
-        dist.barrier()
-    t = torch.tensor([ms], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    torch.cuda.synchronize()
+    tn_ms = timer(step, steps)
+    torch.cuda.synchronize()
     runner.check_errors()
 
-    # ---- stage timings (each stage repeated alone on every rank at once; max over
-    # ranks). A K3 repeated without its K4 rewrites the same slot and flags, which the
-    # next whole step's K4 then reads, so the exchange protocol stays in step.
+    # ---- stage times (each stage repeated alone on every rank at once). A K3 repeated
+    # without the combine rewrites the same lines, which the next whole step reads again,
+    # so the exchange protocol stays in step.
     def stage(name):
-        if name == "combine" and ex is None:
-            return lambda: fleet.combine_shards(parts, out)
-        if name == "all_gather":
-            return lambda: dist.all_gather_into_tensor(parts, local)
-        if name == "k1_k2_k3":
-            return lambda: [runner.attend(q, kv_a, cache, out if ex is not None else None, st, rope_pos=pos,
-                                          shard_out=None if ex is not None else local, new_row=last, exchange=ex)
-                            for st in ("prologue", "attention", "merge")]
-        return lambda: runner.attend(q, kv_a, cache, out if ex is not None else None, name, rope_pos=pos,
-                                     shard_out=None if ex is not None else local, new_row=last, exchange=ex)
-    names = ["prologue", "attention", "merge", "k1_k2_k3"] + ([] if ex is not None else ["all_gather", "combine"])
+        so = None if ex is not None else local
+        o = out if ex is not None else None
+        return lambda: runner.attend(q, kv_a, cache, o, name, rope_pos=pos, shard_out=so, new_row=last, exchange=ex)
+    names = ["prologue", "attention", "merge"]
     stage_ms = []
     for name in names:
-        dist.barrier()
+        if dist is not None:
+            dist.barrier()
         torch.cuda.synchronize()
-        stage_ms.append(timer(stage(name), max(5, args.steps // 2)))
+        stage_ms.append(timer(stage(name), max(5, steps // 2)))
     if ex is not None:  # the same step with the exchange as K3 + K4 instead of the fused K3
         names.append("step_k3_k4_split")
         runner.flags |= native.FLAG_EXCHANGE_SPLIT
-        dist.barrier()
+        if dist is not None:
+            dist.barrier()
         torch.cuda.synchronize()
-        stage_ms.append(timer(step, max(5, args.steps // 2)))
+        stage_ms.append(timer(step, max(5, steps // 2)))
         runner.flags &= ~native.FLAG_EXCHANGE_SPLIT
-    step()  # a whole step last: the peer protocol's step counter advances again
+    step()  # a whole step last: the exchange's step counter advances on every rank
     torch.cuda.synchronize()
     runner.check_errors()
-    t = torch.tensor(stage_ms, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    stages_us = {n: round(float(v) * 1e3, 2) for n, v in zip(names, t.tolist())}
-    peak, _ = measured_peak()
+    t = torch.tensor([t1_ms, tn_ms] + stage_ms, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t1_ms, tn_ms, *stage_ms = t.tolist()
+
+    # ---- the combined output against the one-GPU step on the same rows; rank 0 keeps the
+    # inputs for the oracle check of its CPU leg (check_sequence_sharded)
+    rel1 = float((out.float() - one.float()).abs().max() / one.float().abs().max())
+    check_inputs = None
+    if rank == 0:
+        check_inputs = {"q": q.float().cpu().numpy(), "kv_a": kv_a.float().cpu().numpy(),
+                        "rows": rows.float().cpu().numpy(), "out": out.float().cpu().numpy(), "T": T}
     torch.cuda.synchronize()
-    dist.barrier()
+    if dist is not None:
+        dist.barrier()
     if ex is not None:
         ex.close()
+    if dist is not None:
+        dist.barrier()
+    peak, _ = measured_peak()
+    how = (f"peer exchange of {16 * native.SHARD_STRIDE * 4} B partials per GPU: K3 stores them into every rank's "
+           "buffer over NVLink (64-bit stores tagged with the step) and combines them where its grid is resident "
+           "at once, else K4 does; no collective library in the step" if ex is not None else
+           f"NCCL all-gather of {16 * native.SHARD_STRIDE * 4} B partials per GPU, then mla_combine_shards")
+    return {
+        "workload": "config5b", "context": T, "n_gpus": world, "exchange": exchange, "how": how,
+        "us_per_layer_step": round(tn_ms * 1e3, 3), "kv_gbs": round(kv_b / (tn_ms * 1e-3) / 1e9, 1),
+        "kv_frac_of_hbm_peak_per_gpu": round(kv_b / world / (tn_ms * 1e-3) / 1e9 / peak, 4),
+        "one_gpu_us_per_layer_step": round(t1_ms * 1e3, 3),
+        "strong_scaling_efficiency": round(t1_ms / (world * tn_ms), 4),
+        "speedup_vs_one_gpu": round(t1_ms / tn_ms, 3),
+        "stages_us": {n: round(v * 1e3, 2) for n, v in zip(names, stage_ms)},
+        "kv_bytes_per_step": kv_b, "kv_bytes_per_gpu": kv_b // world,
+        "l2": timer.describe(), "timing": "device time per step, CUDA events, max over ranks",
+        "max_rel_vs_one_gpu": rel1, "check": None, "_check_inputs": check_inputs,
+    }
+
+
+def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torch.device, dist) -> None:
+    """`--workload config5b` under torchrun: the sequence-sharded step alone, as its own
+    bench line (strong scaling)."""
+    clocks = ClockSampler(local_rank)
+    with clocks:
+        blk = sequence_sharded_block(args, rank, world, dev, dist, exchange=args.exchange)
+    inp = blk.pop("_check_inputs")
+    cpu = None
+    if rank == 0:  # CPU leg: the oracle's check of the combined output, and the CPU baseline
+        blk["check"] = check_sequence_sharded(inp)
+        if not args.no_cpu_baseline:
+            cpu = cpu_oracle_sample("config5b", args.cpu_seconds, faithful=False)
+            for k in ("seconds", "bytes", "requests"):
+                cpu.pop(k, None)
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
         return
-    value = kv_b / (ms_max * 1e-3) / 1e9
+    us = blk["us_per_layer_step"]
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "strong",
+        "metric": METRIC, "value": blk["kv_gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(us * 1e-3, 6), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) latents, N(0,0.02) weights)",
-        "config": {"workload": "config5b", "batch": 1, "context": T, "page_size": 64,
-                   "parallelism": (f"sequence-sharded x{world}: page-aligned KV ranges, " +
-                                   (f"peer exchange of {16 * native.SHARD_STRIDE * 4} B partials per GPU (K3 stores "
-                                    "into every rank's buffer over NVLink, K4 waits on flags and combines; no NCCL "
-                                    "in the step)" if ex is not None else
-                                    f"NCCL all-gather of {16 * native.SHARD_STRIDE * 4} B partials per GPU, "
-                                    "fixed-order combine")),
-                   "kv_bytes_per_step": kv_b, "kv_bytes_per_gpu": kv_b // world,
-                   "l2": timer.describe()},
-        "us_per_layer_step": round(ms_max * 1e3, 3),
-        "kv_frac_of_hbm_peak_per_gpu": round(value / world / peak, 4),
+        "config": {"workload": "config5b", "batch": 1, "context": blk["context"], "page_size": 64,
+                   "parallelism": f"sequence-sharded x{world}: page-aligned KV ranges, {blk['how']}",
+                   "kv_bytes_per_step": blk["kv_bytes_per_step"], "kv_bytes_per_gpu": blk["kv_bytes_per_gpu"],
+                   "l2": blk["l2"]},
+        "us_per_layer_step": us,
+        "kv_frac_of_hbm_peak_per_gpu": blk["kv_frac_of_hbm_peak_per_gpu"],
         "gpu_launches": (native.load_library().mla_launches_per_step() + 1) * args.steps,
-        "exchange": args.exchange,
-        "stages_us": stages_us,
+        "sequence_sharded": blk,
+        "cpu_baseline": cpu,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
+
+
+def other_config_summary(name: str, dev: torch.device, steps: int, peak: float) -> dict:
+    """One of the other benchmark configurations on this GPU, for the headline line's
+    `other_configs`: the graph step (K1-K3, CUDA graph) after an L2 flush (if the step reads
+    less than 4x L2) and device time per kernel, each kernel alone after a flush."""
+    wl, lengths, runner, cache, x_n, q, kv_a = build_workload(name, dev, 0)
+    B = len(lengths)
+    stream = torch.cuda.current_stream(dev)
+    kv_b = workloads.kv_bytes(lengths)
+    out = torch.empty(B, 2048, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        runner.attend(q, kv_a, cache, out)
+    out_g = torch.empty_like(out)
+    graph = fleet.DecodeGraph(runner, cache, inputs="qkv", q=q, kv_a=kv_a, out=out_g)
+    for _ in range(3):
+        graph.replay()
+    runner.attend(q, kv_a, cache, out)
+    torch.cuda.synchronize()
+    if not torch.equal(out_g, out):
+        raise RuntimeError(f"{name}: graph step output differs from the eager step")
+    runner.check_errors()
+    timer = StepTimer(stream, kv_b, dev)
+    ms = timer(graph.replay, steps)
+    p = runner.params(q, kv_a, cache, out)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    lib = runner.lib
+    k1 = timer(lambda: lib.mla_prologue(ctypes.byref(p), sptr), steps)
+    k2 = timer(lambda: lib.mla_attention(ctypes.byref(p), sptr), steps)
+    k3 = timer(lambda: lib.mla_merge_uv(ctypes.byref(p), sptr), steps)
+    torch.cuda.synchronize()
+    runner.check_errors()
+    gbs = kv_b / (ms * 1e-3) / 1e9
+    return {"batch": B, "context": lengths[0] if len(set(lengths)) == 1 else [min(lengths), max(lengths)],
+            "us_per_layer_step": round(ms * 1e3, 2), "kv_gbs": round(gbs, 1),
+            "kv_frac_of_hbm_peak": round(gbs / peak, 4), "kv_bytes": kv_b,
+            "stages_us": {"prologue": round(k1 * 1e3, 2), "attention": round(k2 * 1e3, 2),
+                          "merge_uv": round(k3 * 1e3, 2)},
+            "attention_frac_of_hbm_peak": round(kv_b / (k2 * 1e-3) / 1e9 / peak, 4),
+            "l2": "flushed before every timed call" if timer.flush is not None else "no flush (> 4x L2 per step)"}
 
 
 def run_split_sweep(args, runner, cache, q, kv_a, lengths, stream) -> None:
@@ -623,6 +830,8 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU baseline sample: seconds of oracle work on the host cores (about 10-30 s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="headline only: skip other_configs (N = 1) and the sequence-sharded block (N > 1)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="config5b on N > 1 GPUs: how the shard partials move (peer memory or NCCL)")
     ap.add_argument("--sweep-splits", type=lambda v: [int(x) for x in v.split(",")], default=None,

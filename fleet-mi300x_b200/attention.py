@@ -16,6 +16,8 @@ Everything after the GEMM runs in the C-ABI library; there is no CPU path.
 from __future__ import annotations
 
 import ctypes
+import weakref
+from collections import OrderedDict
 from dataclasses import dataclass
 
 import numpy as np
@@ -86,6 +88,10 @@ class MlaDecodeAttention:
             raise ValueError("kernel must be 'mma' (m16n8k16, default) or 'tcgen05'")
         self.flags = native.FLAG_CHECK_KERNEL if check_kernel else (native.FLAG_TCGEN05 if kernel == "tcgen05" else 0)
         self.error_word = torch.zeros(1, dtype=torch.int32, device=dev)
+        # pinned host copy of the error word: the kernels store a code into it when they
+        # record one (MlaDecodeParams.error_host), so the host sees a failed step
+        # without synchronising, also when the step was replayed from a CUDA graph
+        self.error_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._ws: torch.Tensor | None = None
         self._step_key: tuple | None = None   # attend(): params of the last call, reused for the same tensors
         self._step_p: native.MlaDecodeParams | None = None
@@ -123,6 +129,7 @@ class MlaDecodeAttention:
         p.out = _ptr(out)
         p.out_stride = _row_stride(out) if out is not None else self.cfg.heads * self.cfg.v_head
         p.error_word = _ptr(self.error_word)
+        p.error_host = _ptr(self.error_host)
         p.num_ctas = self.num_ctas
         p.flags = self.flags | (0 if new_row else native.FLAG_NO_NEW_ROW)
         p.rope_pos = _ptr(rope_pos)
@@ -157,7 +164,8 @@ class MlaDecodeAttention:
     # ------------------------------------------------------------------ calls
     def attend(self, q: torch.Tensor, kv_a: torch.Tensor, cache: PagedLatentCache,
                out: torch.Tensor | None = None, stage: str = "all", *, rope_pos: torch.Tensor | None = None,
-               shard_out: torch.Tensor | None = None, new_row: bool = True, exchange=None) -> torch.Tensor:
+               shard_out: torch.Tensor | None = None, new_row: bool = True, exchange=None,
+               check: bool | str = True) -> torch.Tensor:
         """K1+K2+K3 from q [B, 3072] and kv_a [B, 576] (bf16 views allowed).
         Appends each request's row at seq_lens[b]; does not advance seq_lens.
 
@@ -167,7 +175,12 @@ class MlaDecodeAttention:
         R(out), to be gathered and combined with `combine_shards`, or `exchange`
         (this rank's distributed.ExchangeBuffers) moves the partials between the
         ranks' GPUs inside the step, which then returns the combined R(out) (stage
-        "combine" runs K4 alone)."""
+        "combine" runs K4 alone).
+
+        `check` (see raise_pending): True raises, before launching, a device error
+        that an earlier call recorded (no synchronisation); "sync" also waits for this
+        call and raises its own error; False skips both."""
+        self._pre_check(check)
         self._check_inputs(q, kv_a, cache)
         if exchange is not None:
             if shard_out is not None:
@@ -196,12 +209,14 @@ class MlaDecodeAttention:
               "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv,
               "combine": self.lib.mla_exchange_combine}[stage]
         native.check(fn(ctypes.byref(p), stream), f"mla {stage}", p)
+        self._post_check(check)
         return out if shard_out is None else shard_out
 
     def attend_x(self, x_n: torch.Tensor, cache: PagedLatentCache, out: torch.Tensor | None = None,
-                 stage: str = "all") -> torch.Tensor:
+                 stage: str = "all", *, check: bool | str = True) -> torch.Tensor:
         """The whole slice in the library, from the post-RMSNorm hidden state x_n
         [B, 2048] bf16 (B <= 64): K0 projects q | kv_a, then K1-K3 as in attend()."""
+        self._pre_check(check)
         self._check_x(x_n, cache)
         if out is None:
             out = torch.empty(x_n.shape[0], self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16,
@@ -218,10 +233,12 @@ class MlaDecodeAttention:
         fn = {"all": self.lib.mla_decode_step, "project": self.lib.mla_project, "prologue": self.lib.mla_prologue,
               "attention": self.lib.mla_attention, "merge": self.lib.mla_merge_uv}[stage]
         native.check(fn(ctypes.byref(p), stream), f"mla {stage}", p)
+        self._post_check(check)
         return out
 
     def attention_block(self, x_n: torch.Tensor, cache: PagedLatentCache, residual: torch.Tensor,
-                        h_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                        h_out: torch.Tensor | None = None, out: torch.Tensor | None = None, *,
+                        check: bool | str = True) -> torch.Tensor:
         """The attention half of a decoder layer (reference_decode.py:300):
         h_out = R(residual + R(W_o R(attention(x_n)))), with R(out) left in `out`.
         Decode batches (<= 64 requests) run as one library call, K0 through K5;
@@ -240,13 +257,15 @@ class MlaDecodeAttention:
                  and residual.stride(-1) == 1 and h_out.stride(-1) == 1 and _row_stride(residual) % 4 == 0
                  and _row_stride(h_out) % 4 == 0)
         if not fused:
-            attn = self(x_n, cache, out)
+            attn = self(x_n, cache, out, check=check)
             h_out.copy_(residual + torch.nn.functional.linear(attn, self.w_o))
             return h_out
+        self._pre_check(check)
         self._check_x(x_n, cache)
         p = self.params(None, None, cache, out, x_n=x_n, residual=residual, h_out=h_out)
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         native.check(self.lib.mla_decode_step(ctypes.byref(p), stream), "mla attention block", p)
+        self._post_check(check)
         return h_out
 
     def _check_x(self, x_n: torch.Tensor, cache: PagedLatentCache) -> None:
@@ -269,21 +288,46 @@ class MlaDecodeAttention:
         return qkv[:, :nq], qkv[:, nq:]
 
     def __call__(self, x_n: torch.Tensor, cache: PagedLatentCache,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, *, check: bool | str = True) -> torch.Tensor:
         """x_n -> R(out). Decode batches (<= 64 requests) run the projection in the
         library (attend_x: a weight stream at HBM rate); larger batches, where the
-        projection is a compute-bound GEMM, use cuBLAS and then attend()."""
+        projection is a compute-bound GEMM, use cuBLAS and then attend(). `check` as
+        in attend()."""
         if x_n.shape[0] <= native.MAX_PROJECT_BATCH and x_n.stride(-1) == 1 and \
                 x_n.data_ptr() % 16 == 0 and _row_stride(x_n) % 8 == 0:
-            return self.attend_x(x_n, cache, out)
+            return self.attend_x(x_n, cache, out, check=check)
+        self._pre_check(check)
         q, kv_a = self.project(x_n)
-        return self.attend(q, kv_a, cache, out)
+        return self.attend(q, kv_a, cache, out, check=check)
+
+    # ------------------------------------------------------------------ device errors
+    def raise_pending(self) -> None:
+        """Raise MlaError if a kernel of an earlier call (eager or replayed from a graph)
+        has recorded a device error. Reads the pinned host word the kernels store the
+        code into; no synchronisation, so a step still running is seen once it has
+        stored. Clears both words before raising."""
+        code = int(self.error_host[0])
+        if code:
+            self.error_host.zero_()
+            if not torch.cuda.is_current_stream_capturing():
+                self.error_word.zero_()
+            raise native.MlaError(code, "device (a step since the last check)")
+
+    def _pre_check(self, check) -> None:
+        if check and not torch.cuda.is_current_stream_capturing():
+            self.raise_pending()
+
+    def _post_check(self, check) -> None:
+        if check == "sync" and not torch.cuda.is_current_stream_capturing():
+            torch.cuda.current_stream(self.device).synchronize()
+            self.raise_pending()
 
     def check_errors(self, reset: bool = True) -> None:
-        """Raise if a kernel recorded a device error (synchronises)."""
-        code = int(self.error_word.item())
+        """Raise if a kernel recorded a device error (synchronises with the device)."""
+        code = int(self.error_word.item()) or int(self.error_host[0])
         if reset and code:
             self.error_word.zero_()
+            self.error_host.zero_()
         if code:
             raise native.MlaError(code, "device")
 
@@ -324,6 +368,10 @@ def attention_absorbed(cfg: ModelConfig, w: LayerWeights, x_n: torch.Tensor, cac
     caller advances positions (cache.advance()).
     Returns R(out): bf16 [B, heads*v_head] (or [heads*v_head] for 1-D x_n), the
     head-concatenated attention output before o_proj.
+    Without `runner`, one MlaDecodeAttention per weight set is kept (up to 64, the
+    layers of a model), so that repeated calls reuse its fused weight and workspace.
+    A device error that an earlier call recorded (bad page, bad position) is raised
+    at the next call, without synchronising (MlaDecodeAttention.raise_pending).
     """
     squeeze = x_n.dim() == 1
     if squeeze:
@@ -334,6 +382,30 @@ def attention_absorbed(cfg: ModelConfig, w: LayerWeights, x_n: torch.Tensor, cac
     if runner is None:
         if cos is None or sin is None:
             raise ValueError("cos/sin tables are required (device_rope_tables)")
-        runner = MlaDecodeAttention(cfg, w, cos, sin)
+        runner = _cached_runner(cfg, w, cos, sin)
     out = runner(x_n, cache)
     return out[0] if squeeze else out
+
+
+# attention_absorbed without `runner=`: one MlaDecodeAttention per weight set (the layers
+# of a model), so that a decode loop does not rebuild the 14.9 MB fused [W_q; W_kv_a] and
+# a workspace at every token. An entry is reused only for the very same tensor objects,
+# unmodified since (torch's in-place version counter) and the same config; the runner
+# holds them alive, so the cache is bounded.
+_RUNNER_CACHE_SIZE = 64
+_runners: "OrderedDict[tuple, tuple[list, MlaDecodeAttention]]" = OrderedDict()
+
+
+def _cached_runner(cfg: ModelConfig, w: LayerWeights, cos: torch.Tensor, sin: torch.Tensor) -> MlaDecodeAttention:
+    tensors = (w.q_proj, w.kv_a_proj_with_mqa, w.kv_a_layernorm, w.kv_b_proj, cos, sin)
+    key = tuple((t.data_ptr(), tuple(t.shape), t.dtype, t._version) for t in tensors) + (
+        cfg.softmax_scale, cfg.rms_eps)
+    hit = _runners.get(key)
+    if hit is not None and all(r() is t for r, t in zip(hit[0], tensors)):
+        _runners.move_to_end(key)
+        return hit[1]
+    runner = MlaDecodeAttention(cfg, w, cos, sin)
+    _runners[key] = ([weakref.ref(t) for t in tensors], runner)
+    while len(_runners) > _RUNNER_CACHE_SIZE:
+        _runners.popitem(last=False)
+    return runner

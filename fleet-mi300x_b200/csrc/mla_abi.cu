@@ -293,6 +293,16 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
     st = device_info(&sms);
     if (st != MLA_OK) return st;
     *out = *p;
+    if (p->error_host) {  // must be pinned host memory that the device can store into
+        if (!aligned(p->error_host, 4)) return MLA_E_MISALIGNED;
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, p->error_host) != cudaSuccess || a.type != cudaMemoryTypeHost ||
+            !a.devicePointer) {
+            cudaGetLastError();
+            return MLA_E_INVALID_ARG;
+        }
+        out->error_host = static_cast<int32_t*>(a.devicePointer);
+    }
     st = resolve_ctas(p, &out->num_ctas);
     if (st != MLA_OK) return st;
     const WsLayout ws = ws_layout(*out);

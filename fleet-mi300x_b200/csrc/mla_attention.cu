@@ -136,15 +136,15 @@ __global__ void __launch_bounds__(kK2Threads, 1)
                 MLA_STAMP((int)t, 0);
                 if (cur.first()) {
                     const int qs = q_fill % kNQ, n = q_fill / kNQ;
-                    if (n > 0 && !(ok = mbar_wait(&S.q_empty[qs], (n - 1) & 1, abort, p.error_word))) break;
+                    if (n > 0 && !(ok = mbar_wait(&S.q_empty[qs], (n - 1) & 1, abort, err_sink(p)))) break;
                     mbar_arrive_expect_tx(&S.q_full[qs], kQBytes);
                     tma_load_3d(q_s + qs * kQBytes, &tmap_q, &S.q_full[qs], 0, cur.b * kQRows, 0, kCacheEvictLast);
                     ++q_fill;
                 }
                 int page = p.block_table[(int64_t)cur.b * p.max_blocks + cur.page_index()];
-                if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
+                if (page < 0 || page >= p.n_pages) { record_error(err_sink(p), MLA_DEV_BAD_PAGE); page = 0; }
                 const uint32_t slot = t % kNTile, n = t / kNTile;
-                if (n > 0 && !(ok = mbar_wait(&S.tile_empty[slot], (n - 1) & 1, abort, p.error_word))) break;
+                if (n > 0 && !(ok = mbar_wait(&S.tile_empty[slot], (n - 1) & 1, abort, err_sink(p)))) break;
                 mbar_arrive_expect_tx(&S.tile_full[slot], kTileBytes);
                 tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.tile_full[slot], 0, 0, 0, page, kCacheEvictFirst);
                 MLA_STAMP((int)t, 1);
@@ -152,11 +152,11 @@ __global__ void __launch_bounds__(kK2Threads, 1)
             // Drain: every issued copy must land before the CTA's shared memory is released.
             for (uint32_t sl = 0; sl < kNTile; ++sl) {
                 const uint32_t fills = t / kNTile + (sl < t % kNTile ? 1u : 0u);
-                if (fills) mbar_drain(&S.tile_full[sl], (fills - 1) & 1, p.error_word);
+                if (fills) mbar_drain(&S.tile_full[sl], (fills - 1) & 1, err_sink(p));
             }
             for (int qs = 0; qs < kNQ; ++qs) {
                 const int fills = q_fill / kNQ + (qs < q_fill % kNQ ? 1 : 0);
-                if (fills) mbar_drain(&S.q_full[qs], (fills - 1) & 1, p.error_word);
+                if (fills) mbar_drain(&S.q_full[qs], (fills - 1) & 1, err_sink(p));
             }
         }
     } else if (warp == 1) {
@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
                     if (idle == 64) {
                         idle_t0 = now;
                     } else if (now - idle_t0 > kWaitLimitNs) {
-                        record_error(p.error_word, MLA_DEV_TIMEOUT);
+                        record_error(err_sink(p), MLA_DEV_TIMEOUT);
                         *abort = 1;
                         break;
                     }
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
             }
             // Drain all issued MMAs before TMEM is freed.
             tc_commit(&S.teardown);
-            mbar_drain(&S.teardown, 0, p.error_word);
+            mbar_drain(&S.teardown, 0, err_sink(p));
         }
     } else {
         // ------------------------------------------------------------ softmax + epilogue
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
 #pragma unroll
                 for (int h = 0; h < 16; ++h) { m_run[h] = -INFINITY; l_thr[h] = 0.f; }
             }
-            if (!mbar_wait(&S.s_full[i & 1], (i >> 1) & 1, abort, p.error_word)) break;
+            if (!mbar_wait(&S.s_full[i & 1], (i >> 1) & 1, abort, err_sink(p))) break;
             tc_fence_after();
             __syncwarp();
             if (wg_tid == 0) MLA_STAMP(i, 6);
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
                         m_run[h] = mn;
                         l_thr[h] *= f[h];
                     }
-                    if (!mbar_wait(&S.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, abort, p.error_word)) break;
+                    if (!mbar_wait(&S.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, abort, err_sink(p))) break;
                     tc_fence_after();
                     __syncwarp();
 #pragma unroll
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
                 l_thr[h] += e;
             }
             // P buffer (i & 1) is free once the output MMA of tile i-2 is done.
-            if (i >= 2 && !mbar_wait(&S.pv_done[i & 1], ((i - 2) >> 1) & 1, abort, p.error_word)) break;
+            if (i >= 2 && !mbar_wait(&S.pv_done[i & 1], ((i - 2) >> 1) & 1, abort, err_sink(p))) break;
             if (lane < 16) {
                 uint8_t* pb = p_s + (i & 1) * kPBytes;
 #pragma unroll
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
                 // C tile too so that 0 * (stale or non-finite bits) cannot
                 // reach the output MMA.
                 const uint32_t slot = (uint32_t)i % kNTile;
-                if (!mbar_wait(&S.tile_full[slot], ((uint32_t)i / kNTile) & 1, abort, p.error_word)) break;
+                if (!mbar_wait(&S.tile_full[slot], ((uint32_t)i / kNTile) & 1, abort, err_sink(p))) break;
                 const int nrows = kPage - valid;
                 const int per_chunk = nrows * 8;
                 uint8_t* base = tile_s + slot * kTileBytes;
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kK2Threads, 1)
             if (wg_tid == 0) MLA_STAMP(i, 7);
 
             if (last) {
-                if (!mbar_wait(&S.pv_done[i & 1], (i >> 1) & 1, abort, p.error_word)) break;
+                if (!mbar_wait(&S.pv_done[i & 1], (i >> 1) & 1, abort, err_sink(p))) break;
                 tc_fence_after();
                 const float lsum = warp_reduce16_transposed<false>(l_thr, lane);
                 if (lane < 16) S.lred[sp][lane] = lsum;
@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(kCkThreads)
             m_run = -INFINITY; l_run = 0.f;
         }
         int page = p.block_table[(int64_t)cur.b * p.max_blocks + cur.page_index()];
-        if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
+        if (page < 0 || page >= p.n_pages) { record_error(err_sink(p), MLA_DEV_BAD_PAGE); page = 0; }
         const int valid = cur.tokens();
         __syncthreads();
         {

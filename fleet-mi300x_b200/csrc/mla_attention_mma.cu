@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     uint32_t issued = 0;
     auto issue_next = [&]() {
         int page = p.block_table[(int64_t)la.b * p.max_blocks + la.page_index()];
-        if (page < 0 || page >= p.n_pages) { record_error(p.error_word, MLA_DEV_BAD_PAGE); page = 0; }
+        if (page < 0 || page >= p.n_pages) { record_error(err_sink(p), MLA_DEV_BAD_PAGE); page = 0; }
         const uint32_t slot = issued % kNSlot;
         mbar_arrive_expect_tx(&S.full[slot], kTileBytes);
         tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.full[slot], 0, kHalf * la_half, 0, page,
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 const int hvalid = min(kHalf, valid - kHalf * hh);  // valid tokens of this half page
                 const bool tile_first = first && hh == 0;
                 const uint32_t slot = i % kNSlot;
-                if (!mbar_wait(&S.full[slot], (i / kNSlot) & 1, abort, p.error_word)) { ok = false; break; }
+                if (!mbar_wait(&S.full[slot], (i / kNSlot) & 1, abort, err_sink(p))) { ok = false; break; }
                 if (i == 0 && w == 0) MLA_TL_MARK(1, 5);  // first half page landed
                 const uint32_t tbase = tile_addr + slot * kTileBytes;
 
@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 // the leader refills this slot with the half page two ahead once all four warps released it
                 bool refill_ok = true;
                 if (leader && la.valid()) {
-                    refill_ok = mbar_wait_idle(&S.empty[slot], (i / kNSlot) & 1, abort, p.error_word);
+                    refill_ok = mbar_wait_idle(&S.empty[slot], (i / kNSlot) & 1, abort, err_sink(p));
                     if (refill_ok) issue_next();
                 }
                 if (!__shfl_sync(0xffffffffu, refill_ok, 0)) { ok = false; break; }  // reconverges the warp
@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                     if (leader) mbar_arrive(stash_bar);
                 } else {
                     if (paired && grp == 0 && cur.u == cur.u_end - 1 && cur.u_end < cur.cb1 &&
-                        mbar_wait(stash_bar, 0, abort, p.error_word)) {
+                        mbar_wait(stash_bar, 0, abort, err_sink(p))) {
                         const float2 p0 = stash_ml[g], p1 = stash_ml[g + 8];
                         const float n0 = fmaxf(m_run[0], p0.x), n1 = fmaxf(m_run[1], p1.x);
                         const float a0 = exp2f(m_run[0] - n0), b0 = exp2f(p0.x - n0);
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         if (leader) {
             for (uint32_t sl = 0; sl < kNSlot; ++sl) {
                 const uint32_t fills = issued / kNSlot + (sl < issued % kNSlot ? 1u : 0u);
-                if (fills) mbar_drain(&S.full[sl], (fills - 1) & 1, p.error_word);
+                if (fills) mbar_drain(&S.full[sl], (fills - 1) & 1, err_sink(p));
             }
         }
     }

@@ -164,10 +164,29 @@ __device__ __forceinline__ int plan_tiles(const MlaDecodeParams& p, int b) {
 }
 
 // ---------------------------------------------------------------------------
-// Error word: first error wins.
+// Device errors. A kernel reports into the caller's device word (first error
+// wins, by atomicCAS) and, if the caller gave one, into a pinned host word
+// (MlaDecodeParams.error_host), which receives the winning code by a plain
+// store over the system bus, so that the host sees the error without
+// synchronising with the stream. Only error paths touch either word.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void record_error(int32_t* w, int code) {
-    if (w) atomicCAS(w, 0, code);
+struct ErrSink {
+    int32_t* dev;
+    int32_t* host;
+};
+
+__host__ __device__ inline ErrSink err_sink(const MlaDecodeParams& p) { return ErrSink{p.error_word, p.error_host}; }
+
+__device__ __forceinline__ void record_error(const ErrSink& e, int code) {
+    int won = code;
+    if (e.dev) {
+        const int old = atomicCAS(e.dev, 0, code);
+        if (old) won = old;
+    }
+    if (e.host) {
+        *reinterpret_cast<volatile int32_t*>(e.host) = won;
+        __threadfence_system();
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -327,7 +346,7 @@ constexpr uint64_t kWaitLimitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s
 // producer waiting for a slot): each probe sleeps up to 20 us, so the waiting
 // thread takes no issue slots from the compute warps on its scheduler.
 __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               int32_t* err) {
+                                               const ErrSink& err) {
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
@@ -343,7 +362,7 @@ __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, v
 }
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int32_t* err) {
+                                          const ErrSink& err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {

@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         MLA_TL_MARK(2, 4);
         {
             int dummy = 0;
-            if (!mbar_wait(bar + 1, 0, &dummy, p.error_word)) return;
+            if (!mbar_wait(bar + 1, 0, &dummy, err_sink(p))) return;
         }
 #pragma unroll 1
         for (int rr = 0; rr < 2; ++rr) {
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     bool w_ok;
     {
         int dummy = 0;
-        w_ok = mbar_wait(bar, 0, &dummy, p.error_word);
+        w_ok = mbar_wait(bar, 0, &dummy, err_sink(p));
     }
     if (kCl == 1) MLA_TL_MARK(2, 4);  // W_UV staged (the cluster form marks its published folds)
 
@@ -555,7 +555,7 @@ __device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const
         *reinterpret_cast<uint32_t*>(out + (int64_t)b * p.out_stride + h * kV + 2 * line) =
             ok ? pack_bf16(a0 * inv, a1 * inv) : 0u;
     }
-    if (!ok) record_error(p.error_word, MLA_DEV_PEER_TIMEOUT);
+    if (!ok) record_error(err_sink(p), MLA_DEV_PEER_TIMEOUT);
 }
 
 // The W_UV MMA and its epilogue, by all eight warps of a K3 CTA: warp w takes the
@@ -799,7 +799,7 @@ __global__ void __launch_bounds__(256) k4_exchange_combine(const MlaDecodeParams
         }
     }
     if (!ok) {
-        record_error(p.error_word, MLA_DEV_PEER_TIMEOUT);
+        record_error(err_sink(p), MLA_DEV_PEER_TIMEOUT);
         fail_s = 1;
     }
     __syncthreads();

@@ -33,7 +33,7 @@ struct StreamArgs {
     const __nv_bfloat16* residual;  // EPI_RESIDUAL only
     int64_t res_stride;
     int batch;
-    int32_t* error_word;
+    ErrSink err;
 };
 
 enum StreamEpi { kEpiBf16 = 0, kEpiResidual = 1 };
@@ -88,8 +88,8 @@ __global__ void __launch_bounds__(128, 1)
             mbar_arrive_expect_tx(&bar[4], S::kXBytes);
             tma_load_3d(x_s, &tmap_x, &bar[4], 0, 16 * mt, 0, kCacheEvictLast);
         }
-        bool ok = mbar_wait(&bar[4], mt & 1, &dummy, a.error_word);
-        if (mt == 0) ok = ok && mbar_wait(&bar[warp], 0, &dummy, a.error_word);
+        bool ok = mbar_wait(&bar[4], mt & 1, &dummy, a.err);
+        if (mt == 0) ok = ok && mbar_wait(&bar[warp], 0, &dummy, a.err);
         if (!__syncthreads_and(ok)) return;  // a timed-out wait (recorded) ends the whole CTA at once
 
         constexpr int kNT = kRows / 8;  // n8 tiles of this CTA
@@ -168,7 +168,7 @@ cudaError_t k0_configure() {
 
 cudaError_t launch_project(const MlaDecodeParams& p, __nv_bfloat16* qkv, const CUtensorMap& tmap_w,
                            const CUtensorMap& tmap_x, cudaStream_t stream) {
-    StreamArgs a{qkv, kQkvRows, nullptr, 0, p.batch, p.error_word};
+    StreamArgs a{qkv, kQkvRows, nullptr, 0, p.batch, err_sink(p)};
     return launch_pdl(k_weight_stream<kK0Rows, kEpiBf16>, dim3(kQkvRows / kK0Rows), dim3(128),
                       WStream<kK0Rows>::kSmemBytes, stream, a, tmap_w, tmap_x);
 }
@@ -176,7 +176,7 @@ cudaError_t launch_project(const MlaDecodeParams& p, __nv_bfloat16* qkv, const C
 cudaError_t launch_o_proj(const MlaDecodeParams& p, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
                           cudaStream_t stream) {
     StreamArgs a{reinterpret_cast<__nv_bfloat16*>(p.h_out), p.h_out_stride,
-                 reinterpret_cast<const __nv_bfloat16*>(p.residual), p.residual_stride, p.batch, p.error_word};
+                 reinterpret_cast<const __nv_bfloat16*>(p.residual), p.residual_stride, p.batch, err_sink(p)};
     return launch_pdl(k_weight_stream<kK5Rows, kEpiResidual>, dim3(kHidden / kK5Rows), dim3(128),
                       WStream<kK5Rows>::kSmemBytes, stream, a, tmap_w, tmap_x);
 }

@@ -59,7 +59,7 @@ __device__ void plan_scan(const MlaDecodeParams& p, int32_t* cum, int32_t* cum_s
         const int b = base + threadIdx.x;
         int n = 0;
         if (b < p.batch) {
-            if (!request_ok(p, b)) record_error(p.error_word, MLA_DEV_BAD_POSITION);
+            if (!request_ok(p, b)) record_error(err_sink(p), MLA_DEV_BAD_POSITION);
             else n = plan_tiles(p, b);
         }
         int incl = n;
@@ -160,7 +160,7 @@ __device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b,
     float lo, hi;
     kv_post_finish(kin, p.rms_eps, cs, sn, lane, outc, lo, hi);
     if (page < 0 || page >= p.n_pages) {
-        if (lane == 0) record_error(p.error_word, MLA_DEV_BAD_PAGE);
+        if (lane == 0) record_error(err_sink(p), MLA_DEV_BAD_PAGE);
         return;
     }
     kv_post_store(reinterpret_cast<__nv_bfloat16*>(p.kv_cache) + ((int64_t)page * kPage + pos % kPage) * kRow, outc,
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
     named_bar_sync(1, kK1MmaWarps * 32);  // q_nope staged, barrier initialised
     {
         int dummy = 0;
-        if (!mbar_wait(bar, 0, &dummy, p.error_word)) return;
+        if (!mbar_wait(bar, 0, &dummy, err_sink(p))) return;
     }
     // D[64 requests][128] = A[64][128 d] x W_UK[h][128 d][128 l]; warp w owns l in [32w, 32w+32)
     const int gq = lane >> 2, t4 = lane & 3, m8 = lane >> 3, r8 = lane & 7;

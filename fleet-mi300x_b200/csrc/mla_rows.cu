@@ -38,13 +38,13 @@ __global__ void __launch_bounds__(kRowsThreads) k_rows_to_pages(const MlaRowsToP
         const int64_t pos64 = (r.first_pos ? r.first_pos[b] : 0) + (i - r.row_start[b]);
         const bool raw = r.mode == MLA_ROWS_RAW;
         if (pos64 < 0 || pos64 >= (int64_t)r.max_blocks * kPage || (raw && pos64 >= r.max_pos)) {
-            if (lane == 0) record_error(r.error_word, MLA_DEV_BAD_POSITION);
+            if (lane == 0) record_error(ErrSink{r.error_word, nullptr}, MLA_DEV_BAD_POSITION);
             continue;
         }
         const int pos = (int)pos64;
         const int page = r.block_table[(int64_t)b * r.max_blocks + pos / kPage];
         if (page < 0 || page >= r.n_pages) {
-            if (lane == 0) record_error(r.error_word, MLA_DEV_BAD_PAGE);
+            if (lane == 0) record_error(ErrSink{r.error_word, nullptr}, MLA_DEV_BAD_PAGE);
             continue;
         }
         const __nv_bfloat16* src = rows + i * r.rows_stride;

@@ -5,6 +5,7 @@
 // The three kernels and their checks are those of mla_decode_step; only the
 // workspace pointer differs. Nothing is allocated: the array is part of this
 // file's device image, and its address is looked up once per device.
+#include <atomic>
 #include <mutex>
 
 #include "mla_common.cuh"
@@ -20,21 +21,32 @@ static __device__ __align__(256) unsigned char g_static_scratch[MLA_STATIC_SCRAT
 constexpr int kMaxDevices = 64;
 
 struct ScratchSlot {
-    std::once_flag once;
-    cudaError_t err = cudaErrorInitializationError;
-    void* ptr = nullptr;
+    std::mutex mu;                    // serialises the lookup
+    std::atomic<void*> ptr{nullptr};  // set once a lookup has succeeded; a failed one is retried
 };
 ScratchSlot g_slots[kMaxDevices];
 
 // Device address of g_static_scratch on the current device, looked up at the
-// first call on that device (with that device current).
+// first call on that device (with that device current). Only a successful
+// lookup is kept, so a first call that failed (made during a stream capture,
+// say) does not disable the entry point: the next call looks it up again.
 int static_scratch(void** ptr) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MLA_E_LAUNCH;
     ScratchSlot& s = g_slots[dev];
-    std::call_once(s.once, [&s]() { s.err = cudaGetSymbolAddress(&s.ptr, g_static_scratch); });
-    if (s.err != cudaSuccess || s.ptr == nullptr) return MLA_E_LAUNCH;
-    *ptr = s.ptr;
+    void* p = s.ptr.load(std::memory_order_acquire);
+    if (!p) {
+        std::lock_guard<std::mutex> lock(s.mu);
+        p = s.ptr.load(std::memory_order_relaxed);
+        if (!p) {
+            if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr) {
+                cudaGetLastError();  // leave no error behind for the caller's next CUDA call
+                return MLA_E_LAUNCH;
+            }
+            s.ptr.store(p, std::memory_order_release);
+        }
+    }
+    *ptr = p;
     return MLA_OK;
 }
 

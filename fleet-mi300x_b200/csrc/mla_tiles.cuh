@@ -87,7 +87,7 @@ __device__ __forceinline__ float warp_reduce16_transposed(const float (&v)[16], 
 
 // Wait that ignores the abort flag (used only to drain in-flight copies and
 // MMAs before the CTA exits); still bounded in time.
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int32_t* err) {
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, const ErrSink& err) {
     int dummy = 0;
     mbar_wait(bar, parity, &dummy, err);
 }

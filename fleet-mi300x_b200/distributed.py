@@ -2,7 +2,7 @@
 
 Two partitions of the attention task:
 
-* **By request** (many independent sequences, BASELINE config 5a): each rank owns
+* **By request** (many independent sequences, config 5a): each rank owns
   whole requests, their pages and block-table rows. There is no collective in the
   step; `request_shard` picks a rank's requests, balanced by cache rows.
 * **By sequence** (one very long sequence, config 5b): each rank owns a

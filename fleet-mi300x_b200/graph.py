@@ -11,6 +11,11 @@ device memory when they run, so one graph serves every step of a decode loop: wr
 the next x_n into `graph.x_n` (or q / kv_a into `graph.q` / `graph.kv_a`), replay,
 read `graph.out`. With `advance=True` the graph also adds 1 to `seq_lens`, as the
 caller of the eager step does after each call.
+
+Device errors (a bad block-table entry or position, a timed-out wait) reach the host
+without a synchronisation: the captured kernels store the code into the runner's
+pinned host word (MlaDecodeParams.error_host), and every replay / submit / wait here
+raises MlaError if an earlier step recorded one (MlaDecodeAttention.raise_pending).
 """
 from __future__ import annotations
 
@@ -66,9 +71,16 @@ class DecodeGraph:
             self.runner.attend(self.q, self.kv_a, self.cache, self.out)
 
     def replay(self) -> torch.Tensor:
-        """Run the captured step on the current stream; returns `out`."""
+        """Run the captured step on the current stream; returns `out`. Raises first if
+        an earlier step recorded a device error."""
+        self.runner.raise_pending()
         self.graph.replay()
         return self.out
+
+    def synchronize(self) -> None:
+        """Wait for the current stream and raise if a step recorded a device error."""
+        torch.cuda.current_stream(self.runner.device).synchronize()
+        self.runner.raise_pending()
 
 
 class HostPipeline:
@@ -87,6 +99,7 @@ class HostPipeline:
         cfg, dev, B = runner.cfg, runner.device, cache.batch
         bf = torch.bfloat16
         self.device = dev
+        self.runner = runner
         self.x_dev = [torch.zeros(B, cfg.hidden, dtype=bf, device=dev) for _ in range(2)]
         self.out_dev = [torch.empty(B, cfg.heads * cfg.v_head, dtype=bf, device=dev) for _ in range(2)]
         self.out_host = [torch.empty(B, cfg.heads * cfg.v_head, dtype=bf).pin_memory() for _ in range(2)]
@@ -102,7 +115,9 @@ class HostPipeline:
         self._used = [False, False]
 
     def submit(self, x_host: torch.Tensor) -> torch.Tensor:
-        """Queue one step whose input is the pinned host tensor x_host [B, hidden] bf16."""
+        """Queue one step whose input is the pinned host tensor x_host [B, hidden] bf16.
+        Raises first if an earlier step recorded a device error."""
+        self.runner.raise_pending()
         i = self.k % 2
         with torch.cuda.stream(self.h2d):
             if self._used[i]:
@@ -124,9 +139,11 @@ class HostPipeline:
         return self.out_host[i]
 
     def wait(self) -> None:
-        """Block until every submitted step's R(out) is in host memory."""
+        """Block until every submitted step's R(out) is in host memory; raise MlaError
+        if any of them recorded a device error."""
         for st in (self.h2d, self.compute, self.d2h):
             st.synchronize()
+        self.runner.raise_pending()
 
 
 class HostStepGraph:
@@ -168,6 +185,13 @@ class HostStepGraph:
 
     def replay(self) -> torch.Tensor:
         """Queue the step on the current stream; returns `out_host` (valid once the
-        stream has reached this point)."""
+        stream has reached this point). Raises first if an earlier step recorded a
+        device error."""
+        self.runner.raise_pending()
         self.graph.replay()
         return self.out_host
+
+    def synchronize(self) -> None:
+        """Wait for the current stream and raise if a step recorded a device error."""
+        torch.cuda.current_stream(self.runner.device).synchronize()
+        self.runner.raise_pending()

@@ -13,7 +13,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libmla_decode.so"
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 HEADS, QK_NOPE, QK_ROPE, V_HEAD, KV_LORA, PAGE_SIZE = 16, 128, 64, 128, 512, 64
 ROW = KV_LORA + QK_ROPE
 MAX_BATCH = 65536
@@ -86,6 +86,7 @@ class MlaDecodeParams(ctypes.Structure):
         ("h_out", ctypes.c_void_p), ("h_out_stride", ctypes.c_int64),
         ("exchange", ctypes.c_void_p * MAX_RANKS), ("rank", ctypes.c_int32), ("world", ctypes.c_int32),
         ("exchange_batch", ctypes.c_int32), ("exchange_timeout_us", ctypes.c_int32),
+        ("error_host", ctypes.c_void_p),
     ]
 
 

@@ -41,15 +41,15 @@ class Workload:
 
 
 WORKLOADS = {
-    # single layer, batch 1, context 1024 (the reference's NumPy case)
+    # config 1: single layer, batch 1, context 1024 (the reference's NumPy case)
     "config1": Workload("config1", 1, (1024,), permute=False, normed_cache=True, seed=0),
-    # batched paged decode, B=32, ragged contexts U[512, 8192], permuted block table
+    # config 3: batched paged decode, B=32, ragged contexts U[512, 8192], permuted block table
     "config3": Workload("config3", 32, None, 512, 8192, permute=True, seed=3),
-    # long-context split-KV, B=8 x 32768
+    # config 4: long-context split-KV, B=8 x 32768
     "config4": Workload("config4", 8, (32768,), permute=True, seed=4),
-    # configs[4] (a): B=256 x 4096, sharded by request at N > 1
+    # config 5a: B=256 x 4096, sharded by request at N > 1
     "config5a": Workload("config5a", 256, (4096,), permute=True, seed=5),
-    # configs[4] (b): one sequence of 131072 tokens, sharded by sequence at N > 1
+    # config 5b: one sequence of 131072 tokens, sharded by sequence at N > 1
     "config5b": Workload("config5b", 1, (131072,), permute=True, seed=6),
 }
 

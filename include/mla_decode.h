@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define MLA_ABI_VERSION 5
+#define MLA_ABI_VERSION 6
 
 /* Fixed model dimensions. The reference's launcher refuses any other shape
  * (src/host/fleet_launch.hip:573-577: kv_lora != 512 or qk_rope != 64);
@@ -181,6 +181,18 @@ typedef struct MlaDecodeParams {
     int32_t world;                 /* number of shards: 0 (no exchange) or 1..MLA_MAX_RANKS */
     int32_t exchange_batch;        /* the batch the buffers were sized for; batch <= exchange_batch */
     int32_t exchange_timeout_us;   /* K4's limit on waiting for a shard; 0 = 2,000,000 (2 s) */
+
+    /* Host-visible device errors (ABI v6). Optional pinned host int32 (cudaHostAlloc /
+     * cudaMallocHost memory, which unified addressing maps into the device) that a
+     * kernel stores the device error code into whenever it records one in error_word,
+     * by a plain store over the system bus. The host can then read it at any time
+     * without synchronising with the stream (a kernel's store is visible once that
+     * kernel has completed): a caller that checks it before each step learns of a
+     * failed step without a device synchronisation, and inside CUDA graphs too. The
+     * library never clears it. NULL = no host word. Any other memory is refused with
+     * MLA_E_INVALID_ARG. The reference's host polls its abort word the same way
+     * (fleet_runtime.h:194-198, read back by fleet_launch.hip:284-311). */
+    int32_t* error_host;
 } MlaDecodeParams;
 
 #define MLA_SHARD_STRIDE (MLA_V_HEAD + 4)
@@ -324,7 +336,8 @@ int mla_rows_to_pages(const MlaRowsToPages* r, void* stream);
  * ordered with one another, or from several host threads) race on it. Order
  * them on one stream or with events. The first call on a device, with that device
  * current, looks up the scratch array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture on that device. */
+ * make that first call before any stream capture on that device. A lookup that
+ * fails returns MLA_E_LAUNCH and is not remembered: the next call tries again. */
 int mla_decode_step_static(const MlaDecodeParams* p, void* stream);
 
 #ifdef __cplusplus

@@ -129,7 +129,8 @@ def known_answers(ref) -> dict:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference", help="path of the cklxx/fleet-mi300x tree")
+    ap.add_argument("--reference", required=True, help="path of a cklxx/fleet-mi300x checkout (the tree whose "
+                                                        "src/host/reference_decode.py generates the vectors)")
     a = ap.parse_args()
     sys.path.insert(0, str(Path(a.reference) / "src" / "host"))
     ref = importlib.import_module("reference_decode")

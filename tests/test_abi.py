@@ -98,8 +98,14 @@ def test_static_step_limit_matches_header_and_refuses_before_launch(lib):
     text = (ROOT / "include" / "mla_decode.h").read_text()
     m = re.search(r"#define MLA_STATIC_SCRATCH_BYTES \((\d+)ull << (\d+)\)", text)
     assert m and int(m.group(1)) << int(m.group(2)) == native.STATIC_SCRATCH_BYTES
-    # 558 requests fit at 148 CTAs, 559 do not; the refusal comes before any CUDA call
+    # 558 requests fit at 148 CTAs, 559 do not; at the default 296 CTAs of a B200, 463 fit and
+    # 464 do not; the refusal comes before any CUDA call
     assert expected_workspace(558, 148) <= native.STATIC_SCRATCH_BYTES < expected_workspace(559, 148)
+    assert expected_workspace(463, 296) <= native.STATIC_SCRATCH_BYTES < expected_workspace(464, 296)
+    for batch, ctas in ((464, 296), (600, 148)):
+        p = native.new_params()
+        p.batch, p.num_ctas = batch, ctas
+        assert lib.mla_decode_step_static(ctypes.byref(p), None) == -8  # MLA_E_LIMIT
     p = native.new_params()
     p.batch, p.num_ctas = 559, 148
     assert lib.mla_decode_step_static(ctypes.byref(p), None) == -8  # MLA_E_LIMIT

@@ -104,3 +104,57 @@ def test_host_step_graph_matches_eager_loop(cuda_device):
     runner.check_errors()
     assert torch.equal(cache_h.seq_lens, cache_e.seq_lens)
     assert torch.equal(cache_h.pages, cache_e.pages)
+
+
+def _bad_entry(cache):
+    """Point request 4's first logical page outside the pool (the kernels' bounds checks
+    record MLA_DEV_BAD_PAGE and read page 0 instead; nothing faults)."""
+    good = cache.block_table[4, 0].clone()
+    cache.block_table[4, 0] = cache.n_pages + 7
+    return good
+
+
+def test_host_pipeline_raises_device_errors_without_check_errors(cuda_device):
+    """A bad block-table entry in a pipelined decode loop surfaces as MlaError from the
+    pipeline itself (wait(), or the next submit()), with no check_errors() call; once the
+    table is repaired the loop runs on."""
+    runner, cache = _runner_and_cache(cuda_device, seed=31)
+    pipe = fleet.HostPipeline(runner, cache)
+    x = torch.randn(len(LENS), 2048, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).pin_memory()
+    pipe.submit(x)
+    pipe.wait()
+    good = _bad_entry(cache)
+    pipe.submit(x)
+    with pytest.raises(fleet.MlaError) as e:
+        pipe.wait()
+    assert e.value.code == 1
+    cache.block_table[4, 0] = good
+    pipe.submit(x)
+    pipe.wait()  # the error was cleared when it was raised
+    runner.check_errors()
+
+
+def test_decode_graph_and_eager_calls_raise_device_errors(cuda_device):
+    """The same through a replayed CUDA graph (raised by synchronize() or the next replay)
+    and through the eager call (check='sync' raises at once; the default raises at the
+    next call, without synchronising)."""
+    runner, cache = _runner_and_cache(cuda_device, seed=32)
+    graph = fleet.DecodeGraph(runner, cache)
+    graph.replay()
+    graph.synchronize()
+    good = _bad_entry(cache)
+    graph.replay()
+    with pytest.raises(fleet.MlaError) as e:
+        graph.synchronize()
+    assert e.value.code == 1
+    x = graph.x_n.clone()
+    with pytest.raises(fleet.MlaError):
+        runner(x, cache, check="sync")
+    runner(x, cache)
+    torch.cuda.synchronize(cuda_device)
+    with pytest.raises(fleet.MlaError):
+        runner(x, cache)  # raised before this call launches anything
+    cache.block_table[4, 0] = good
+    runner(x, cache, check="sync")
+    graph.replay()
+    graph.synchronize()

@@ -245,7 +245,7 @@ def test_device_errors_are_reported(cuda_device):
 
 @pytest.mark.parametrize("cfg_name,subset", [("config3", [0, 13, 31]), ("config4", [2])])
 def test_full_size_config_subset(cuda_device, cfg_name, subset):
-    """BASELINE configs 3 and 4 at full size: every request against the CUDA-core check
+    """Configs 3 and 4 at full size: every request against the CUDA-core check
     kernel, a subset against the oracle (vectorised form)."""
     wl = workloads.WORKLOADS[cfg_name]
     lengths = wl.seq_lens()

@@ -65,6 +65,62 @@ def test_static_step_equals_decode_step_on_two_calls(cuda_device):
             assert free1 == free0, "the static step allocated device memory"
 
 
+def _static_call(runner, p, dev):
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    p.workspace, p.workspace_bytes = None, 0  # ignored by the static entry point
+    native.check(runner.lib.mla_decode_step_static(ctypes.byref(p), stream), "mla_decode_step_static", p)
+    torch.cuda.synchronize(dev)
+    runner.check_errors()
+
+
+def test_static_step_with_projection_and_o_proj(cuda_device):
+    """The whole attention block from the static scratch: K0 projects q | kv_a from x_n
+    into the scratch's qkv region, K1-K3 attend, K5 applies o_proj and the residual.
+    Bit for bit equal to mla_decode_step with a caller workspace, on two calls in a row."""
+    runner, cache, _, _ = _setup(cuda_device)
+    lw = workloads.make_layer_weights(11)
+    runner.w_o = lw.o_proj.to(cuda_device).contiguous()
+    B = len(LENS)
+    g = torch.Generator().manual_seed(13)
+    x_n = workloads.make_hidden(14, B).to(cuda_device)
+    h = torch.randn(B, 2048, generator=g).to(torch.bfloat16).to(cuda_device)
+    out_w, h_w = torch.empty(B, 2048, dtype=torch.bfloat16, device=cuda_device), torch.empty_like(h)
+    p = runner.params(None, None, cache, out_w, x_n=x_n, residual=h, h_out=h_w)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    native.check(runner.lib.mla_decode_step(ctypes.byref(p), stream), "mla_decode_step", p)
+    torch.cuda.synchronize(cuda_device)
+    runner.check_errors()
+    for call in range(2):
+        out_s, h_s = torch.full_like(out_w, float("nan")), torch.full_like(h, float("nan"))
+        _static_call(runner, runner.params(None, None, cache, out_s, x_n=x_n, residual=h, h_out=h_s), cuda_device)
+        assert torch.equal(out_s, out_w), f"call {call}: R(out) differs"
+        assert torch.equal(h_s, h_w), f"call {call}: the new hidden state differs"
+
+
+def test_static_step_at_the_default_plan_limit(cuda_device):
+    """463 requests, the largest batch whose workspace fits the 32 MiB scratch at the
+    default 296 split-KV CTAs (464 is refused): equal to mla_decode_step bit for bit."""
+    B = 463
+    runner, _, _, _ = _setup(cuda_device)
+    lens = [int(x) for x in torch.randint(0, 200, (B,), generator=torch.Generator().manual_seed(15))]
+    g = torch.Generator().manual_seed(16)
+    cache = fleet.PagedLatentCache.for_lengths(lens, generator=g, device=cuda_device)
+    cache.pages.copy_(torch.randn(cache.pages.shape, generator=g).to(torch.bfloat16))
+    q = torch.randn(B, 3072, generator=g).to(torch.bfloat16).to(cuda_device)
+    kv_a = torch.randn(B, 576, generator=g).to(torch.bfloat16).to(cuda_device)
+    assert runner.workspace_bytes(B) <= native.STATIC_SCRATCH_BYTES < runner.workspace_bytes(B + 1)
+    want = runner.attend(q, kv_a, cache).clone()
+    runner.check_errors()
+    for call in range(2):
+        out = torch.full_like(want, float("nan"))
+        _static_call(runner, runner.params(q, kv_a, cache, out), cuda_device)
+        assert torch.equal(out, want), f"call {call}: static-scratch output differs at {B} requests"
+    p = runner.params(q, kv_a, cache, out)
+    p.batch = B + 1
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    assert runner.lib.mla_decode_step_static(ctypes.byref(p), stream) == -8  # MLA_E_LIMIT, before any launch
+
+
 def test_static_step_refuses_batches_beyond_its_scratch(cuda_device):
     runner, cache, q, kv_a = _setup(cuda_device)
     out = torch.zeros(len(LENS), 2048, dtype=torch.bfloat16, device=cuda_device)
