@@ -68,7 +68,12 @@ class MlaDecodeAttention:
     """
 
     def __init__(self, cfg: ModelConfig, w: LayerWeights, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
-                 *, num_ctas: int = 0, check_kernel: bool = False, kernel: str = "mma"):
+                 *, num_ctas: int = 0, check_kernel: bool = False, kernel: str = "mma", qc_hilo: bool = False,
+                 p_hilo: bool = False):
+        """qc_hilo / p_hilo (default kernel only): keep the absorbed query, and the
+        probabilities of P c_kv, as bf16 hi/lo pairs instead of rounding them to bf16
+        (MLA_FLAG_QC_HILO / MLA_FLAG_P_HILO), closer to the reference's fp32 q_c and P
+        (reference_decode.py:250-253) at the cost of more tensor-core issue in K2."""
         cfg.check_supported()
         self.cfg = cfg
         self.lib = native.load_library()
@@ -87,6 +92,9 @@ class MlaDecodeAttention:
         if kernel not in ("mma", "tcgen05"):
             raise ValueError("kernel must be 'mma' (m16n8k16, default) or 'tcgen05'")
         self.flags = native.FLAG_CHECK_KERNEL if check_kernel else (native.FLAG_TCGEN05 if kernel == "tcgen05" else 0)
+        if (qc_hilo or p_hilo) and self.flags:
+            raise ValueError("qc_hilo / p_hilo exist in the default (mma) kernel only")
+        self.flags |= (native.FLAG_QC_HILO if qc_hilo else 0) | (native.FLAG_P_HILO if p_hilo else 0)
         self.error_word = torch.zeros(1, dtype=torch.int32, device=dev)
         # pinned host copy of the error word: the kernels store a code into it when they
         # record one (MlaDecodeParams.error_host), so the host sees a failed step
@@ -335,6 +343,7 @@ class MlaDecodeAttention:
         p = native.new_params()
         p.batch = batch
         p.num_ctas = self.num_ctas
+        p.flags = self.flags
         need = ctypes.c_uint64()
         native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
         return int(need.value)

@@ -265,8 +265,11 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         if (p->x_stride < MLA_HIDDEN) return MLA_E_INVALID_ARG;
         if (!aligned(p->x_n, 16) || (p->x_stride & 7) || !aligned(p->w_qkv, 16)) return MLA_E_MISALIGNED;
     }
-    if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW | MLA_FLAG_EXCHANGE_SPLIT))
+    if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW | MLA_FLAG_EXCHANGE_SPLIT |
+                     MLA_FLAG_QC_HILO | MLA_FLAG_P_HILO))
         return MLA_E_INVALID_ARG;
+    if ((p->flags & (MLA_FLAG_QC_HILO | MLA_FLAG_P_HILO)) && (p->flags & (MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05)))
+        return MLA_E_INVALID_ARG;  // the hi/lo forms exist in the default kernel only
     if (p->world < 0 || p->world > MLA_MAX_RANKS) return MLA_E_INVALID_ARG;
     if (p->world > 0) {  // peer exchange: K3 writes every rank's buffer, K4 combines into out
         if (p->rank < 0 || p->rank >= p->world || p->shard_out || !p->out || p->exchange_timeout_us < 0)
@@ -400,7 +403,7 @@ int mla_workspace_size(const MlaDecodeParams* p, uint64_t* bytes) {
     int ctas = 0;
     st = resolve_ctas(p, &ctas);
     if (st != MLA_OK) return st;
-    *bytes = ws_layout(p->batch, ctas, p->x_n != nullptr).total;
+    *bytes = ws_layout(p->batch, ctas, p->x_n != nullptr, (p->flags & MLA_FLAG_QC_HILO) != 0).total;
     return MLA_OK;
 }
 
@@ -411,7 +414,7 @@ int mla_plan_info(const MlaDecodeParams* p, int32_t* num_ctas, int32_t* num_slot
     st = resolve_ctas(p, &ctas);
     if (st != MLA_OK) return st;
     if (num_ctas) *num_ctas = ctas;
-    if (num_slots) *num_slots = ws_layout(p->batch, ctas, p->x_n != nullptr).slots;
+    if (num_slots) *num_slots = ws_layout(p->batch, ctas, p->x_n != nullptr, (p->flags & MLA_FLAG_QC_HILO) != 0).slots;
     return MLA_OK;
 }
 

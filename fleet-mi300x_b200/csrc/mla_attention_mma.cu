@@ -39,6 +39,10 @@
 // Pairs (k2_pairs, G = num_ctas): the two groups hold adjacent plan CTAs 2k, 2k + 1;
 // where their boundary falls inside a request, group 1's first partial is merged
 // into group 0's last one in shared memory (slot 2k + b), so K3 folds fewer.
+// Precision forms (template flags): kQLo (MLA_FLAG_QC_HILO) adds the score MMAs of
+// the low half of q_c (K1's qa_lo) over the 512 latent columns; kPLo
+// (MLA_FLAG_P_HILO) keeps each probability as bf16 hi + lo in two P buffers, runs
+// the output MMAs on both and sums the row totals over the unrounded values.
 #include <cuda.h>
 
 #include "mla_common.cuh"
@@ -82,7 +86,11 @@ constexpr int kOffStash = (kOffMisc + kGroups * (int)sizeof(GroupSmem) + 15) & ~
 constexpr int kStashOBytes = kGroupWarps * 16 * 32 * 16;         // 32,768
 constexpr int kStashBytes = kStashOBytes + kHeads * 8 + 16;
 constexpr int kSmemBytes = kOffStash + kStashBytes + 1024;
-static_assert(kSmemBytes <= 232448, "K2 (mma) shared memory exceeds 227 KB");
+// kPLo: the low halves of P, [group][2] blocks laid out as the P blocks
+constexpr int kOffPLo = (kOffStash + kStashBytes + 127) & ~127;
+constexpr int kSmemBytesPLo = kOffPLo + kGroups * 2 * kPBytes + 1024;
+static_assert(kSmemBytesPLo <= 232448, "K2 (mma) shared memory exceeds 227 KB");
+constexpr int smem_bytes(bool plo) { return plo ? kSmemBytesPLo : kSmemBytes; }
 static_assert(kTileBytes % 1024 == 0 && kOffS % 1024 == 0, "TMA slots must stay 1024-byte aligned");
 
 // Zero the bf16 halves of a B fragment register whose token index is >= valid.
@@ -99,6 +107,7 @@ __device__ __forceinline__ int p_offset(int head, int u) { return head * 64 + ((
 
 }  // namespace mmak
 
+template <bool kQLo, bool kPLo>
 __global__ void __launch_bounds__(mmak::kThreads, 1)
     k2_attention_mma(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kv, float scale_log2,
                      int pairs) {
@@ -113,11 +122,13 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     uint8_t* tile_s = smem + kOffTile + grp * kNSlot * kTileBytes;
     float* spart = reinterpret_cast<float*>(smem + kOffS + grp * kSPartBytes);
     uint8_t* p_s = smem + kOffP + grp * 2 * kPBytes;
+    uint8_t* plo_s = smem + kOffPLo + grp * 2 * kPBytes;  // kPLo only
 
     const WsLayout ws = ws_layout(p);
     char* wsb = reinterpret_cast<char*>(p.workspace);
     const int32_t* cum = reinterpret_cast<const int32_t*>(wsb + ws.tiles_cum);
     const __nv_bfloat16* qa = reinterpret_cast<const __nv_bfloat16*>(wsb + ws.qa);
+    const __nv_bfloat16* qa_lo = reinterpret_cast<const __nv_bfloat16*>(wsb + ws.qa_lo);  // kQLo only
     float* part_ml = reinterpret_cast<float*>(wsb + ws.part_ml);
     float* part_acc = reinterpret_cast<float*>(wsb + ws.part_acc);
 
@@ -243,9 +254,10 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         cur.init_at(cumv, p.seq_lens, p.batch, pe, new_row_count(p));
         const int g = lane >> 2, t4 = lane & 3;
         const int m8 = lane >> 3, r8 = lane & 7;  // ldmatrix: matrix index, row in matrix
-        const uint32_t tile_addr = smem_u32(tile_s), p_addr = smem_u32(p_s);
+        const uint32_t tile_addr = smem_u32(tile_s), p_addr = smem_u32(p_s), plo_addr = smem_u32(plo_s);
 
         uint32_t qf[9][4];                     // Q fragments, k-steps [9w, 9w+9)
+        uint32_t ql[kQLo ? 9 : 1][4];          // kQLo: fragments of the low half of q_c (latent k-steps only)
         float o[16][4];                        // O_w: 16 latent tiles of 8
         float m_run[2], l_run[2];              // heads g, g+8
         int rows_b = 0;                        // rows attended by the current request
@@ -281,6 +293,21 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                     qf[j][2] = *reinterpret_cast<const uint32_t*>(q0 + g * kRow + 8);
                     qf[j][3] = *reinterpret_cast<const uint32_t*>(q0 + (g + 8) * kRow + 8);
                 }
+                if constexpr (kQLo) {
+                    const __nv_bfloat16* lrow = qa_lo + (int64_t)cur.b * kQRows * kLora + 144 * w + 2 * t4;
+#pragma unroll
+                    for (int j = 0; j < 9; ++j) {
+                        if (144 * w + 16 * j < kLora) {
+                            const __nv_bfloat16* l0 = lrow + 16 * j;
+                            ql[j][0] = *reinterpret_cast<const uint32_t*>(l0 + g * kLora);
+                            ql[j][1] = *reinterpret_cast<const uint32_t*>(l0 + (g + 8) * kLora);
+                            ql[j][2] = *reinterpret_cast<const uint32_t*>(l0 + g * kLora + 8);
+                            ql[j][3] = *reinterpret_cast<const uint32_t*>(l0 + (g + 8) * kLora + 8);
+                        } else {
+                            ql[j][0] = ql[j][1] = ql[j][2] = ql[j][3] = 0u;
+                        }
+                    }
+                }
 #pragma unroll
                 for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
                 m_run[0] = m_run[1] = -INFINITY;
@@ -310,6 +337,12 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                         ldsm_x4(tbase + chunk * kChunkBytes + tok * 128 + ((unit ^ r8) << 4), b00, b01, b10, b11);
                         mma16816(sacc[2 * q], qf[j], b00, b01);
                         mma16816(sacc[2 * q + 1], qf[j], b10, b11);
+                        if constexpr (kQLo) {
+                            if (k < kLora) {  // warp-uniform: the q_pe columns have no low half
+                                mma16816(sacc[2 * q], ql[kQLo ? j : 0], b00, b01);
+                                mma16816(sacc[2 * q + 1], ql[kQLo ? j : 0], b10, b11);
+                            }
+                        }
                     }
                 }
                 // ---- exchange: every warp publishes its partials, then sums its 8 tokens ----
@@ -370,7 +403,18 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 }
                 // ---- probabilities (bf16) for this warp's 8 tokens -> P buffer ----
                 uint8_t* pb = p_s + (i & 1) * kPBytes;
-                {
+                if constexpr (kPLo) {
+                    const float e0 = fast_exp2(s[0] - m_run[0]), e1 = fast_exp2(s[1] - m_run[0]);
+                    const float e2 = fast_exp2(s[2] - m_run[1]), e3 = fast_exp2(s[3] - m_run[1]);
+                    const float h0 = bf16_round(e0), h1 = bf16_round(e1), h2 = bf16_round(e2), h3 = bf16_round(e3);
+                    l_run[0] += e0 + e1;
+                    l_run[1] += e2 + e3;
+                    uint8_t* pl = plo_s + (i & 1) * kPBytes;
+                    *reinterpret_cast<uint32_t*>(pb + p_offset(g, w) + 4 * t4) = pack_bf16(h0, h1);
+                    *reinterpret_cast<uint32_t*>(pb + p_offset(g + 8, w) + 4 * t4) = pack_bf16(h2, h3);
+                    *reinterpret_cast<uint32_t*>(pl + p_offset(g, w) + 4 * t4) = pack_bf16(e0 - h0, e1 - h1);
+                    *reinterpret_cast<uint32_t*>(pl + p_offset(g + 8, w) + 4 * t4) = pack_bf16(e2 - h2, e3 - h3);
+                } else {
                     const float e0 = bf16_round(fast_exp2(s[0] - m_run[0]));
                     const float e1 = bf16_round(fast_exp2(s[1] - m_run[0]));
                     const float e2 = bf16_round(fast_exp2(s[2] - m_run[1]));
@@ -386,8 +430,11 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 const uint32_t pbase = p_addr + (i & 1) * kPBytes;
 #pragma unroll
                 for (int ks = 0; ks < 2; ++ks) {
-                    uint32_t a[4];
+                    uint32_t a[4], al[4];
                     ldsm_x4(pbase + p_offset((m8 & 1) * 8 + r8, 2 * ks + (m8 >> 1)), a[0], a[1], a[2], a[3]);
+                    if constexpr (kPLo)
+                        ldsm_x4(plo_addr + (i & 1) * kPBytes + p_offset((m8 & 1) * 8 + r8, 2 * ks + (m8 >> 1)), al[0],
+                                al[1], al[2], al[3]);
                     const int tok = 16 * ks + (m8 & 1) * 8 + r8;
 #pragma unroll
                     for (int pp = 0; pp < 8; ++pp) {  // latent tiles 2pp, 2pp+1 of this warp
@@ -404,6 +451,10 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                         }
                         mma16816(o[2 * pp], a, b00, b01);
                         mma16816(o[2 * pp + 1], a, b10, b11);
+                        if constexpr (kPLo) {
+                            mma16816(o[2 * pp], al, b00, b01);
+                            mma16816(o[2 * pp + 1], al, b10, b11);
+                        }
                     }
                 }
                 __syncwarp();
@@ -483,15 +534,29 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
 int k2_mma_smem_bytes() { return mmak::kSmemBytes; }
 
 cudaError_t k2_mma_configure() {
-    return cudaFuncSetAttribute(k2_attention_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, mmak::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(k2_attention_mma<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         mmak::smem_bytes(false));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k2_attention_mma<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 mmak::smem_bytes(false));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k2_attention_mma<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 mmak::smem_bytes(true));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k2_attention_mma<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 mmak::smem_bytes(true));
+    return e;
 }
 
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
                                  int sm_count, cudaStream_t stream) {
     static_assert(mmak::kGroups == 2, "k2_grid assumes two plan CTAs per CTA");
     const int grid = k2_grid(p.num_ctas, sm_count);
-    const cudaError_t e = launch_pdl(k2_attention_mma, dim3(grid), dim3(mmak::kThreads), mmak::kSmemBytes,
-                                     stream, p, tmap_kv, scale_log2, k2_pairs(p, sm_count) ? 1 : 0);
+    const bool qlo = (p.flags & MLA_FLAG_QC_HILO) != 0, plo = (p.flags & MLA_FLAG_P_HILO) != 0;
+    auto kern = qlo ? (plo ? k2_attention_mma<true, true> : k2_attention_mma<true, false>)
+                    : (plo ? k2_attention_mma<false, true> : k2_attention_mma<false, false>);
+    const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(mmak::kThreads), mmak::smem_bytes(plo), stream, p,
+                                     tmap_kv, scale_log2, k2_pairs(p, sm_count) ? 1 : 0);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

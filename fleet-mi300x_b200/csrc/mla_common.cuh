@@ -37,10 +37,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 //   qa         bf16  [batch][16][576]     absorbed query q_c (512) | roped q_pe (64), per head
 //   part_ml    f32   [slots][16][2]       split partial: running max (log2 domain), sum of exps
 //   part_acc   f32   [slots][16][512]     split partial: unnormalised sum_t p_t * c_t
+//   qkv        bf16  [batch][3648]        q | kv_a, when the step projects x_n itself (K0)
+//   qa_lo      bf16  [batch][16][512]     q_c - bf16(q_c), with MLA_FLAG_QC_HILO
 // slots = num_ctas + batch: CTA c writes the partial of request b at slot c + b.
 // ---------------------------------------------------------------------------
 struct WsLayout {
-    uint64_t tiles_cum, plan, qa, part_ml, part_acc, qkv, total;
+    uint64_t tiles_cum, plan, qa, part_ml, part_acc, qkv, qa_lo, total;
     int32_t slots;
 };
 
@@ -61,7 +63,8 @@ __host__ __device__ inline uint64_t align256(uint64_t x) { return (x + 255) & ~u
 
 // with_qkv: the step projects x_n itself (MlaDecodeParams.x_n set), and q | kv_a
 // of every request live in the workspace as [batch][3648] bf16.
-__host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with_qkv = false) {
+// with_qlo: MLA_FLAG_QC_HILO, the low half of q_c lives in qa_lo.
+__host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with_qkv = false, bool with_qlo = false) {
     WsLayout w;
     w.slots = num_ctas + batch;
     uint64_t off = 0;
@@ -71,12 +74,13 @@ __host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with
     w.part_ml = off;   off = align256(off + uint64_t(w.slots) * kHeads * 2 * 4);
     w.part_acc = off;  off = align256(off + uint64_t(w.slots) * kHeads * kLora * 4);
     w.qkv = off;       off = align256(off + (with_qkv ? uint64_t(batch) * kQkvRows * 2 : 0));
+    w.qa_lo = off;     off = align256(off + (with_qlo ? uint64_t(batch) * kQRows * kLora * 2 : 0));
     w.total = off;
     return w;
 }
 
 __host__ __device__ inline WsLayout ws_layout(const MlaDecodeParams& p) {
-    return ws_layout(p.batch, p.num_ctas, p.x_n != nullptr);
+    return ws_layout(p.batch, p.num_ctas, p.x_n != nullptr, (p.flags & MLA_FLAG_QC_HILO) != 0);
 }
 
 

@@ -10,7 +10,8 @@
 //    head, quarter of the latent) an m16n8k16 GEMM [64 requests x 128] x
 //    [128 x 128] against a 32 KB slice of W_UK[h] staged by one TMA box; q_nope
 //    and W_UK are bf16 already, so the products are exact; q_c is stored bf16 as
-//    an operand of the attention kernel's score contraction;
+//    an operand of the attention kernel's score contraction (with
+//    MLA_FLAG_QC_HILO also its remainder, as a second bf16 operand);
 //  * the split plan: prefix sum of 64-token tiles per request, consumed by K2/K3.
 //
 // One 1-D grid with two kinds of CTA:
@@ -276,6 +277,9 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
             }
         }
     }
+    // MLA_FLAG_QC_HILO: the remainder q_c - bf16(q_c), rounded to bf16, into qa_lo
+    __nv_bfloat16* qa_lo = (p.flags & MLA_FLAG_QC_HILO) ? reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa_lo) : nullptr;
+    auto lo2 = [](float x, float y) { return pack_bf16(x - bf16_round(x), y - bf16_round(y)); };
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt) {
         if (mt >= n_mt) break;
@@ -283,12 +287,20 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
         for (int n = 0; n < 4; ++n) {
             const int l = kK1LatQ * j + 32 * warp + 8 * n + 2 * t4;
             const int r0 = 16 * mt + gq, r1 = r0 + 8;
-            if (r0 < nreq)
+            if (r0 < nreq) {
                 *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + r0) * kQRows + h) * kRow + l) =
                     pack_bf16(acc[mt][n][0], acc[mt][n][1]);
-            if (r1 < nreq)
+                if (qa_lo)
+                    *reinterpret_cast<uint32_t*>(qa_lo + ((int64_t)(b0 + r0) * kQRows + h) * kLora + l) =
+                        lo2(acc[mt][n][0], acc[mt][n][1]);
+            }
+            if (r1 < nreq) {
                 *reinterpret_cast<uint32_t*>(qa + ((int64_t)(b0 + r1) * kQRows + h) * kRow + l) =
                     pack_bf16(acc[mt][n][2], acc[mt][n][3]);
+                if (qa_lo)
+                    *reinterpret_cast<uint32_t*>(qa_lo + ((int64_t)(b0 + r1) * kQRows + h) * kLora + l) =
+                        lo2(acc[mt][n][2], acc[mt][n][3]);
+            }
         }
     }
     MLA_TL_MARK(0, 4);

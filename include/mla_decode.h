@@ -101,6 +101,14 @@ typedef enum {
                                      store no row and attend over cache rows 0..seq_lens[b]-1 only */
 #define MLA_FLAG_EXCHANGE_SPLIT 0x10 /* peer exchange (world > 0): run it as K3 + K4 even where the fused
                                         form (K3 waits for the other ranks and combines, no K4) applies */
+/* Precision of the two operands the default kernel narrows to bf16 where the reference keeps
+ * fp32 (reference_decode.py:250-253). Default kernel only (refused with MLA_FLAG_CHECK_KERNEL
+ * or MLA_FLAG_TCGEN05). Each costs tensor-core issue in K2, not HBM bytes. */
+#define MLA_FLAG_QC_HILO 0x20  /* the absorbed query q_c = q_nope W_UK as a bf16 hi/lo pair: K1 writes both halves,
+                                  K2 runs the score MMAs of the 512 latent columns on both (about 16 mantissa bits
+                                  of the fp32 q_c instead of 8); the workspace grows by batch x 16 KB */
+#define MLA_FLAG_P_HILO 0x40   /* the probabilities of P c_kv as a bf16 hi/lo pair (two MMAs per step) and the row
+                                  sums over the unrounded fp32 values, instead of bf16-rounded probabilities */
 
 typedef struct MlaDecodeParams {
     uint32_t struct_size; /* sizeof(MlaDecodeParams) */

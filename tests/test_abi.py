@@ -70,6 +70,17 @@ def test_workspace_size(lib, batch, ctas):
     assert (c.value, s.value) == (ctas, ctas + batch)
 
 
+def test_workspace_size_with_qc_hilo(lib):
+    """MLA_FLAG_QC_HILO adds the low half of q_c, [batch][16][512] bf16, after the other regions."""
+    a = lambda x: (x + 255) // 256 * 256
+    for batch, ctas in ((1, 296), (256, 296)):
+        p = native.new_params()
+        p.batch, p.num_ctas, p.flags = batch, ctas, native.FLAG_QC_HILO | native.FLAG_P_HILO
+        n = ctypes.c_uint64()
+        assert lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(n)) == 0
+        assert n.value == expected_workspace(batch, ctas) + a(batch * 16 * 512 * 2)
+
+
 def test_validation_errors(lib):
     n = ctypes.c_uint64()
     p = native.new_params()

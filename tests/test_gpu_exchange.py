@@ -189,8 +189,9 @@ def test_missing_peer_times_out_with_error(cuda_device, split):
         out = torch.full((1, 2048), 1.0, dtype=BF, device=cuda_device)
         runner.attend(q, kv_a, caches[0], out, rope_pos=pos, new_row=False, exchange=ex[0])
         torch.cuda.synchronize()
-        assert int(runner.error_word.item()) == 4  # MLA_DEV_PEER_TIMEOUT
-        runner.error_word.zero_()
+        with pytest.raises(fleet.MlaError) as e:  # clears the device and the host error word
+            runner.check_errors()
+        assert e.value.code == 4  # MLA_DEV_PEER_TIMEOUT
         assert not out.float().abs().sum().item()
         # the device still runs work after the timed-out wait
         again = runner.attend(q, kv_a, caches[1], rope_pos=pos, new_row=True)

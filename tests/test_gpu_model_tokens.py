@@ -1,21 +1,25 @@
-"""Config 2: 27-layer token identity with only the attention task swapped.
+"""Config 2: 27-layer greedy decode with only the attention task swapped.
 
 A DeepSeek-V2-Lite-shaped decoder (tests/dsv2_model.py, random init, bf16) prefills a
-1024-token random prompt (positions 0..1022, shared by both arms), then decodes 32
-greedy tokens twice:
-  arm A -- every layer's attention task is the oracle's (the reference's arithmetic,
-           reference_decode.py:224-254, NumPy on the host);
-  arm B -- every layer's attention task is libmla_decode.so through MlaDecodeAttention
-           (cuBLAS q|kv_a + K1-K3 over a permuted paged cache).
-  arm C -- a control: the same arithmetic in plain torch fp32 on the GPU, no library code.
-Arm A decodes greedily; arms B and C are fed arm A's tokens so that every step compares
-the same context. Two correct implementations drift apart through 27 bf16 layers of
-random-init MoE, and a greedy token can flip where the oracle's top-2 margin is a near-tie.
-The gate: the library's logits and appended rows are no further from the oracle's than
-the control's are (x 1.5), every token where the library differs from the oracle lies in
-that step's noise band (oracle top-2 margin <= 2x the measured logit gap), and the library
-flips at most two steps more than the control.
-Logits are fp32 products of the bf16 head (bf16 logits tie often over 102,400 entries).
+1024-token random prompt (positions 0..1022, shared by every arm), then decodes 32
+greedy tokens. The library leads: arm L (libmla_decode.so through MlaDecodeAttention,
+cuBLAS q|kv_a + K1-K3 over a permuted paged cache, default precision) decodes greedily
+from its own tokens. Every other arm is fed L's tokens, keeps its own caches and says at
+each step which token it would pick:
+  A    the oracle's attention task (the reference's arithmetic, reference_decode.py:224-254,
+       NumPy on the host): the reference path;
+  C    a control, the same arithmetic in plain torch fp32 on the GPU (no library code);
+  Lq, Lp, Lqp  the library with q_c, P, or both kept as bf16 hi/lo pairs (MLA_FLAG_QC_HILO,
+       MLA_FLAG_P_HILO), the two operands it otherwise narrows to bf16.
+If A picks L's token at all 32 steps, then A's own greedy decode (the reference path run
+free) produces exactly L's 32 tokens: at each step A sees the same prefix and picks the
+same token. A step where A disagrees can only be an fp32 near-tie: the gate allows it only
+where A's top-2 margin is below the logit gap the control shows there, i.e. within what two
+correct fp32 implementations (different summation orders) disagree by after 27 bf16
+layers; every other step must agree. Logits are fp32 products of the bf16 head (bf16
+logits tie often over 102,400 entries). Top-2 margins are logged as the reference does
+(src/host/reference_run.py:102-106); its own gate is token-for-token identity
+(src/host/fleet_launch.hip:787-807).
 """
 import json
 
@@ -28,9 +32,10 @@ from mla_testlib import O, fleet, oracle_weights, workloads
 
 pytestmark = pytest.mark.gpu
 PROMPT, STEPS = 1024, 32
+LIB_ARMS = {"L": {}, "Lq": {"qc_hilo": True}, "Lp": {"p_hilo": True}, "Lqp": {"qc_hilo": True, "p_hilo": True}}
 
 
-def test_config2_token_identity_27_layers(cuda_device):
+def test_config2_greedy_tokens_27_layers(cuda_device):
     dev = cuda_device
     shape = Shape()
     cfg = fleet.ModelConfig()
@@ -56,23 +61,26 @@ def test_config2_token_identity_27_layers(cuda_device):
         out = O.attention_task(ocfg, ws[l], x_n.float().cpu().numpy()[0], flat[l], pos, cos, sin)
         return torch.from_numpy(out).to(torch.bfloat16).to(dev)[None]
 
-    # arm B: the library, one runner and one paged cache per layer
-    runners = [fleet.MlaDecodeAttention(cfg, w, cos_t, sin_t) for w in lws_dev]
-    caches = []
-    for l, r in enumerate(rows):
-        c = fleet.PagedLatentCache.for_lengths([T0], extra_tokens=STEPS, spare_pages=1,
-                                               generator=torch.Generator().manual_seed(l), device=dev)
-        c.write_rows(0, 0, r)
-        caches.append(c)
+    # library arms: one runner and one paged cache per layer each
+    def lib_arm(**kw):
+        runners = [fleet.MlaDecodeAttention(cfg, w, cos_t, sin_t, **kw) for w in lws_dev]
+        caches = []
+        for l, r in enumerate(rows):
+            c = fleet.PagedLatentCache.for_lengths([T0], extra_tokens=STEPS, spare_pages=1,
+                                                   generator=torch.Generator().manual_seed(l), device=dev)
+            c.write_rows(0, 0, r)
+            caches.append(c)
 
-    def attn_b(l, x_n, pos):
-        assert int(caches[l].seq_lens[0]) == pos
-        out = runners[l](x_n, caches[l])
-        caches[l].advance()
-        return out
+        def attn(l, x_n, pos):
+            assert int(caches[l].seq_lens[0]) == pos
+            out = runners[l](x_n, caches[l])
+            caches[l].advance()
+            return out
+        return attn, runners, caches
 
-    # control arm C: the same arithmetic in plain torch fp32 on the GPU (no library code),
-    # to measure how far two correct implementations drift apart through 27 bf16 layers
+    libs = {name: lib_arm(**kw) for name, kw in LIB_ARMS.items()}
+
+    # control arm C: the same arithmetic in plain torch fp32 on the GPU (no library code)
     flat_c = [torch.zeros(T0 + STEPS, 576, dtype=torch.bfloat16, device=dev) for _ in rows]
     for l, r in enumerate(rows):
         flat_c[l][:T0] = r
@@ -80,59 +88,58 @@ def test_config2_token_identity_27_layers(cuda_device):
     def attn_c(l, x_n, pos):
         return model.attend_one(l, x_n, flat_c[l], pos, cos_t, sin_t)
 
-    # arm A decodes greedily; arm B is fed arm A's tokens (teacher forcing), so one
-    # near-tie cannot turn every later step into a comparison of different contexts
-    inputs, toks_a, margins, deltas, toks_b = [int(tokens[-1])], [], [], [], []
-    toks_c, deltas_c, rl2_b, rl2_c = [], [], [], []
+    arms = {"A": attn_a, "C": attn_c, **{n: v[0] for n, v in libs.items()}}
+    toks = {n: [] for n in arms}
+    gap = {n: [] for n in arms if n != "A"}  # max |logit - oracle logit| per step
+    margins, fed = [], [int(tokens[-1])]
     with torch.no_grad():
         for s in range(STEPS):
-            la = model.decode(inputs[-1], T0 + s, attn_a)
-            lb = model.decode(inputs[-1], T0 + s, attn_b)
-            lc = model.decode(inputs[-1], T0 + s, attn_c)
-            top = la.topk(2)
-            toks_a.append(int(top.indices[0]))
-            toks_b.append(int(lb.argmax()))
-            toks_c.append(int(lc.argmax()))
+            logits = {n: model.decode(fed[-1], T0 + s, fn) for n, fn in arms.items()}
+            top = logits["A"].topk(2)
             margins.append(float(top.values[0] - top.values[1]))
-            deltas.append(float((la - lb).abs().max()))
-            deltas_c.append(float((la - lc).abs().max()))
-            rl2_b.append(float((la - lb).norm() / la.norm()))
-            rl2_c.append(float((la - lc).norm() / la.norm()))
-            inputs.append(toks_a[-1])
-    for r in runners:
-        r.check_errors()
-    # appended rows: layer 0 sees the same x_n in both arms, so its rows agree up to bf16
+            for n, lg in logits.items():
+                toks[n].append(int(lg.argmax()))
+                if n != "A":
+                    gap[n].append(float((lg - logits["A"]).abs().max()))
+            fed.append(toks["L"][-1])  # the library decodes free
+    for _, runners, _ in libs.values():
+        for r in runners:
+            r.check_errors()
+
+    # appended rows: layer 0 sees the same x_n in every arm, so its rows agree up to bf16
     # rounding ties; deeper layers see hidden states that already differ at bf16 level
-    row_mism0, row_rel, row_rel_c = 0, [], []
-    for l in range(shape.layers):
-        got = caches[l].read_rows(0, T0, STEPS).float().cpu().numpy()
-        ctl = flat_c[l][T0:T0 + STEPS].float().cpu().numpy()
-        want = flat[l][T0:T0 + STEPS]
-        if l == 0:
-            row_mism0 = int(np.count_nonzero(got != want))
-        row_rel.append(float(np.abs(got - want).max() / np.abs(want).max()))
-        row_rel_c.append(float(np.abs(ctl - want).max() / np.abs(want).max()))
-    diff = [s for s in range(STEPS) if toks_a[s] != toks_b[s]]
-    ties = [s for s in diff if margins[s] <= 2 * deltas[s]]
-    diff_c = [s for s in range(STEPS) if toks_a[s] != toks_c[s]]
-    summary = {"tokens_identical": not diff, "steps": STEPS, "flips_vs_oracle": diff, "near_ties_flipped": ties,
-               "tokens_identical_to_control": toks_b == toks_c,
-               "control_flips": diff_c, "max_logit_delta": max(deltas), "max_logit_delta_control": max(deltas_c),
-               "mean_logit_rel_l2": sum(rl2_b) / STEPS, "mean_logit_rel_l2_control": sum(rl2_c) / STEPS,
-               "min_margin_a": min(margins),
-               "layer0_row_mismatches": row_mism0, "max_row_rel": max(row_rel),
-               "max_row_rel_control": max(row_rel_c),
-               "margins_a": [round(m, 4) for m in margins], "logit_delta": [round(d, 4) for d in deltas],
-               "logit_delta_control": [round(d, 4) for d in deltas_c]}
+    caches_l = libs["L"][2]
+    got0 = caches_l[0].read_rows(0, T0, STEPS).float().cpu().numpy()
+    row_mism0 = int(np.count_nonzero(got0 != flat[0][T0:T0 + STEPS]))
+    row_rel = {}
+    for n in ("L", "Lqp"):
+        row_rel[n] = max(float(np.abs(libs[n][2][l].read_rows(0, T0, STEPS).float().cpu().numpy()
+                                      - flat[l][T0:T0 + STEPS]).max() / np.abs(flat[l][T0:T0 + STEPS]).max())
+                         for l in range(shape.layers))
+    row_rel["C"] = max(float(np.abs(flat_c[l][T0:T0 + STEPS].float().cpu().numpy() - flat[l][T0:T0 + STEPS]).max()
+                             / np.abs(flat[l][T0:T0 + STEPS]).max()) for l in range(shape.layers))
+
+    differ = {n: [s for s in range(STEPS) if toks[n][s] != toks["A"][s]] for n in arms if n != "A"}
+    ties = [s for s in differ["L"] if margins[s] <= gap["C"][s]]
+    summary = {
+        "steps": STEPS, "library_tokens": toks["L"], "oracle_agrees_at_every_step": not differ["L"],
+        "steps_where_oracle_differs": differ, "near_ties": ties,
+        "oracle_margins_at_differing_steps": {s: round(margins[s], 5) for s in differ["L"]},
+        "control_gap_at_differing_steps": {s: round(gap["C"][s], 4) for s in differ["L"]},
+        "max_logit_gap": {n: round(max(v), 4) for n, v in gap.items()},
+        "mean_logit_gap": {n: round(sum(v) / STEPS, 5) for n, v in gap.items()},
+        "min_oracle_margin": round(min(margins), 5), "layer0_row_mismatches": row_mism0,
+        "max_row_rel": {n: round(v, 5) for n, v in row_rel.items()},
+        "margins": [round(m, 4) for m in margins],
+    }
     print("config2 " + json.dumps(summary))
     assert row_mism0 <= STEPS * 8, f"layer 0: {row_mism0} of {STEPS * 576} appended-row elements differ"
     # the library is no further from the oracle than an independent fp32 implementation is
-    assert max(row_rel) <= max(2e-2, 1.5 * max(row_rel_c)), (max(row_rel), max(row_rel_c))
-    assert max(deltas) <= 1.5 * max(deltas_c), (max(deltas), max(deltas_c))
-    assert sum(rl2_b) <= 1.5 * sum(rl2_c), (sum(rl2_b) / STEPS, sum(rl2_c) / STEPS)
-    # every token that differs from the oracle's lies in that step's noise band (the oracle's
-    # top-2 margin is within twice the measured logit gap), and the library flips at most two
-    # steps more than the control does
-    real = [s for s in diff if margins[s] > 2 * deltas[s]]
-    assert not real, f"steps {real}: tokens differ with oracle margins {[margins[s] for s in real]}"
-    assert len(diff) <= len(diff_c) + 2, f"library flips {diff} against control flips {diff_c}"
+    assert row_rel["L"] <= max(2e-2, 1.5 * row_rel["C"]), row_rel
+    assert max(gap["L"]) <= 1.5 * max(gap["C"]), summary["max_logit_gap"]
+    assert sum(gap["L"]) <= 1.5 * sum(gap["C"]), summary["mean_logit_gap"]
+    # identity at every step, except where the oracle's own top-2 margin is below the gap
+    # between the oracle and the control at that step (an fp32 near-tie)
+    real = [s for s in differ["L"] if margins[s] > gap["C"][s]]
+    assert not real, f"steps {real}: the oracle picks another token with margins {[margins[s] for s in real]}"
+    assert len(differ["L"]) <= 2, f"the oracle differs at {differ['L']} (near-ties {ties})"

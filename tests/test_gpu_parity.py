@@ -270,3 +270,48 @@ def test_full_size_config_subset(cuda_device, cfg_name, subset):
     want, _ = oracle_paged(cache.block_table.cpu().numpy(), pages_before, d, requests=subset, fast=True)
     for b in subset:
         assert_close(tc[b], want[b], f"{cfg_name} request {b} vs oracle")
+
+
+def _ulp_err(got, want):
+    """|got - want| in units of the bf16 spacing at |want| (0 = the same bf16 value)."""
+    w = np.abs(np.asarray(want, np.float64))
+    spacing = np.exp2(np.floor(np.log2(np.maximum(w, 1e-30))) - 7)
+    return np.abs(np.asarray(got, np.float64) - np.asarray(want, np.float64)) / spacing
+
+
+@pytest.mark.parametrize("flags", [dict(qc_hilo=True), dict(p_hilo=True), dict(qc_hilo=True, p_hilo=True)],
+                         ids=["qc", "p", "qc+p"])
+def test_hilo_precision_forms(cuda_device, flags):
+    """MLA_FLAG_QC_HILO / MLA_FLAG_P_HILO keep q_c and P as bf16 hi/lo pairs. Each must pass
+    the parity bar, give repeatable bits, and bring R(out) no further from the oracle's fp32
+    arithmetic than the default form; with both, nearly every output element is the
+    oracle's bf16 value or its neighbour."""
+    d = ragged_batch(cuda_device, EDGE_LENGTHS + [20000])
+    pages_np = d["cache"].pages.float().cpu().numpy()
+    bt = d["cache"].block_table.cpu().numpy()
+    want, _ = oracle_paged(bt, pages_np, d, fast=True)
+    runner = fleet.MlaDecodeAttention(fleet.ModelConfig(), to_dev(d["lw"], cuda_device),
+                                      torch.from_numpy(d["cos"]).to(cuda_device),
+                                      torch.from_numpy(d["sin"]).to(cuda_device), **flags)
+    q = torch.from_numpy(d["q"]).to(BF).to(cuda_device)
+    kv_a = torch.from_numpy(d["kv_a"]).to(BF).to(cuda_device)
+    got = runner.attend(q, kv_a, d["cache"]).float().cpu().numpy()
+    again = runner.attend(q, kv_a, d["cache"]).float().cpu().numpy()
+    runner.check_errors()
+    np.testing.assert_array_equal(got, again)
+    base = run_gpu(d, cuda_device)
+    for b in range(len(d["lengths"])):
+        assert_close(got[b], want[b], f"request {b} (T={d['lengths'][b]}, {flags})")
+    e_hilo, e_base = _ulp_err(got, want), _ulp_err(base, want)
+    assert e_hilo.mean() <= e_base.mean(), (e_hilo.mean(), e_base.mean())
+    if len(flags) == 2:
+        assert np.mean(e_hilo <= 1.0) >= 0.995, f"{np.mean(e_hilo <= 1.0):.4f} of elements within one bf16 step"
+    print(f"{flags}: mean ulp error {e_hilo.mean():.3f} (default {e_base.mean():.3f}), "
+          f"within one step {np.mean(e_hilo <= 1.0):.4f} (default {np.mean(e_base <= 1.0):.4f})")
+
+
+def test_hilo_flags_refused_with_other_kernels(cuda_device):
+    with pytest.raises(ValueError):
+        fleet.MlaDecodeAttention(fleet.ModelConfig(), to_dev(workloads.make_layer_weights(1), cuda_device),
+                                 torch.zeros(8, 64, device=cuda_device), torch.zeros(8, 64, device=cuda_device),
+                                 kernel="tcgen05", qc_hilo=True)
