@@ -138,8 +138,10 @@ def test_config2_greedy_tokens_27_layers(cuda_device):
     assert row_rel["L"] <= max(2e-2, 1.5 * row_rel["C"]), row_rel
     assert max(gap["L"]) <= 1.5 * max(gap["C"]), summary["max_logit_gap"]
     assert sum(gap["L"]) <= 1.5 * sum(gap["C"]), summary["mean_logit_gap"]
-    # identity at every step, except where the oracle's own top-2 margin is below the gap
-    # between the oracle and the control at that step (an fp32 near-tie)
-    real = [s for s in differ["L"] if margins[s] > gap["C"][s]]
-    assert not real, f"steps {real}: the oracle picks another token with margins {[margins[s] for s in real]}"
-    assert len(differ["L"]) <= 2, f"the oracle differs at {differ['L']} (near-ties {ties})"
+    # identity at every step, for the library in each precision form, except where the
+    # oracle's own top-2 margin is below the gap between the oracle and the control at that
+    # step (an fp32 near-tie: two correct fp32 implementations disagree by more than that)
+    for n in LIB_ARMS:
+        real = [s for s in differ[n] if margins[s] > gap["C"][s]]
+        assert not real, f"{n}: steps {real}, the oracle picks another token with margins " \
+                         f"{[margins[s] for s in real]} above the control's gaps {[gap['C'][s] for s in real]}"
