@@ -491,13 +491,18 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     seq = None
     if world > 1 and not args.no_extra:
         seq = sequence_sharded_block(args, rank, world, dev, dist)
-    others = None
+    others = stack = None
     if world == 1 and not args.no_extra:
         peak0, _ = measured_peak()
         oclocks = ClockSampler(local_rank)
         with oclocks:
             others = {n: other_config_summary(n, dev, max(10, args.steps), peak0)
                       for n in ("config1", "config3", "config4", "config5b") if n != args.workload}
+            for n in others:
+                others[n]["stack"] = stack_summary(n, dev, max(10, args.steps), peak0)
+                torch.cuda.empty_cache()
+            stack = stack_summary(args.workload, dev, max(5, args.steps // 2), peak0)
+            torch.cuda.empty_cache()
         others["clocks"] = oclocks.summary()
 
     cpu = None
@@ -550,6 +555,7 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     if seq is not None:
         line["sequence_sharded"] = seq
     if others is not None:
+        line["stack"] = stack
         line["other_configs"] = others
     print(json.dumps(line), flush=True)
 
@@ -741,6 +747,51 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
+
+
+STACK_LAYERS = 27  # DeepSeek-V2-Lite's decoder layers
+
+
+def stack_summary(name: str, dev: torch.device, steps: int, peak: float, layers: int = STACK_LAYERS) -> dict:
+    """The attention slice of `layers` layers as one CUDA graph (LayerStackGraph, slice
+    mode): each layer has its own weights (seeded per layer) and its own cache with the
+    workload's shape, as in a decoder, so the step reads layers x the KV bytes. Device time
+    per step / layers = µs per layer-step inside a multi-layer decode step, the unit of the
+    reference's per-layer figure (measured inside its all-layers persistent kernel). L2 is
+    flushed before every timed step if the stack reads less than 4x L2."""
+    wl = workloads.WORKLOADS[name]
+    lengths = wl.seq_lens()
+    cfg = fleet.ModelConfig()
+    cos, sin = fleet.device_rope_tables(cfg, max(lengths) + 8, dev)
+    x_n = workloads.make_hidden(wl.seed + 1, len(lengths)).to(dev)
+    runners, caches, qs, kvs = [], [], [], []
+    for l in range(layers):
+        lw = workloads.make_layer_weights(wl.seed + 1000 * (l + 1))
+        w = fleet.LayerWeights(*(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm,
+                                                       lw.kv_b_proj)))
+        r = fleet.MlaDecodeAttention(cfg, w, cos, sin)
+        c = fleet.PagedLatentCache.for_lengths(lengths, permute=wl.permute, zero=False,
+                                               generator=torch.Generator().manual_seed(wl.seed + l), device=dev)
+        workloads.fill_pool_random(c.pages, wl.seed + 7919 * (l + 1))
+        q, kv_a = (t.contiguous() for t in r.project(x_n))
+        runners.append(r)
+        caches.append(c)
+        qs.append(q)
+        kvs.append(kv_a)
+    stack = fleet.LayerStackGraph(runners, caches, mode="slice", q=qs, kv_a=kvs)
+    for _ in range(3):
+        stack.replay()
+    stack.synchronize()
+    kv_b = workloads.kv_bytes(lengths)
+    weights = layers * (2 * 16 * 128 * 512 * 2)
+    timer = StepTimer(torch.cuda.current_stream(dev), layers * kv_b + weights, dev)
+    ms = timer(stack.replay, steps)
+    stack.synchronize()
+    us = ms * 1e3 / layers
+    return {"layers": layers, "us_per_layer_step": round(us, 3), "kv_gbs": round(kv_b / (us * 1e-6) / 1e9, 1),
+            "kv_frac_of_hbm_peak": round(kv_b / (us * 1e-6) / 1e9 / peak, 4),
+            "step_us": round(ms * 1e3, 2),
+            "l2": "flushed before every timed step" if timer.flush is not None else "no flush (> 4x L2 per step)"}
 
 
 def other_config_summary(name: str, dev: torch.device, steps: int, peak: float) -> dict:

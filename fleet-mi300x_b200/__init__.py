@@ -12,13 +12,13 @@ The directory name is not a Python identifier; import it with
 from .config import ModelConfig, rope_tables, yarn_cos_sin, yarn_get_mscale
 from .cache import PagedLatentCache
 from .attention import LayerWeights, MlaDecodeAttention, attention_absorbed, combine_shards, device_rope_tables
-from .graph import DecodeGraph, HostPipeline, HostStepGraph
+from .graph import DecodeGraph, HostPipeline, HostStepGraph, LayerStackGraph
 from .handoff import caches_from_flat, read_flat_cache, rows_to_pages, write_flat_cache
 from .native import MlaError, load_library
 
 __all__ = [
     "ModelConfig", "rope_tables", "yarn_cos_sin", "yarn_get_mscale", "PagedLatentCache",
     "LayerWeights", "MlaDecodeAttention", "attention_absorbed", "combine_shards", "device_rope_tables",
-    "DecodeGraph", "HostPipeline", "HostStepGraph", "MlaError", "load_library", "caches_from_flat", "read_flat_cache", "rows_to_pages",
+    "DecodeGraph", "HostPipeline", "HostStepGraph", "LayerStackGraph", "MlaError", "load_library", "caches_from_flat", "read_flat_cache", "rows_to_pages",
     "write_flat_cache",
 ]

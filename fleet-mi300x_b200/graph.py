@@ -195,3 +195,108 @@ class HostStepGraph:
         """Wait for the current stream and raise if a step recorded a device error."""
         torch.cuda.current_stream(self.runner.device).synchronize()
         self.runner.raise_pending()
+
+
+def rms_norm_bf16(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """DeepseekV2RMSNorm of a bf16 hidden state with HF's two bf16 roundings
+    (reference_decode.py:51-65): fp32 normalisation rounded to bf16, times the weight."""
+    x32 = x.float()
+    y = x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + eps)
+    return weight * y.to(torch.bfloat16)
+
+
+class LayerStackGraph:
+    """One decode step over a stack of layers as a single CUDA graph.
+
+    The reference runs every layer of a token in one persistent launch
+    (src/kernels/fleet_kernel.hip:938-1043). Here the layers' kernels are captured in
+    order into one graph, so a step pays one graph launch instead of one per layer, and
+    each layer's first kernel, a programmatic dependent launch, becomes resident while
+    the previous layer's last kernel still runs (its weight copies start before its wait).
+
+    mode="slice": layer l runs its attention task K1-K3 from its own q / kv_a buffers
+      (self.q[l], self.kv_a[l]) over caches[l] into self.out[l]: the attention slice of
+      every layer with its own weights and cache, the unit the per-layer-step metric counts.
+    mode="block": the hidden state self.h [B, 2048] flows through the layers: for each l,
+      x_n = RMSNorm(h, in_norms[l]) (torch), then runners[l].attention_block(x_n, caches[l],
+      residual=h, h_out=h) (K0-K5: projection, attention, o_proj and the residual add in the
+      library for batches up to 64), then `ffn(l, h)` if given (capturable torch ops that
+      update h in place, e.g. the layer's FFN with its residual).
+
+    With advance=True the graph also adds 1 to every cache's seq_lens. Device errors of any
+    layer are raised by replay() / synchronize() (each runner's pinned host error word).
+    """
+
+    def __init__(self, runners, caches, *, mode: str = "slice", q=None, kv_a=None, h=None, in_norms=None,
+                 ffn=None, advance: bool = False):
+        if mode not in ("slice", "block"):
+            raise ValueError("mode must be 'slice' or 'block'")
+        if len(runners) != len(caches) or not runners:
+            raise ValueError("one cache per runner, at least one layer")
+        self.runners, self.caches, self.mode, self.ffn = list(runners), list(caches), mode, ffn
+        r0, dev, B = runners[0], runners[0].device, caches[0].batch
+        cfg, bf = r0.cfg, torch.bfloat16
+        if any(c.batch != B for c in caches):
+            raise ValueError("every layer's cache must hold the same batch")
+        n = len(runners)
+        if mode == "slice":
+            self.q = q if q is not None else [torch.zeros(B, cfg.heads * cfg.q_head_dim, dtype=bf, device=dev)
+                                              for _ in range(n)]
+            self.kv_a = kv_a if kv_a is not None else [
+                torch.zeros(B, cfg.kv_lora_rank + cfg.qk_rope, dtype=bf, device=dev) for _ in range(n)]
+            self.out = [torch.empty(B, cfg.heads * cfg.v_head, dtype=bf, device=dev) for _ in range(n)]
+        else:
+            if in_norms is None or len(in_norms) != n:
+                raise ValueError("mode 'block' needs one input RMSNorm weight per layer")
+            self.in_norms = list(in_norms)
+            self.h = h if h is not None else torch.zeros(B, cfg.hidden, dtype=bf, device=dev)
+            self.x_n = torch.empty(B, cfg.hidden, dtype=bf, device=dev)
+            self.attn = torch.empty(B, cfg.heads * cfg.v_head, dtype=bf, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # library set-up and workspaces before the capture
+            self._params_warm()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+            if advance:
+                for c in self.caches:
+                    c.seq_lens.add_(1)
+
+    def _params_warm(self) -> None:
+        """Run each layer's library call once outside the capture (workspace allocation,
+        per-device set-up); state that a step changes (rows, h) is restored after."""
+        if self.mode == "slice":
+            self._step()
+            return
+        h0 = self.h.clone()
+        self._step()
+        self.h.copy_(h0)
+
+    def _step(self) -> None:
+        if self.mode == "slice":
+            for l, (r, c) in enumerate(zip(self.runners, self.caches)):
+                r.attend(self.q[l], self.kv_a[l], c, self.out[l])
+            return
+        for l, (r, c) in enumerate(zip(self.runners, self.caches)):
+            self.x_n.copy_(rms_norm_bf16(self.h, self.in_norms[l], r.cfg.rms_eps))
+            r.attention_block(self.x_n, c, self.h, h_out=self.h, out=self.attn)
+            if self.ffn is not None:
+                self.ffn(l, self.h)
+
+    def _raise_pending(self) -> None:
+        for r in self.runners:
+            r.raise_pending()
+
+    def replay(self) -> None:
+        """Run the captured step on the current stream (raises first if an earlier step of
+        any layer recorded a device error)."""
+        self._raise_pending()
+        self.graph.replay()
+
+    def synchronize(self) -> None:
+        """Wait for the current stream and raise if a step recorded a device error."""
+        torch.cuda.current_stream(self.runners[0].device).synchronize()
+        self._raise_pending()
