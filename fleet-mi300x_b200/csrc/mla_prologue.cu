@@ -121,51 +121,79 @@ __device__ void plan_entries(const MlaDecodeParams& p, const int32_t* cum, const
     }
 }
 
-// One warp: q_pe RoPE of request b, then (unless the call stores no row)
-// kv_post + the cache append at local row seq_lens[b].
-__device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b, int lane) {
-    // Two dependent rounds of loads: first everything that depends on b alone (the
-    // row counts, q_pe of all heads, the raw kv_a row and gamma), then what depends
-    // on the position (the RoPE tables, the block-table entry of the new row).
-    const int pos = p.seq_lens[b];
-    const int rp = p.rope_pos ? p.rope_pos[b] : pos;
+// The per-request warp's inputs that no earlier kernel writes: the row count and RoPE
+// position, the RoPE table rows of that position, the block-table entry of the new
+// row and kv_a_layernorm's weight. They are loaded before the wait on the previous
+// kernel (positions, tables and weights are the step's inputs, as for the split
+// plan that K2 derives before its own wait), so that after the wait only q_pe and
+// the raw kv_a row, the previous kernel's output, remain to be loaded.
+struct RowPre {
+    int pos, rp, page;
+    bool ok, append;
+    float c0, c1, s0, s1;
+    __align__(16) __nv_bfloat16 gw[16];
+};
+
+__device__ void request_rows_pre(const MlaDecodeParams& p, int b, int lane, RowPre& r) {
+    r.pos = p.seq_lens[b];
+    r.rp = p.rope_pos ? p.rope_pos[b] : r.pos;
+    r.append = new_row_count(p) != 0;
+    const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w);
+    if (r.append) {
+        if ((reinterpret_cast<uintptr_t>(gam) & 15) == 0) {
+            reinterpret_cast<uint4*>(r.gw)[0] = reinterpret_cast<const uint4*>(gam)[2 * lane];
+            reinterpret_cast<uint4*>(r.gw)[1] = reinterpret_cast<const uint4*>(gam)[2 * lane + 1];
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) r.gw[k] = gam[16 * lane + k];
+        }
+    }
+    // request_ok on the loaded values (an invalid request is recorded by the planner)
+    r.ok = r.pos >= 0 && r.rp >= 0 && r.rp < p.max_pos && r.pos + new_row_count(p) <= p.max_blocks * kPage;
+    r.page = 0;
+    if (!r.ok) return;
+    const float* cs = p.rope_cos + (int64_t)r.rp * kRope;
+    const float* sn = p.rope_sin + (int64_t)r.rp * kRope;
+    r.c0 = cs[lane]; r.c1 = cs[32 + lane]; r.s0 = sn[lane]; r.s1 = sn[32 + lane];
+    if (r.append) r.page = p.block_table[(int64_t)b * p.max_blocks + r.pos / kPage];
+}
+
+// One warp, after the wait: q_pe RoPE of request b, then (unless the call stores no
+// row) kv_post + the cache append at local row seq_lens[b].
+__device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b, int lane, const RowPre& r) {
+    if (!r.ok) return;
     const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q) + (int64_t)b * p.q_stride;
     __nv_bfloat162 xq[kHeads];
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) xq[h] = reinterpret_cast<const __nv_bfloat162*>(q + h * kQHead + kNope)[lane];
-    const bool append = new_row_count(p) != 0;
     KvPostIn kin;
-    if (append)
-        kv_post_load(reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride,
-                     reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w), lane, kin);
-    // request_ok, on the values already loaded (an invalid request is recorded by the planner)
-    if (!(pos >= 0 && rp >= 0 && rp < p.max_pos && pos + new_row_count(p) <= p.max_blocks * kPage)) return;
-
-    const float* cs = p.rope_cos + (int64_t)rp * kRope;
-    const float* sn = p.rope_sin + (int64_t)rp * kRope;
-    const float c0 = cs[lane], c1 = cs[32 + lane], s0 = sn[lane], s1 = sn[32 + lane];
-    const int page = append ? p.block_table[(int64_t)b * p.max_blocks + pos / kPage] : 0;
+    if (r.append) {
+        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride;
+        kv_post_load(src, nullptr, lane, kin);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) kin.gw[k] = r.gw[k];
+    }
 
     // q_pe of all 16 heads: lane j rotates pair j
     __nv_bfloat16* qrow = qa + (int64_t)b * kQRows * kRow;
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) {
         float lo, hi;
-        rope_pair_r(__low2float(xq[h]), __high2float(xq[h]), c0, s0, c1, s1, lo, hi);
+        rope_pair_r(__low2float(xq[h]), __high2float(xq[h]), r.c0, r.s0, r.c1, r.s1, lo, hi);
         qrow[h * kRow + kLora + lane] = __float2bfloat16_rn(lo);
         qrow[h * kRow + kLora + 32 + lane] = __float2bfloat16_rn(hi);
     }
-    if (!append) return;
+    if (!r.append) return;
 
     __align__(16) __nv_bfloat16 outc[16];
     float lo, hi;
-    kv_post_finish(kin, p.rms_eps, cs, sn, lane, outc, lo, hi);
-    if (page < 0 || page >= p.n_pages) {
+    kv_post_finish_r(kin, p.rms_eps, r.c0, r.s0, r.c1, r.s1, lane, outc, lo, hi);
+    if (r.page < 0 || r.page >= p.n_pages) {
         if (lane == 0) record_error(err_sink(p), MLA_DEV_BAD_PAGE);
         return;
     }
-    kv_post_store(reinterpret_cast<__nv_bfloat16*>(p.kv_cache) + ((int64_t)page * kPage + pos % kPage) * kRow, outc,
-                  lo, hi, lane);
+    kv_post_store(reinterpret_cast<__nv_bfloat16*>(p.kv_cache) + ((int64_t)r.page * kPage + r.pos % kPage) * kRow,
+                  outc, lo, hi, lane);
 }
 
 __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p,
@@ -189,6 +217,19 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
         mbar_arrive_expect_tx(bar, kWukBytes);
         tma_load_3d(w_s, &tmap_wuk, bar, 0, h * kKvbHead, kK1WukBlocks * j, kCacheEvictLast);
     }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b0 = rb * kReqBlock;
+    const int nreq = min(kReqBlock, p.batch - b0);
+    if (cta != g.total - 1 && warp == kK1MmaWarps) {  // the per-request work of request b0 + c_in
+        RowPre pre;
+        if (c_in < nreq) request_rows_pre(p, b0 + c_in, lane, pre);
+        pdl_wait();  // q and kv_a come from the previous kernel
+        MLA_TL_WAITED(0);
+        pdl_trigger();
+        if (c_in < nreq) request_rows(p, qa, b0 + c_in, lane, pre);
+        MLA_TL_MARK(0, 5);
+        return;  // joins no barrier
+    }
     pdl_wait();     // q, kv_a and the cache come from earlier work on the stream
     MLA_TL_WAITED(0);
     pdl_trigger();  // K2 may become resident now; it waits for this grid before reading its output
@@ -202,14 +243,6 @@ __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams 
     }
 
     // ---- absorb CTA: q_c[b][h][128j + l] = q_nope[b][h] @ W_UK[h][:, 128j + l] ----
-    const int b0 = rb * kReqBlock;
-    const int nreq = min(kReqBlock, p.batch - b0);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp == kK1MmaWarps) {  // the per-request work of request b0 + c_in; joins no barrier
-        if (c_in < nreq) request_rows(p, qa, b0 + c_in, lane);
-        MLA_TL_MARK(0, 5);
-        return;
-    }
     // q_nope [64][128] -> shared, 256-byte rows with 16-byte units XOR (row & 7)
     {
         const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q);

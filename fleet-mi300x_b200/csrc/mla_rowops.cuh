@@ -36,6 +36,7 @@ struct KvPostIn {
     float kp0, kp1;
 };
 
+// gam = nullptr: the caller fills in.gw itself.
 __device__ __forceinline__ void kv_post_load(const __nv_bfloat16* src, const __nv_bfloat16* gam, int lane,
                                              KvPostIn& in) {
     {
@@ -51,7 +52,8 @@ __device__ __forceinline__ void kv_post_load(const __nv_bfloat16* src, const __n
             for (int k = 0; k < 16; ++k) in.x[k] = __bfloat162float(src[16 * lane + k]);
         }
     }
-    if ((reinterpret_cast<uintptr_t>(gam) & 15) == 0) {
+    if (gam == nullptr) {
+    } else if ((reinterpret_cast<uintptr_t>(gam) & 15) == 0) {
         reinterpret_cast<uint4*>(in.gw)[0] = reinterpret_cast<const uint4*>(gam)[2 * lane];
         reinterpret_cast<uint4*>(in.gw)[1] = reinterpret_cast<const uint4*>(gam)[2 * lane + 1];
     } else {
@@ -63,11 +65,13 @@ __device__ __forceinline__ void kv_post_load(const __nv_bfloat16* src, const __n
     in.kp1 = __bfloat162float(kp[1]);
 }
 
-// One warp: the cache row of the loaded raw kv_a values at the RoPE position whose
-// tables are cs / sn. Lane owns c[16 lane, 16 lane + 16) (outc) and RoPE pair
-// `lane` of k_pe (lo -> column 512 + lane, hi -> 544 + lane).
-__device__ __forceinline__ void kv_post_finish(const KvPostIn& in, float eps, const float* cs, const float* sn,
-                                               int lane, __nv_bfloat16 (&outc)[16], float& lo, float& hi) {
+// One warp: the cache row of the loaded raw kv_a values at a RoPE position whose
+// table entries for this lane's pair are c_lo = cos[lane], s_lo = sin[lane],
+// c_hi = cos[32 + lane], s_hi = sin[32 + lane]. Lane owns c[16 lane, 16 lane + 16)
+// (outc) and RoPE pair `lane` of k_pe (lo -> column 512 + lane, hi -> 544 + lane).
+__device__ __forceinline__ void kv_post_finish_r(const KvPostIn& in, float eps, float c_lo, float s_lo, float c_hi,
+                                                 float s_hi, int lane, __nv_bfloat16 (&outc)[16], float& lo,
+                                                 float& hi) {
     // kv_post (reference_decode.py:60-65): var = mean(x^2); y = x * (1 / sqrt(var + eps));
     // row = bf16(bf16(y) * weight). Lane owns c[16*lane, 16*lane+16).
     float ss = 0.f;
@@ -82,7 +86,13 @@ __device__ __forceinline__ void kv_post_finish(const KvPostIn& in, float eps, co
         const float y = bf16_round(__fmul_rn(in.x[k], inv));
         outc[k] = __float2bfloat16_rn(__fmul_rn(y, __bfloat162float(in.gw[k])));
     }
-    rope_pair(in.kp0, in.kp1, cs, sn, lane, lo, hi);
+    rope_pair_r(in.kp0, in.kp1, c_lo, s_lo, c_hi, s_hi, lo, hi);
+}
+
+// The same with the position's tables cs / sn in memory.
+__device__ __forceinline__ void kv_post_finish(const KvPostIn& in, float eps, const float* cs, const float* sn,
+                                               int lane, __nv_bfloat16 (&outc)[16], float& lo, float& hi) {
+    kv_post_finish_r(in, eps, cs[lane], sn[lane], cs[32 + lane], sn[32 + lane], lane, outc, lo, hi);
 }
 
 // kv_post_load + kv_post_finish, for callers with nothing to overlap.
