@@ -407,28 +407,36 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     traffic = ncu_traffic(args.workload)
 
     # ---- the q | kv_a projection (K0, the step before the task) and o_proj + residual
-    # (K5, the step after), decode batches only; both weights fit in L2, so L2 is flushed
-    # before every timed call
-    projection = None
-    if B <= native.MAX_PROJECT_BATCH:
-        ptimer = StepTimer(stream, 0, dev)
-        runner.attend_x(x_n, cache, out, stage="project")
-        k0_ms = ptimer(lambda: runner.attend_x(x_n, cache, out, stage="project"), max(5, args.steps))
-        w_bytes = runner.w_qkv.numel() * 2
-        projection = {"kernel": "k0_project", "weight_bytes": w_bytes, "k0_us": round(k0_ms * 1e3, 2),
-                      "k0_gbs": round(w_bytes / (k0_ms * 1e-3) / 1e9, 1),
-                      "k0_frac_of_peak": round(w_bytes / (k0_ms * 1e-3) / 1e9 / peak, 4),
-                      "l2": "flushed: 256 MB written before every timed call, outside its CUDA events"}
-        h = torch.randn(B, 2048, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(dev)
-        h2 = torch.empty_like(h)
-        po = runner.params(None, None, cache, out, x_n=x_n, residual=h, h_out=h2)
-        native.check(lib.mla_o_proj(ctypes.byref(po), sptr), "o_proj")
-        k5_ms = ptimer(lambda: lib.mla_o_proj(ctypes.byref(po), sptr), max(5, args.steps))
-        wo_bytes = runner.w_o.numel() * 2
-        projection["o_proj"] = {"kernel": "k_weight_stream<16, residual>", "weight_bytes": wo_bytes,
-                                "k5_us": round(k5_ms * 1e3, 2),
-                                "k5_gbs": round(wo_bytes / (k5_ms * 1e-3) / 1e9, 1),
-                                "k5_frac_of_peak": round(wo_bytes / (k5_ms * 1e-3) / 1e9 / peak, 4)}
+    # (K5, the step after): a weight stream up to 64 requests, a tcgen05 GEMM beyond;
+    # cuBLAS on the same operands beside them. L2 flushed before every timed call.
+    ptimer = StepTimer(stream, 0, dev)
+    runner.attend_x(x_n, cache, out, stage="project")
+    k0_ms = ptimer(lambda: runner.attend_x(x_n, cache, out, stage="project", check=False), max(5, args.steps))
+    cublas_ms = ptimer(lambda: runner.project(x_n), max(5, args.steps))
+    w_bytes = runner.w_qkv.numel() * 2
+    gemm = B > native.MAX_PROJECT_BATCH
+    flops = 2 * B * runner.w_qkv.shape[0] * runner.w_qkv.shape[1]
+    bf16_peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops") \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    projection = {"kernel": "k_project_tc (tcgen05 GEMM, 4-CTA clusters split K)" if gemm else
+                  "k_weight_stream<32> (m16n8k16 weight stream)",
+                  "batch": B, "weight_bytes": w_bytes, "k0_us": round(k0_ms * 1e3, 2),
+                  "cublas_us_same_operands": round(cublas_ms * 1e3, 2),
+                  "k0_gbs": round(w_bytes / (k0_ms * 1e-3) / 1e9, 1),
+                  "k0_frac_of_hbm_peak": round(w_bytes / (k0_ms * 1e-3) / 1e9 / peak, 4),
+                  "k0_tflops": round(flops / (k0_ms * 1e-3) / 1e12, 1),
+                  "k0_frac_of_bf16_peak": round(flops / (k0_ms * 1e-3) / 1e12 / bf16_peak, 4),
+                  "l2": "flushed: 256 MB written before every timed call, outside its CUDA events"}
+    h = torch.randn(B, 2048, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(dev)
+    h2 = torch.empty_like(h)
+    po = runner.params(None, None, cache, out, x_n=x_n, residual=h, h_out=h2)
+    native.check(lib.mla_o_proj(ctypes.byref(po), sptr), "o_proj")
+    k5_ms = ptimer(lambda: lib.mla_o_proj(ctypes.byref(po), sptr), max(5, args.steps))
+    wo_bytes = runner.w_o.numel() * 2
+    projection["o_proj"] = {"kernel": "k_project_tc<residual>" if gemm else "k_weight_stream<16, residual>",
+                            "weight_bytes": wo_bytes, "k5_us": round(k5_ms * 1e3, 2),
+                            "k5_gbs": round(wo_bytes / (k5_ms * 1e-3) / 1e9, 1),
+                            "k5_frac_of_hbm_peak": round(wo_bytes / (k5_ms * 1e-3) / 1e9 / peak, 4)}
 
     # ---- e2e through the public API: pinned host x_n -> device, the task, R(out) -> host,
     # every step. HostPipeline (graph.py) replays the step as a CUDA graph and overlaps the
@@ -505,21 +513,22 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
             torch.cuda.empty_cache()
         others["clocks"] = oclocks.summary()
 
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_oracle_sample(args.workload, args.cpu_seconds, faithful=False)
-        for k in ("seconds", "bytes", "requests"):
-            cpu.pop(k, None)
-    if seq is not None:
-        inp = seq.pop("_check_inputs")
-        if rank == 0:  # the CPU leg also checks the sequence-sharded output against the oracle
-            seq["check"] = check_sequence_sharded(inp)
-
+    seq_inp = seq.pop("_check_inputs") if seq is not None else None
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    # CPU leg, rank 0 alone once the other ranks have left (a rank waiting in a collective
+    # would compete for the host cores): the CPU baseline, and the oracle's check of the
+    # sequence-sharded output
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_oracle_sample(args.workload, args.cpu_seconds, faithful=False)
+        for k in ("seconds", "bytes", "requests"):
+            cpu.pop(k, None)
+    if seq_inp is not None:
+        seq["check"] = check_sequence_sharded(seq_inp)
     us = ms_max * 1e3
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -547,8 +556,8 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                 "h2d_bytes_per_step": int(x_n.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2),
                 "path": ("HostPipeline (double-buffered graphs, copies on their own streams)" if timer.flush is None
                          else "HostStepGraph (one graph: copy in, step, copy out)") +
-                        ": pinned x_n H2D, the step (q|kv_a projection: K0 for <= 64 requests, else cuBLAS; "
-                        "K1-K3), R(out) D2H", "mode": e2e_mode},
+                        ": pinned x_n H2D, the step (K0: q|kv_a projection in the library, a weight stream "
+                        "for <= 64 requests, a tcgen05 GEMM beyond; K1-K3), R(out) D2H", "mode": e2e_mode},
         "gpu_launches": native.load_library().mla_launches_per_step() * args.steps,
         "clocks": clocks.summary(),
     }
@@ -719,17 +728,17 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
     with clocks:
         blk = sequence_sharded_block(args, rank, world, dev, dist, exchange=args.exchange)
     inp = blk.pop("_check_inputs")
-    cpu = None
-    if rank == 0:  # CPU leg: the oracle's check of the combined output, and the CPU baseline
-        blk["check"] = check_sequence_sharded(inp)
-        if not args.no_cpu_baseline:
-            cpu = cpu_oracle_sample("config5b", args.cpu_seconds, faithful=False)
-            for k in ("seconds", "bytes", "requests"):
-                cpu.pop(k, None)
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
         return
+    # CPU leg, rank 0 alone: the oracle's check of the combined output, and the CPU baseline
+    blk["check"] = check_sequence_sharded(inp)
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_oracle_sample("config5b", args.cpu_seconds, faithful=False)
+        for k in ("seconds", "bytes", "requests"):
+            cpu.pop(k, None)
     us = blk["us_per_layer_step"]
     line = {
         "metric": METRIC, "value": blk["kv_gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,

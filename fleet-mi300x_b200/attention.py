@@ -6,12 +6,14 @@ this token's cache row, attends and returns o_proj of the result. The north-star
 slice kept here starts at the post-RMSNorm hidden state x_n (:224) and ends at the
 head-concatenated bf16 output R(out) before o_proj (:256):
 
-    q, kv_a      = R(W_q x_n), R(W_kv_a x_n)       cuBLAS bf16 GEMM (torch), one fused [W_q; W_kv_a]
+    K0 project   q, kv_a = R(W_q x_n), R(W_kv_a x_n) with the fused [W_q; W_kv_a]: a
+                 weight stream up to 64 requests, a tcgen05 GEMM beyond   (libmla_decode.so)
     K1 prologue  kv_post + cache append + q_pe RoPE + q_c = q_nope W_UK      (libmla_decode.so)
     K2 attention split-KV scores, online softmax, P c_kv (m16n8k16 MMAs)    (libmla_decode.so)
     K3 merge     fixed-order LSE merge + W_UV up-projection, bf16 out       (libmla_decode.so)
 
-Everything after the GEMM runs in the C-ABI library; there is no CPU path.
+All of it runs in the C-ABI library; there is no CPU path. (project() below is a
+cuBLAS GEMM through torch, kept for callers that want q / kv_a themselves.)
 """
 from __future__ import annotations
 
@@ -223,7 +225,7 @@ class MlaDecodeAttention:
     def attend_x(self, x_n: torch.Tensor, cache: PagedLatentCache, out: torch.Tensor | None = None,
                  stage: str = "all", *, check: bool | str = True) -> torch.Tensor:
         """The whole slice in the library, from the post-RMSNorm hidden state x_n
-        [B, 2048] bf16 (B <= 64): K0 projects q | kv_a, then K1-K3 as in attend()."""
+        [B, 2048] bf16: K0 projects q | kv_a, then K1-K3 as in attend()."""
         self._pre_check(check)
         self._check_x(x_n, cache)
         if out is None:
@@ -248,9 +250,9 @@ class MlaDecodeAttention:
                         h_out: torch.Tensor | None = None, out: torch.Tensor | None = None, *,
                         check: bool | str = True) -> torch.Tensor:
         """The attention half of a decoder layer (reference_decode.py:300):
-        h_out = R(residual + R(W_o R(attention(x_n)))), with R(out) left in `out`.
-        Decode batches (<= 64 requests) run as one library call, K0 through K5;
-        larger ones use cuBLAS for the two projections around attend()."""
+        h_out = R(residual + R(W_o R(attention(x_n)))), with R(out) left in `out`:
+        one library call, K0 through K5 (inputs that break the library's alignment
+        rules take torch's o_proj around the slice instead)."""
         B = x_n.shape[0]
         if self.w_o is None:
             raise ValueError("attention_block needs LayerWeights.o_proj")
@@ -260,7 +262,7 @@ class MlaDecodeAttention:
             h_out = torch.empty_like(residual)
         if out is None:
             out = torch.empty(B, self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16, device=self.device)
-        fused = (B <= native.MAX_PROJECT_BATCH and x_n.stride(-1) == 1 and x_n.data_ptr() % 16 == 0
+        fused = (x_n.stride(-1) == 1 and x_n.data_ptr() % 16 == 0
                  and _row_stride(x_n) % 8 == 0 and out.data_ptr() % 16 == 0 and _row_stride(out) % 8 == 0
                  and residual.stride(-1) == 1 and h_out.stride(-1) == 1 and _row_stride(residual) % 4 == 0
                  and _row_stride(h_out) % 4 == 0)
@@ -283,8 +285,6 @@ class MlaDecodeAttention:
             raise ValueError("x_n rows must be contiguous")
         if x_n.shape[0] != cache.batch:
             raise ValueError(f"batch {x_n.shape[0]} does not match the cache's {cache.batch} requests")
-        if x_n.shape[0] > native.MAX_PROJECT_BATCH:
-            raise ValueError(f"the in-library projection takes at most {native.MAX_PROJECT_BATCH} requests")
 
     def project(self, x_n: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """q = R(W_q x_n), kv_a = R(W_kv_a x_n) as views of one bf16 GEMM output.
@@ -297,12 +297,11 @@ class MlaDecodeAttention:
 
     def __call__(self, x_n: torch.Tensor, cache: PagedLatentCache,
                  out: torch.Tensor | None = None, *, check: bool | str = True) -> torch.Tensor:
-        """x_n -> R(out). Decode batches (<= 64 requests) run the projection in the
-        library (attend_x: a weight stream at HBM rate); larger batches, where the
-        projection is a compute-bound GEMM, use cuBLAS and then attend(). `check` as
-        in attend()."""
-        if x_n.shape[0] <= native.MAX_PROJECT_BATCH and x_n.stride(-1) == 1 and \
-                x_n.data_ptr() % 16 == 0 and _row_stride(x_n) % 8 == 0:
+        """x_n -> R(out), projection included, in the library (attend_x: a weight
+        stream up to 64 requests, a tcgen05 GEMM beyond). x_n that breaks the
+        projection's alignment rules (16-byte rows, a row stride of 8 elements) is
+        projected by cuBLAS and then attended. `check` as in attend()."""
+        if x_n.stride(-1) == 1 and x_n.data_ptr() % 16 == 0 and _row_stride(x_n) % 8 == 0:
             return self.attend_x(x_n, cache, out, check=check)
         self._pre_check(check)
         q, kv_a = self.project(x_n)

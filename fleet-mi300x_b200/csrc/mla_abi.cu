@@ -37,6 +37,9 @@ cudaError_t launch_o_proj(const MlaDecodeParams& p, const CUtensorMap& tmap_w, c
                           cudaStream_t stream);
 cudaError_t launch_project(const MlaDecodeParams& p, __nv_bfloat16* qkv, const CUtensorMap& tmap_w,
                            const CUtensorMap& tmap_x, cudaStream_t stream);
+cudaError_t k0w_configure();
+cudaError_t launch_project_tc(int epi, const GemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
+                              cudaStream_t stream);
 
 namespace {
 
@@ -61,8 +64,8 @@ int device_info(int* sm_count) {
         cudaDeviceProp prop;
         if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) { d.status = MLA_E_LAUNCH; return; }
         if (prop.major != 10) { d.status = MLA_E_ARCH; return; }
-        if (k0_configure() != cudaSuccess || k1_configure() != cudaSuccess || k2_configure() != cudaSuccess ||
-            k2_mma_configure() != cudaSuccess || k3_configure() != cudaSuccess) {
+        if (k0_configure() != cudaSuccess || k0w_configure() != cudaSuccess || k1_configure() != cudaSuccess ||
+            k2_configure() != cudaSuccess || k2_mma_configure() != cudaSuccess || k3_configure() != cudaSuccess) {
             d.status = MLA_E_LAUNCH;
             return;
         }
@@ -157,7 +160,41 @@ int make_tmap_x(CUtensorMap* m, const void* x, int batch, int64_t x_stride) {
     return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
 }
 
+// [rows][2048] bf16 with a row pitch of `stride` elements as an operand of the
+// tensor-core projection: dims {64 columns, rows, 32 column blocks}, box {64,
+// box_rows, 1} (one 64-column block of box_rows rows, 128-byte swizzle); rows past
+// `rows` read as zeros.
+int make_tmap_operand(CUtensorMap* m, const void* base, int rows, int64_t stride, int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn;
+    if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, kHidden / 64};
+    cuuint64_t strides[2] = {(cuuint64_t)stride * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MLA_OK : MLA_E_DRIVER;
+}
+
+// Batches beyond MLA_MAX_PROJECT_BATCH: the projection as a tensor-core GEMM (epi 0:
+// y = bf16(x W^T); epi 1: y = bf16(residual + bf16(x W^T))).
+int run_gemm_tc(int epi, const GemmArgs& a, const void* x, int64_t x_stride, const void* w, cudaStream_t s) {
+    CUtensorMap tx, tw;
+    int st = make_tmap_operand(&tx, x, a.batch, x_stride, 256);
+    if (st != MLA_OK) return st;
+    st = make_tmap_operand(&tw, w, a.n_rows, kHidden, 128);
+    if (st != MLA_OK) return st;
+    return launch_project_tc(epi, a, tx, tw, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
+}
+
 int run_project(const MlaDecodeParams& q, cudaStream_t s) {
+    if (q.batch > MLA_MAX_PROJECT_BATCH) {
+        __nv_bfloat16* qkv =
+            reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(q.workspace) + ws_layout(q).qkv);
+        const GemmArgs a{qkv, kQkvRows, nullptr, 0, q.batch, kQkvRows, err_sink(q)};
+        return run_gemm_tc(0, a, q.x_n, q.x_stride, q.w_qkv, s);
+    }
     CUtensorMap tw, tx;
     int st = make_tmap_weight(&tw, q.w_qkv, kQkvRows, 32);
     if (st != MLA_OK) return st;
@@ -168,6 +205,12 @@ int run_project(const MlaDecodeParams& q, cudaStream_t s) {
 }
 
 int run_o_proj(const MlaDecodeParams& q, cudaStream_t s) {
+    if (q.batch > MLA_MAX_PROJECT_BATCH) {
+        const GemmArgs a{reinterpret_cast<__nv_bfloat16*>(q.h_out), q.h_out_stride,
+                         reinterpret_cast<const __nv_bfloat16*>(q.residual), q.residual_stride, q.batch, kHidden,
+                         err_sink(q)};
+        return run_gemm_tc(1, a, q.out, q.out_stride, q.w_o, s);
+    }
     CUtensorMap tw, tx;
     int st = make_tmap_weight(&tw, q.w_o, kHidden, 16);
     if (st != MLA_OK) return st;
@@ -254,14 +297,12 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         return MLA_E_INVALID_ARG;
     if (p->w_o) {  // K5 reads `out` back through a TMA map and writes h_out
         if (!p->out || p->shard_out || !p->residual || !p->h_out) return MLA_E_INVALID_ARG;
-        if (p->batch > MLA_MAX_PROJECT_BATCH) return MLA_E_LIMIT;
         if (p->residual_stride < MLA_HIDDEN || p->h_out_stride < MLA_HIDDEN) return MLA_E_INVALID_ARG;
         if (!aligned(p->out, 16) || (p->out_stride & 7) || !aligned(p->w_o, 16) || !aligned(p->residual, 8) ||
             (p->residual_stride & 3) || !aligned(p->h_out, 8) || (p->h_out_stride & 3))
             return MLA_E_MISALIGNED;
     }
     if (project) {
-        if (p->batch > MLA_MAX_PROJECT_BATCH) return MLA_E_LIMIT;
         if (p->x_stride < MLA_HIDDEN) return MLA_E_INVALID_ARG;
         if (!aligned(p->x_n, 16) || (p->x_stride & 7) || !aligned(p->w_qkv, 16)) return MLA_E_MISALIGNED;
     }

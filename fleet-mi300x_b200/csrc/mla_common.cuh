@@ -181,6 +181,17 @@ struct ErrSink {
 
 __host__ __device__ inline ErrSink err_sink(const MlaDecodeParams& p) { return ErrSink{p.error_word, p.error_host}; }
 
+// Arguments of the tensor-core projection (mla_project_tc.cu): y[b][n] = epi(sum_k
+// x[b][k] W[n][k]) for n < n_rows, b < batch; epi adds the residual for o_proj.
+struct GemmArgs {
+    __nv_bfloat16* y;
+    int64_t y_stride;
+    const __nv_bfloat16* residual;  // o_proj + residual only
+    int64_t res_stride;
+    int batch, n_rows;
+    ErrSink err;
+};
+
 __device__ __forceinline__ void record_error(const ErrSink& e, int code) {
     int won = code;
     if (e.dev) {
@@ -402,6 +413,38 @@ __device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
         : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
         : "memory");
     return r != 0;
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block cluster primitives (sm_90+): this CTA's rank, a cluster-wide
+// barrier with release/acquire ordering of shared memory, the cluster address of
+// a shared-memory location in a peer CTA, and stores into it that complete their
+// bytes on an mbarrier there (distributed shared memory; no global memory).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void dsmem_push4(uint32_t addr, float4 v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ void dsmem_push2(uint32_t addr, float2 v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
+                 ::"r"(addr), "f"(v.x), "f"(v.y), "r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ void dsmem_push1(uint32_t addr, uint32_t v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                 ::"r"(addr), "r"(v), "r"(remote_bar) : "memory");
 }
 
 // ---------------------------------------------------------------------------

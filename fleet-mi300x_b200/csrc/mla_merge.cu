@@ -54,33 +54,6 @@ constexpr int kClusterCtas = kK3ClusterCtas;  // cluster form: CTAs per (head, r
 // the plain form would leave most SMs idle.
 __host__ __device__ inline bool k3_use_cluster(int batch) { return (batch + k3::kReq - 1) / k3::kReq <= 4; }
 
-// Thread-block cluster primitives (sm_90+): this CTA's rank, a cluster-wide
-// barrier with release/acquire ordering of shared memory, the cluster address of
-// a shared-memory location in a peer CTA, and stores into it.
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t dsmem_addr(uint32_t smem_addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
-    return r;
-}
-// Stores into a peer CTA's shared memory that complete their bytes on an mbarrier
-// there (cluster addresses from dsmem_addr).
-__device__ __forceinline__ void dsmem_push4(uint32_t addr, float4 v, uint32_t remote_bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
-                 ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar) : "memory");
-}
-__device__ __forceinline__ void dsmem_push2(uint32_t addr, float2 v, uint32_t remote_bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
-                 ::"r"(addr), "f"(v.x), "f"(v.y), "r"(remote_bar) : "memory");
-}
-
 // Partial slot s = (c + b) * heads + h: its (m, L) pair and the lane's four
 // float4 of acc (latent l = 4 lane + 128 k, k < 4).
 __device__ __forceinline__ void load_partial(const float* __restrict__ part_ml, const float* __restrict__ part_acc,

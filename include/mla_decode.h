@@ -60,7 +60,8 @@ extern "C" {
 #define MLA_ROW (MLA_KV_LORA + MLA_QK_ROPE)
 #define MLA_HIDDEN 2048                                     /* model width: x_n rows */
 #define MLA_QKV_ROWS (MLA_HEADS * (MLA_QK_NOPE + MLA_QK_ROPE) + MLA_ROW)  /* 3648: [W_q; W_kv_a] */
-#define MLA_MAX_PROJECT_BATCH 64                            /* batch limit of the in-library projection */
+#define MLA_MAX_PROJECT_BATCH 64                            /* the projections of batches up to this stream their
+                                                               weight (m16n8k16); larger batches run a tcgen05 GEMM */
 #define MLA_MAX_RANKS 8                                     /* shards of a step with the peer exchange */
 #define MLA_IPC_HANDLE_BYTES 64                             /* size of an exchange buffer's IPC handle */
 
@@ -151,8 +152,11 @@ typedef struct MlaDecodeParams {
 
     /* In-library q | kv_a projection (ABI v3). If x_n is set, the step first
      * computes q = R(W_q x_n) and kv_a = R(W_kv_a x_n) itself (K0, into the
-     * workspace) and q / kv_a above must be NULL; the batch is then limited to
-     * MLA_MAX_PROJECT_BATCH. NULL = q / kv_a are given (ABI v2 behaviour). */
+     * workspace) and q / kv_a above must be NULL. Up to MLA_MAX_PROJECT_BATCH
+     * requests K0 streams the weight (m16n8k16); beyond, it is a tcgen05 GEMM (256
+     * requests x 128 weight rows per CTA, K split over a 4-CTA cluster whose
+     * partials meet in distributed shared memory). NULL = q / kv_a are given (ABI
+     * v2 behaviour). */
     const void* x_n;          /* [batch][x_stride] bf16 post-RMSNorm hidden state, 16-byte aligned */
     int64_t x_stride;         /* elements between rows, a multiple of 8, >= MLA_HIDDEN */
     const void* w_qkv;        /* [MLA_QKV_ROWS][MLA_HIDDEN] bf16 = rows of q_proj then kv_a_proj_with_mqa,
@@ -161,8 +165,8 @@ typedef struct MlaDecodeParams {
     /* In-library o_proj with the layer's residual add (ABI v4). If w_o is set,
      * the step ends with h_out = R(residual + R(W_o R(out))) (K5;
      * reference_decode.py:256, 300), reading `out` back (then 16-byte aligned,
-     * out_stride a multiple of 8, not with shard_out); the batch is limited to
-     * MLA_MAX_PROJECT_BATCH. NULL = the step ends at R(out). */
+     * out_stride a multiple of 8, not with shard_out); the two forms of K0 by
+     * batch. NULL = the step ends at R(out). */
     const void* w_o;          /* [MLA_HIDDEN][MLA_HEADS*MLA_V_HEAD] bf16 o_proj.weight, 16-byte aligned */
     const void* residual;     /* [batch][residual_stride] bf16: the layer's input hidden state */
     int64_t residual_stride;  /* elements between rows, a multiple of 4, >= MLA_HIDDEN */

@@ -31,7 +31,7 @@ def _setup(dev, B, seed):
     return runner, cache, x, h, lw, w_o, lens
 
 
-@pytest.mark.parametrize("B", [1, 9, 64])
+@pytest.mark.parametrize("B", [1, 9, 64, 65, 256])  # 65, 256: the tcgen05 GEMM form of K5
 def test_o_proj_residual_matches_numpy_on_the_same_out(cuda_device, B):
     runner, cache, x, h, _, w_o, _ = _setup(cuda_device, B, 70)
     out = torch.empty(B, 2048, dtype=BF, device=cuda_device)
