@@ -418,7 +418,7 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     flops = 2 * B * runner.w_qkv.shape[0] * runner.w_qkv.shape[1]
     bf16_peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops") \
         if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
-    projection = {"kernel": "k_project_tc (tcgen05 GEMM, 4-CTA clusters split K)" if gemm else
+    projection = {"kernel": "k_project_tc (tcgen05 GEMM, 128 x 64 tiles over all of K)" if gemm else
                   "k_weight_stream<32> (m16n8k16 weight stream)",
                   "batch": B, "weight_bytes": w_bytes, "k0_us": round(k0_ms * 1e3, 2),
                   "cublas_us_same_operands": round(cublas_ms * 1e3, 2),
@@ -556,8 +556,9 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
                 "h2d_bytes_per_step": int(x_n.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2),
                 "path": ("HostPipeline (double-buffered graphs, copies on their own streams)" if timer.flush is None
                          else "HostStepGraph (one graph: copy in, step, copy out)") +
-                        ": pinned x_n H2D, the step (K0: q|kv_a projection in the library, a weight stream "
-                        "for <= 64 requests, a tcgen05 GEMM beyond; K1-K3), R(out) D2H", "mode": e2e_mode},
+                        ": pinned x_n H2D, the step (q|kv_a projection: the library's weight stream for <= 64 "
+                        "requests, else cuBLAS, measured faster than the library's tcgen05 GEMM here; K1-K3), "
+                        "R(out) D2H", "mode": e2e_mode},
         "gpu_launches": native.load_library().mla_launches_per_step() * args.steps,
         "clocks": clocks.summary(),
     }

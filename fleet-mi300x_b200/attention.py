@@ -7,13 +7,17 @@ slice kept here starts at the post-RMSNorm hidden state x_n (:224) and ends at t
 head-concatenated bf16 output R(out) before o_proj (:256):
 
     K0 project   q, kv_a = R(W_q x_n), R(W_kv_a x_n) with the fused [W_q; W_kv_a]: a
-                 weight stream up to 64 requests, a tcgen05 GEMM beyond   (libmla_decode.so)
+                 weight stream up to 64 requests, a tcgen05 GEMM beyond   (libmla_decode.so;
+                 above 64 requests __call__ uses cuBLAS instead, measured faster here)
     K1 prologue  kv_post + cache append + q_pe RoPE + q_c = q_nope W_UK      (libmla_decode.so)
     K2 attention split-KV scores, online softmax, P c_kv (m16n8k16 MMAs)    (libmla_decode.so)
     K3 merge     fixed-order LSE merge + W_UV up-projection, bf16 out       (libmla_decode.so)
 
-All of it runs in the C-ABI library; there is no CPU path. (project() below is a
-cuBLAS GEMM through torch, kept for callers that want q / kv_a themselves.)
+All of it runs in the C-ABI library; there is no CPU path. project() below is a
+cuBLAS GEMM through torch: __call__ takes it above 64 requests, where the library's
+own tcgen05 GEMM is slower (17.4 against 12.9 us at 256 requests: without TMA
+multicast, which code that runs on several GPUs here must not use, each of its CTAs
+streams its rows of x_n itself), and callers that want q / kv_a themselves use it.
 """
 from __future__ import annotations
 
@@ -250,9 +254,10 @@ class MlaDecodeAttention:
                         h_out: torch.Tensor | None = None, out: torch.Tensor | None = None, *,
                         check: bool | str = True) -> torch.Tensor:
         """The attention half of a decoder layer (reference_decode.py:300):
-        h_out = R(residual + R(W_o R(attention(x_n)))), with R(out) left in `out`:
-        one library call, K0 through K5 (inputs that break the library's alignment
-        rules take torch's o_proj around the slice instead)."""
+        h_out = R(residual + R(W_o R(attention(x_n)))), with R(out) left in `out`.
+        Decode batches (<= 64 requests) run as one library call, K0 through K5;
+        larger ones (and inputs that break the library's alignment rules) use cuBLAS
+        for the two projections around attend(), as __call__ does."""
         B = x_n.shape[0]
         if self.w_o is None:
             raise ValueError("attention_block needs LayerWeights.o_proj")
@@ -262,7 +267,7 @@ class MlaDecodeAttention:
             h_out = torch.empty_like(residual)
         if out is None:
             out = torch.empty(B, self.cfg.heads * self.cfg.v_head, dtype=torch.bfloat16, device=self.device)
-        fused = (x_n.stride(-1) == 1 and x_n.data_ptr() % 16 == 0
+        fused = (B <= native.MAX_PROJECT_BATCH and x_n.stride(-1) == 1 and x_n.data_ptr() % 16 == 0
                  and _row_stride(x_n) % 8 == 0 and out.data_ptr() % 16 == 0 and _row_stride(out) % 8 == 0
                  and residual.stride(-1) == 1 and h_out.stride(-1) == 1 and _row_stride(residual) % 4 == 0
                  and _row_stride(h_out) % 4 == 0)
@@ -297,11 +302,11 @@ class MlaDecodeAttention:
 
     def __call__(self, x_n: torch.Tensor, cache: PagedLatentCache,
                  out: torch.Tensor | None = None, *, check: bool | str = True) -> torch.Tensor:
-        """x_n -> R(out), projection included, in the library (attend_x: a weight
-        stream up to 64 requests, a tcgen05 GEMM beyond). x_n that breaks the
-        projection's alignment rules (16-byte rows, a row stride of 8 elements) is
-        projected by cuBLAS and then attended. `check` as in attend()."""
-        if x_n.stride(-1) == 1 and x_n.data_ptr() % 16 == 0 and _row_stride(x_n) % 8 == 0:
+        """x_n -> R(out). Decode batches (<= 64 requests) run the projection in the
+        library (attend_x: a weight stream at HBM rate); larger batches project with
+        cuBLAS (see project()) and then attend(). `check` as in attend()."""
+        if x_n.shape[0] <= native.MAX_PROJECT_BATCH and x_n.stride(-1) == 1 and \
+                x_n.data_ptr() % 16 == 0 and _row_stride(x_n) % 8 == 0:
             return self.attend_x(x_n, cache, out, check=check)
         self._pre_check(check)
         q, kv_a = self.project(x_n)

@@ -38,6 +38,9 @@ cudaError_t launch_o_proj(const MlaDecodeParams& p, const CUtensorMap& tmap_w, c
 cudaError_t launch_project(const MlaDecodeParams& p, __nv_bfloat16* qkv, const CUtensorMap& tmap_w,
                            const CUtensorMap& tmap_x, cudaStream_t stream);
 cudaError_t k0w_configure();
+int k0w_box_rows_x();
+int k0w_box_rows_w();
+int k0w_box_blocks();
 cudaError_t launch_project_tc(int epi, const GemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                               cudaStream_t stream);
 
@@ -162,14 +165,14 @@ int make_tmap_x(CUtensorMap* m, const void* x, int batch, int64_t x_stride) {
 
 // [rows][2048] bf16 with a row pitch of `stride` elements as an operand of the
 // tensor-core projection: dims {64 columns, rows, 32 column blocks}, box {64,
-// box_rows, 1} (one 64-column block of box_rows rows, 128-byte swizzle); rows past
-// `rows` read as zeros.
-int make_tmap_operand(CUtensorMap* m, const void* base, int rows, int64_t stride, int box_rows) {
+// box_rows, blocks} (landing as [blocks][box_rows rows][128 B], 128-byte swizzle);
+// rows past `rows` read as zeros.
+int make_tmap_operand(CUtensorMap* m, const void* base, int rows, int64_t stride, int box_rows, int blocks) {
     PFN_cuTensorMapEncodeTiled_v12000 fn;
     if (encode_fn(&fn) != MLA_OK) return MLA_E_DRIVER;
     cuuint64_t dims[3] = {64, (cuuint64_t)rows, kHidden / 64};
     cuuint64_t strides[2] = {(cuuint64_t)stride * 2, 128};
-    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)blocks};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -181,9 +184,9 @@ int make_tmap_operand(CUtensorMap* m, const void* base, int rows, int64_t stride
 // y = bf16(x W^T); epi 1: y = bf16(residual + bf16(x W^T))).
 int run_gemm_tc(int epi, const GemmArgs& a, const void* x, int64_t x_stride, const void* w, cudaStream_t s) {
     CUtensorMap tx, tw;
-    int st = make_tmap_operand(&tx, x, a.batch, x_stride, 256);
+    int st = make_tmap_operand(&tx, x, a.batch, x_stride, k0w_box_rows_x(), k0w_box_blocks());
     if (st != MLA_OK) return st;
-    st = make_tmap_operand(&tw, w, a.n_rows, kHidden, 128);
+    st = make_tmap_operand(&tw, w, a.n_rows, kHidden, k0w_box_rows_w(), k0w_box_blocks());
     if (st != MLA_OK) return st;
     return launch_project_tc(epi, a, tx, tw, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }

@@ -7,29 +7,35 @@
 // weight-stream kernel (mla_project.cu) runs instead; beyond that the product is
 // a GEMM (3.8 GFLOP at 256 requests for K0) with M = batch.
 //
-// Tiling: a CTA owns 256 batch rows (two M = 128 tcgen05 tiles) x 128 weight rows
-// (N = 128) over one quarter of K (512). The four quarters of an output tile are
-// the four CTAs of a thread-block cluster, so 116 CTAs cover K0 at 256 requests.
-//   * warp 0, one thread: TMA producer. Per 64-column chunk of K, one box of x
-//     (256 rows, rows past the batch read as zeros) and one of W (128 rows, rows
-//     past N as zeros), 48 KB, into a 4-stage ring; the first four W chunks are
-//     requested before the wait on the previous kernel (no kernel writes a weight).
-//     No multicast.
-//   * warp 1: allocates 256 columns of tensor memory (D of the two M tiles, fp32)
-//     and one thread issues tcgen05.mma (kind::f16, bf16 operands, both K-major in
-//     128-byte swizzled tiles), 4 K-steps x 2 M tiles per chunk, commits each
-//     stage back to the producer and the last one to the epilogue.
-//   * all 4 warps, epilogue: warp w reads its 32 lanes (batch rows) of D. The four
-//     K-quarter partials meet through distributed shared memory: rank r of the
-//     cluster sums output columns [32 r, 32 r + 32) of the tile. Each rank first
-//     tells every peer that its stage ring is free (one 4-byte st.async per peer
-//     on the peer's mbarrier), waits for the same from all peers, then pushes each
-//     peer its 32 columns of every row (st.async, completing bytes on the peer's
-//     receive mbarrier) and keeps its own. Once all three peers' bytes have landed
-//     it adds the four partials in rank order (a fixed order: the result does not
-//     depend on timing), rounds (and for K5 adds the residual), and stores bf16.
-// Every wait is bounded (mla::mbar_wait); the protocol runs to its end on every
-// rank even after a timeout, which is recorded in the error word.
+// Tiling: a CTA owns 128 batch rows (one M = 128 tcgen05 tile) x 64 weight rows
+// (N = 64) over the whole K, so no partial sums cross CTAs and the epilogue goes
+// from tensor memory straight to global memory (K0 at 256 requests: 57 x 2 = 114
+// CTAs). Warp roles:
+//   * warp 0, one thread: TMA producer. Per 256-column chunk of K (8 chunks), one
+//     box of x (128 rows x 4 column blocks, 64 KB; rows past the batch read as
+//     zeros) and one of W (64 rows x 4 blocks, 32 KB; rows past N as zeros) into a
+//     2-stage ring (192 KB in flight). Large boxes: a copy engine moves far more
+//     bytes per SM in few large requests than in many 8-16 KB ones. The first two W
+//     chunks are requested before the wait on the previous kernel (no kernel
+//     writes a weight). No multicast.
+//   * warp 1: allocates 64 columns of tensor memory (D, fp32) and one thread
+//     issues tcgen05.mma (kind::f16, bf16 operands, both K-major in 128-byte
+//     swizzled tiles), 16 K-steps per chunk, committing each stage back to the
+//     producer and the last one to the epilogue.
+//   * all 4 warps, epilogue: warp w reads its 32 lanes (batch rows) of D, rounds
+//     (K5: adds the residual and rounds again) and stores 64 bf16 per row.
+// Every wait is bounded (mla::mbar_wait); a timeout is recorded in the error word.
+//
+// Measured at 256 requests, L2 flushed before each call (1x B200): 17.4 us, against
+// 12.9 us for cuBLAS's GEMM on the same operands. Each of the 114 CTAs streams 768 KB
+// (its 128 rows of x and 64 rows of W over all of K) at about 50 GB/s. cuBLAS's kernel
+// here runs in 2 x 4 thread-block clusters, whose TMA multicast shares operand tiles
+// across CTAs; code that runs on several GPUs in this pool must not use multicast
+// loads, so the Python host keeps cuBLAS above 64 requests and this kernel serves C
+// callers (the x_n / w_o fields) that want the whole block without cuBLAS. Measured
+// and not kept: 24 KB stages (20.5 us), 48 KB stages (18.4 us), and K split over a
+// 4-CTA cluster with the partials summed through distributed shared memory (21.8 us:
+// 96 KB of 16-byte pushes per CTA).
 #include <cuda.h>
 
 #include "mla_common.cuh"
@@ -39,29 +45,26 @@
 namespace mla {
 
 namespace k0w {
-constexpr int kBM = 256;                          // batch rows per CTA: two M = 128 MMA tiles
-constexpr int kBN = 128;                          // weight rows per CTA: the MMA's N
-constexpr int kSplit = 4;                         // K quarters = CTAs of a cluster
-constexpr int kKc = 64;                           // K per chunk: one 128-byte swizzle atom of bf16
-constexpr int kChunks = kHidden / kSplit / kKc;   // 8
-constexpr int kStages = 4;
-constexpr int kABytes = kBM * kKc * 2;            // 32768: [256 rows][128 B]
-constexpr int kBBytes = kBN * kKc * 2;            // 16384: [128 rows][128 B]
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kNq = kBN / kSplit;                 // 32 output columns summed by each rank
-constexpr int kRecvPitch = kNq + 4;               // floats per row of a received block (16-byte aligned,
-                                                  // 8 consecutive rows in distinct bank groups)
-constexpr int kRecvBytes = kSplit * kBM * kRecvPitch * 4;  // [source rank][row][kRecvPitch] fp32
+constexpr int kBM = 128;                          // batch rows per CTA: the MMA's M
+constexpr int kBN = 64;                           // weight rows per CTA: the MMA's N
+constexpr int kBlk = 4;                           // 64-column blocks (128-byte swizzle atoms) per chunk
+constexpr int kKc = 64 * kBlk;                    // K per chunk: 256
+constexpr int kChunks = kHidden / kKc;            // 8
+constexpr int kStages = 2;
+constexpr int kABlock = kBM * 128;                // 16384: one block of x, [128 rows][128 B]
+constexpr int kBBlock = kBN * 128;                // 8192: one block of W, [64 rows][128 B]
+constexpr int kABytes = kBlk * kABlock;           // 65536
+constexpr int kBBytes = kBlk * kBBlock;           // 32768
+constexpr int kStageBytes = kABytes + kBBytes;    // 96 KB, a multiple of 1024 (swizzle atoms stay aligned)
 constexpr int kThreads = 128;
-constexpr int kTmemCols = 256;
-static_assert(kRecvBytes <= kStages * kStageBytes, "the receive blocks reuse the stage ring");
+constexpr int kTmemCols = 64;
 static_assert(kChunks >= kStages, "the producer requests the first kStages weight chunks up front");
-constexpr uint32_t kIdesc = idesc_bf16_f32(128, kBN, 0, 0);
+static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
+constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN, 0, 0);
 
 struct Smem {
     uint64_t full[kStages], empty[kStages];
-    uint64_t done, ready, recv;
-    uint32_t ready_word[kSplit];
+    uint64_t done;
     uint32_t tmem;
     int abort;
 };
@@ -78,27 +81,26 @@ __global__ void __launch_bounds__(k0w::kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Smem& S = *reinterpret_cast<Smem*>(smem + kStages * kStageBytes);
-    float* recv = reinterpret_cast<float*>(smem);  // after every rank's MMAs: [source][row][kRecvPitch]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rank = (int)cluster_rank();            // the K quarter of this CTA
-    const int n0 = (blockIdx.x / kSplit) * kBN;
+    const int n0 = blockIdx.x * kBN;
     const int m0 = blockIdx.y * kBM;
-    const int mt = min(2, (a.batch - m0 + 127) / 128);  // M tiles that hold batch rows
+    // K order rotated per weight tile: the tiles of one batch block read different
+    // chunks of x at any moment instead of all the same L2 lines at once
+    const int k_rot = blockIdx.x % kChunks;
     volatile int* abort = &S.abort;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], 1); }
         mbar_init(&S.done, 1);
-        mbar_init(&S.ready, 1);
-        mbar_init(&S.recv, 1);
         S.abort = 0;
         fence_mbar_init();
-        // bytes the peers will complete here: a 4-byte "ready" from each, then 128 B per
-        // row of each M tile from each
-        mbar_arrive_expect_tx(&S.ready, (kSplit - 1) * 4);
-        mbar_arrive_expect_tx(&S.recv, (uint32_t)(kSplit - 1) * mt * 128 * kNq * 4);
         prefetch_tmap(&tmap_x);
         prefetch_tmap(&tmap_w);
+        for (int c = 0; c < kStages; ++c) {  // the weight's first chunks: no kernel writes it
+            mbar_arrive_expect_tx(&S.full[c], kStageBytes);
+            tma_load_3d(smem + c * kStageBytes + kABytes, &tmap_w, &S.full[c], 0, n0,
+                        kBlk * ((c + k_rot) % kChunks), kCacheEvictFirst);
+        }
     }
     if (warp == 1) {
         tmem_alloc(&S.tmem, kTmemCols);
@@ -107,16 +109,7 @@ __global__ void __launch_bounds__(k0w::kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    cluster_sync_all();  // every rank's barriers are initialised before any peer completes bytes on them
     const uint32_t tmem = S.tmem;
-    const int k_blk0 = rank * kChunks;  // first 64-column block of this quarter
-
-    if (warp == 0 && lane == 0) {  // the weight's first chunks: no kernel writes it
-        for (int c = 0; c < kStages; ++c) {
-            mbar_arrive_expect_tx(&S.full[c], kStageBytes);
-            tma_load_3d(smem + c * kStageBytes + kABytes, &tmap_w, &S.full[c], 0, n0, k_blk0 + c, kCacheEvictFirst);
-        }
-    }
     pdl_wait();  // x (and the residual) come from earlier work on the stream
     MLA_TL_WAITED(4);
     pdl_trigger();
@@ -130,13 +123,14 @@ __global__ void __launch_bounds__(k0w::kThreads, 1)
                 if (n > 0) {
                     if (!mbar_wait(&S.empty[s], (n - 1) & 1, abort, a.err)) break;
                     mbar_arrive_expect_tx(&S.full[s], kStageBytes);
-                    tma_load_3d(smem + s * kStageBytes + kABytes, &tmap_w, &S.full[s], 0, n0, k_blk0 + c,
-                                kCacheEvictFirst);
+                    tma_load_3d(smem + s * kStageBytes + kABytes, &tmap_w, &S.full[s], 0, n0,
+                                kBlk * ((c + k_rot) % kChunks), kCacheEvictFirst);
                 }
-                tma_load_3d(smem + s * kStageBytes, &tmap_x, &S.full[s], 0, m0, k_blk0 + c, kCacheEvictLast);
+                tma_load_3d(smem + s * kStageBytes, &tmap_x, &S.full[s], 0, m0, kBlk * ((c + k_rot) % kChunks),
+                            kCacheEvictLast);
             }
-            // Drain: every issued copy lands before the ring is reused or released (the
-            // loop issues both copies of the first kStages chunks without a wait, so c >= kStages)
+            // Drain: every issued copy lands before the ring is released (both copies of
+            // the first kStages chunks go out without a wait, so c >= kStages here).
             for (int s = 0; s < kStages; ++s) {
                 const int fills = c / kStages + (s < c % kStages ? 1 : 0);
                 if (fills) mbar_drain(&S.full[s], (fills - 1) & 1, a.err);
@@ -153,13 +147,11 @@ __global__ void __launch_bounds__(k0w::kThreads, 1)
                 tc_fence_after();
                 const uint32_t sa = base + s * kStageBytes, sb = sa + kABytes;
 #pragma unroll
-                for (int kk = 0; kk < kKc / 16; ++kk) {
-                    const uint64_t bd = dK + ((sb + kk * 32) >> 4);
-                    for (int m = 0; m < mt; ++m) {
-                        const uint64_t ad = dK + ((sa + m * (128 * 128) + kk * 32) >> 4);
-                        tc_mma_f16(tmem + m * kBN, ad, bd, kIdesc, (c | kk) ? 1u : 0u);
-                    }
-                }
+                for (int j = 0; j < kBlk; ++j)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_f16(tmem, dK + ((sa + j * kABlock + kk * 32) >> 4),
+                                   dK + ((sb + j * kBBlock + kk * 32) >> 4), kIdesc, (c | j | kk) ? 1u : 0u);
                 tc_commit(&S.empty[s]);
             }
             tc_commit(&S.done);  // also after an abort: every issued MMA completes before the epilogue
@@ -170,80 +162,35 @@ __global__ void __launch_bounds__(k0w::kThreads, 1)
     // ---------------------------------------------------------------- epilogue (all warps)
     mbar_wait(&S.done, 0, abort, a.err);
     tc_fence_after();
-    // this rank's stage ring is free: tell every peer, then wait until every peer's is
-    if (threadIdx.x == 0) {
-        const uint32_t wl = smem_u32(&S.ready_word[rank]), bl = smem_u32(&S.ready);
-        for (int q = 0; q < kSplit; ++q)
-            if (q != rank) dsmem_push1(dsmem_addr(wl, (uint32_t)q), 1u, dsmem_addr(bl, (uint32_t)q));
-    }
-    mbar_wait(&S.ready, 0, abort, a.err);
-    // rows 32 warp + lane of each M tile: columns [32 q, 32 q + 32) go to rank q
-    const uint32_t recv_l = smem_u32(recv), recv_bar = smem_u32(&S.recv);
-    for (int m = 0; m < mt; ++m) {
-        const int row = m * 128 + 32 * warp + lane;
-#pragma unroll 1
-        for (int q = 0; q < kSplit; ++q) {
-            float v[32];
-            const uint32_t ta = tmem_lane_addr(tmem, warp, m * kBN + kNq * q);
-            tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(v));
-            tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-            tmem_wait_ld();
-            const uint32_t off = (uint32_t)((rank * kBM + row) * kRecvPitch) * 4u;  // slot [rank][row] at q
-            if (q == rank) {
+    const int row = 32 * warp + lane, b = m0 + row;
+    float v[kBN];
 #pragma unroll
-                for (int j = 0; j < kNq; j += 4)
-                    *reinterpret_cast<float4*>(recv + (rank * kBM + row) * kRecvPitch + j) =
-                        make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-                const uint32_t dst = dsmem_addr(recv_l + off, (uint32_t)q), bar = dsmem_addr(recv_bar, (uint32_t)q);
-#pragma unroll
-                for (int j = 0; j < kNq; j += 4)
-                    dsmem_push4(dst + 4u * j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]), bar);
-            }
-        }
-    }
-    mbar_wait(&S.recv, 0, abort, a.err);
+    for (int j = 0; j < kBN; j += 16)
+        tmem_ld16(tmem_lane_addr(tmem, warp, j), *reinterpret_cast<float(*)[16]>(v + j));
+    tmem_wait_ld();
     tc_fence_before();
-    __syncthreads();  // own block written; every tcgen05.ld done before the tensor memory is freed
+    __syncthreads();  // every tcgen05.ld done before the tensor memory is freed
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
-
-    // sum of the four K quarters in rank order, epilogue, store (thread = one row of a tile)
-    const int ncol0 = n0 + kNq * rank;
-    for (int m = 0; m < mt; ++m) {
-        const int row = m * 128 + threadIdx.x, b = m0 + row;
-        if (b >= a.batch || ncol0 >= a.n_rows) continue;
-        float acc[kNq];
+    if (b >= a.batch) return;
+    // 8-byte accesses: K5's residual and h_out rows are 8-byte aligned (strides of 4 elements)
+    __nv_bfloat16* yrow = a.y + (int64_t)b * a.y_stride + n0;
+    const __nv_bfloat16* rrow = kEpi ? a.residual + (int64_t)b * a.res_stride + n0 : nullptr;
 #pragma unroll
-        for (int j = 0; j < kNq; ++j) acc[j] = 0.f;
-#pragma unroll
-        for (int src = 0; src < kSplit; ++src) {
-            const float* r = recv + (src * kBM + row) * kRecvPitch;
-#pragma unroll
-            for (int j = 0; j < kNq; j += 4) {
-                const float4 x = *reinterpret_cast<const float4*>(r + j);
-                acc[j] += x.x; acc[j + 1] += x.y; acc[j + 2] += x.z; acc[j + 3] += x.w;
-            }
+    for (int j = 0; j < kBN; j += 4) {
+        if (n0 + j >= a.n_rows) break;  // the last tile of K0's 3648 rows is half full
+        float o[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
+        if (kEpi) {
+            const uint2 rv = *reinterpret_cast<const uint2*>(rrow + j);
+            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+            o[0] = __low2float(r2[0]) + bf16_round(o[0]);
+            o[1] = __high2float(r2[0]) + bf16_round(o[1]);
+            o[2] = __low2float(r2[1]) + bf16_round(o[2]);
+            o[3] = __high2float(r2[1]) + bf16_round(o[3]);
         }
-        // 8-byte accesses: K5's residual and h_out rows are 8-byte aligned (strides of 4 elements)
-        __nv_bfloat16* yrow = a.y + (int64_t)b * a.y_stride + ncol0;
-        const __nv_bfloat16* rrow = kEpi ? a.residual + (int64_t)b * a.res_stride + ncol0 : nullptr;
-#pragma unroll
-        for (int j = 0; j < kNq; j += 4) {
-            if (ncol0 + j >= a.n_rows) break;  // the last tile of K0's 3648 rows is half full
-            float v[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
-            if (kEpi) {
-                const uint2 rv = *reinterpret_cast<const uint2*>(rrow + j);
-                const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
-                v[0] = __low2float(r2[0]) + bf16_round(v[0]);
-                v[1] = __high2float(r2[0]) + bf16_round(v[1]);
-                v[2] = __low2float(r2[1]) + bf16_round(v[2]);
-                v[3] = __high2float(r2[1]) + bf16_round(v[3]);
-            }
-            uint2 o;
-            o.x = pack_bf16(v[0], v[1]);
-            o.y = pack_bf16(v[2], v[3]);
-            *reinterpret_cast<uint2*>(yrow + j) = o;
-        }
+        uint2 st;
+        st.x = pack_bf16(o[0], o[1]);
+        st.y = pack_bf16(o[2], o[3]);
+        *reinterpret_cast<uint2*>(yrow + j) = st;
     }
 }
 
@@ -254,27 +201,18 @@ cudaError_t k0w_configure() {
     return cudaFuncSetAttribute(k_project_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, k0w::kSmemBytes);
 }
 
+int k0w_box_rows_x() { return k0w::kBM; }
+int k0w_box_rows_w() { return k0w::kBN; }
+int k0w_box_blocks() { return k0w::kBlk; }
+
 // x [batch][2048] (row pitch x_stride elements) and W [n_rows][2048] as the operand maps
 // of the kernel: dims {64 columns, rows, 32 column blocks}, 128-byte swizzle, boxes of
-// 256 (x) and 128 (W) rows by one 64-column block.
+// k0w_box_rows_x() / k0w_box_rows_w() rows by k0w_box_blocks() 64-column blocks.
 cudaError_t launch_project_tc(int epi, const GemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                               cudaStream_t stream) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(((a.n_rows + k0w::kBN - 1) / k0w::kBN) * k0w::kSplit, (a.batch + k0w::kBM - 1) / k0w::kBM);
-    cfg.blockDim = dim3(k0w::kThreads);
-    cfg.dynamicSmemBytes = k0w::kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = k0w::kSplit;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    return epi ? cudaLaunchKernelEx(&cfg, k_project_tc<1>, a, tmap_x, tmap_w)
-               : cudaLaunchKernelEx(&cfg, k_project_tc<0>, a, tmap_x, tmap_w);
+    const dim3 grid((a.n_rows + k0w::kBN - 1) / k0w::kBN, (a.batch + k0w::kBM - 1) / k0w::kBM);
+    return epi ? launch_pdl(k_project_tc<1>, grid, dim3(k0w::kThreads), k0w::kSmemBytes, stream, a, tmap_x, tmap_w)
+               : launch_pdl(k_project_tc<0>, grid, dim3(k0w::kThreads), k0w::kSmemBytes, stream, a, tmap_x, tmap_w);
 }
 
 }  // namespace mla

@@ -153,10 +153,9 @@ typedef struct MlaDecodeParams {
     /* In-library q | kv_a projection (ABI v3). If x_n is set, the step first
      * computes q = R(W_q x_n) and kv_a = R(W_kv_a x_n) itself (K0, into the
      * workspace) and q / kv_a above must be NULL. Up to MLA_MAX_PROJECT_BATCH
-     * requests K0 streams the weight (m16n8k16); beyond, it is a tcgen05 GEMM (256
-     * requests x 128 weight rows per CTA, K split over a 4-CTA cluster whose
-     * partials meet in distributed shared memory). NULL = q / kv_a are given (ABI
-     * v2 behaviour). */
+     * requests K0 streams the weight (m16n8k16); beyond, it is a tcgen05 GEMM (128
+     * requests x 64 weight rows x all of K per CTA, accumulators in tensor memory).
+     * NULL = q / kv_a are given (ABI v2 behaviour). */
     const void* x_n;          /* [batch][x_stride] bf16 post-RMSNorm hidden state, 16-byte aligned */
     int64_t x_stride;         /* elements between rows, a multiple of 8, >= MLA_HIDDEN */
     const void* w_qkv;        /* [MLA_QKV_ROWS][MLA_HIDDEN] bf16 = rows of q_proj then kv_a_proj_with_mqa,
