@@ -684,10 +684,55 @@ def sequence_sharded_block(args, rank: int, world: int, dev: torch.device, dist,
     step()  # a whole step last: the exchange's step counter advances on every rank
     torch.cuda.synchronize()
     runner.check_errors()
-    t = torch.tensor([t1_ms, tn_ms] + stage_ms, device=dev)
+
+    # ---- the same in a 27-layer decode step (LayerStackGraph): every layer its own rows,
+    # whole on one GPU and sharded over the N, the shards of all layers sharing the
+    # exchange buffers (one protocol step per layer)
+    layers = STACK_LAYERS
+    stack_one = stack_n = None
+    g_rows = torch.Generator(device=dev).manual_seed(wl.seed + 17)
+    full_l, shard_l = [], []
+    for l in range(layers):
+        rl = torch.randn(T, 576, generator=g_rows, device=dev).to(torch.bfloat16)
+        c1 = fleet.PagedLatentCache.for_lengths([T], permute=True, zero=False,
+                                                generator=torch.Generator().manual_seed(l), device=dev)
+        c1.write_rows(0, 0, rl)
+        cn = fleet.PagedLatentCache.for_lengths([b - a], extra_tokens=1 if last else 0, permute=True, zero=False,
+                                                generator=torch.Generator().manual_seed(l + 100 * rank), device=dev)
+        cn.write_rows(0, 0, rl[a:b])
+        full_l.append(c1)
+        shard_l.append(cn)
+        del rl
+    st1 = fleet.LayerStackGraph([runner] * layers, full_l, mode="slice", q=[q] * layers, kv_a=[kv_a] * layers)
+    kw = dict(rope_pos=pos, new_row=last)
+    if ex is not None:
+        kw["exchange"] = ex
+    if dist is not None:
+        dist.barrier()
+    stn = fleet.LayerStackGraph([runner] * layers, shard_l, mode="slice", q=[q] * layers, kv_a=[kv_a] * layers,
+                                attend_kw=kw) if ex is not None else None
+    stimer = StepTimer(stream, layers * kv_b // world, dev)
+    for _ in range(3):
+        st1.replay()
+    st1.synchronize()
+    stack_one = stimer(st1.replay, max(5, steps // 2)) / layers
+    st1.synchronize()
+    if stn is not None:
+        for _ in range(3):
+            stn.replay()
+        stn.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        stack_n = stimer(stn.replay, max(5, steps // 2)) / layers
+        stn.synchronize()
+    del st1, stn
+    torch.cuda.synchronize()
+
+    t = torch.tensor([t1_ms, tn_ms, stack_one, stack_n or 0.0] + stage_ms, device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t1_ms, tn_ms, *stage_ms = t.tolist()
+    t1_ms, tn_ms, stack_one, stack_n, *stage_ms = t.tolist()
 
     # ---- the combined output against the one-GPU step on the same rows; rank 0 keeps the
     # inputs for the oracle check of its CPU leg (check_sequence_sharded)
@@ -719,6 +764,14 @@ def sequence_sharded_block(args, rank: int, world: int, dev: torch.device, dist,
         "kv_bytes_per_step": kv_b, "kv_bytes_per_gpu": kv_b // world,
         "l2": timer.describe(), "timing": "device time per step, CUDA events, max over ranks",
         "max_rel_vs_one_gpu": rel1, "check": None, "_check_inputs": check_inputs,
+        "stack": None if ex is None else {
+            "layers": layers, "us_per_layer_step": round(stack_n * 1e3, 3),
+            "one_gpu_us_per_layer_step": round(stack_one * 1e3, 3),
+            "speedup_vs_one_gpu": round(stack_one / stack_n, 3),
+            "strong_scaling_efficiency": round(stack_one / (world * stack_n), 4),
+            "kv_frac_of_hbm_peak_per_gpu": round(kv_b / world / (stack_n * 1e-3) / 1e9 / peak, 4),
+            "what": "27 layers in one CUDA graph (LayerStackGraph), each layer its own 131,072 rows; on N GPUs "
+                    "each rank its shard of every layer, one exchange buffer set for all layers"},
     }
 
 

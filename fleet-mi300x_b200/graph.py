@@ -217,6 +217,9 @@ class LayerStackGraph:
     mode="slice": layer l runs its attention task K1-K3 from its own q / kv_a buffers
       (self.q[l], self.kv_a[l]) over caches[l] into self.out[l]: the attention slice of
       every layer with its own weights and cache, the unit the per-layer-step metric counts.
+      `attend_kw` is passed to every layer's MlaDecodeAttention.attend, e.g. rope_pos,
+      new_row and exchange for one shard of a sequence-sharded step (the layers then
+      share the exchange buffers: each layer's step is one step of its protocol).
     mode="block": the hidden state self.h [B, 2048] flows through the layers: for each l,
       x_n = RMSNorm(h, in_norms[l]) (torch), then runners[l].attention_block(x_n, caches[l],
       residual=h, h_out=h) (K0-K5: projection, attention, o_proj and the residual add in the
@@ -228,12 +231,13 @@ class LayerStackGraph:
     """
 
     def __init__(self, runners, caches, *, mode: str = "slice", q=None, kv_a=None, h=None, in_norms=None,
-                 ffn=None, advance: bool = False):
+                 ffn=None, advance: bool = False, attend_kw: dict | None = None):
         if mode not in ("slice", "block"):
             raise ValueError("mode must be 'slice' or 'block'")
         if len(runners) != len(caches) or not runners:
             raise ValueError("one cache per runner, at least one layer")
         self.runners, self.caches, self.mode, self.ffn = list(runners), list(caches), mode, ffn
+        self.attend_kw = dict(attend_kw or {})
         r0, dev, B = runners[0], runners[0].device, caches[0].batch
         cfg, bf = r0.cfg, torch.bfloat16
         if any(c.batch != B for c in caches):
@@ -278,7 +282,7 @@ class LayerStackGraph:
     def _step(self) -> None:
         if self.mode == "slice":
             for l, (r, c) in enumerate(zip(self.runners, self.caches)):
-                r.attend(self.q[l], self.kv_a[l], c, self.out[l])
+                r.attend(self.q[l], self.kv_a[l], c, self.out[l], **self.attend_kw)
             return
         for l, (r, c) in enumerate(zip(self.runners, self.caches)):
             self.x_n.copy_(rms_norm_bf16(self.h, self.in_norms[l], r.cfg.rms_eps))
