@@ -15,9 +15,9 @@ head-concatenated bf16 output R(out) before o_proj (:256):
 
 All of it runs in the C-ABI library; there is no CPU path. project() below is a
 cuBLAS GEMM through torch: __call__ takes it above 64 requests, where the library's
-own tcgen05 GEMM is slower (17.4 against 12.9 us at 256 requests: without TMA
-multicast, which code that runs on several GPUs here must not use, each of its CTAs
-streams its rows of x_n itself), and callers that want q / kv_a themselves use it.
+own tcgen05 GEMM is slower (17.4 against 12.9 us at 256 requests: it uses no cluster
+multicast loads, so each of its CTAs streams its rows of x_n itself), and callers that
+want q / kv_a themselves use it.
 """
 from __future__ import annotations
 

@@ -29,9 +29,9 @@
 // Measured at 256 requests, L2 flushed before each call (1x B200): 17.4 us, against
 // 12.9 us for cuBLAS's GEMM on the same operands. Each of the 114 CTAs streams 768 KB
 // (its 128 rows of x and 64 rows of W over all of K) at about 50 GB/s. cuBLAS's kernel
-// here runs in 2 x 4 thread-block clusters, whose TMA multicast shares operand tiles
-// across CTAs; code that runs on several GPUs in this pool must not use multicast
-// loads, so the Python host keeps cuBLAS above 64 requests and this kernel serves C
+// here is a 2 x 4-cluster kernel by its name, whose CTAs can share operand tiles
+// within a cluster; this library uses no cluster multicast loads (its code also runs
+// on several GPUs), so the Python host keeps cuBLAS above 64 requests and this kernel serves C
 // callers (the x_n / w_o fields) that want the whole block without cuBLAS. Measured
 // and not kept: 24 KB stages (20.5 us), 48 KB stages (18.4 us), and K split over a
 // 4-CTA cluster with the partials summed through distributed shared memory (21.8 us:
