@@ -15,7 +15,8 @@
 // bits of o_c, as the reference's fp32 GEMV does. Three forms (k3_launch):
 //   * cluster form, batches of at most 4 blocks of 16: a thread-block cluster of 4
 //     CTAs per (head, block), each folding a quarter of the partials and owning 32
-//     rows of W_UV; the folds meet through distributed shared memory;
+//     rows of W_UV; the folds meet through distributed shared memory. Batches of
+//     5-16 run as two blocks of 4 or 8 requests (k3_cluster_rpb);
 //   * plain form, one CTA per (head, block of 16), while that grid fits one wave;
 //   * plain form in blocks of 32 (two m16 tiles on one staged W_UV[h]) beyond.
 // Sequence-sharded steps end here too: shard_out (fp32 partials for a gather) or
@@ -148,7 +149,7 @@ __device__ __forceinline__ void k3_fused_combine(const MlaDecodeParams& p, const
 // inside a request (PartIdx).
 template <int kCl, int kRq, bool kFuse>
 __global__ void __launch_bounds__(k3::kThreads, 1)
-    k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb, int pairs) {
+    k3_merge_uv(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kvb, int pairs, int rpb) {
     using namespace k3;
     MLA_TL_SCOPE(2);
     using Sh = Shape<kCl, kRq>;
@@ -171,8 +172,8 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
 
     const int q = kCl > 1 ? (int)cluster_rank() : 0;  // rank within the (head, request block) cluster
     const int h = blockIdx.x / kCl;
-    const int b0 = blockIdx.y * kRq;
-    const int nreq = min(kRq, p.batch - b0);
+    const int b0 = blockIdx.y * rpb;  // rpb <= kRq requests per block (rows past them are zero)
+    const int nreq = min(rpb, p.batch - b0);
 
     // cluster form: bar[1] counts the bytes of the other ranks' folds pushed into xch
     constexpr uint32_t kPushBytes = (kLora + 2) * 4;  // one request's acc[512], m, L
@@ -832,20 +833,27 @@ namespace {
 // shared memory), beyond that in blocks of 32 (two m16 tiles on one staged W_UV[h]),
 // which halves the waves.
 struct K3Launch {
-    int cl, rq;
+    int cl, rq, rpb;  // form, m16 capacity of a block, requests per block
     dim3 grid;
 };
 
+// The cluster form fills two blocks where the batch allows: 5-8 requests run as two
+// blocks of 4 and 9-16 as two of 8 (128 CTAs instead of 64), so each CTA folds half
+// as many partials; the W_UV MMA still runs one m16 tile, its rows past the block zero.
+inline int k3_cluster_rpb(int batch) { return batch <= 4 ? 4 : batch <= 8 ? 4 : batch <= 16 ? 8 : k3::kReq; }
+
 K3Launch k3_launch(int batch, int sm_count) {
-    if (k3_use_cluster(batch))
-        return {k3::kClusterCtas, k3::kReq, dim3(kHeads * k3::kClusterCtas, (batch + k3::kReq - 1) / k3::kReq)};
+    if (k3_use_cluster(batch)) {
+        const int rpb = k3_cluster_rpb(batch);
+        return {k3::kClusterCtas, k3::kReq, rpb, dim3(kHeads * k3::kClusterCtas, (batch + rpb - 1) / rpb)};
+    }
     const int blocks16 = (batch + k3::kReq - 1) / k3::kReq;
-    if (kHeads * blocks16 <= sm_count) return {1, k3::kReq, dim3(kHeads, blocks16)};
-    return {1, 2 * k3::kReq, dim3(kHeads, (batch + 2 * k3::kReq - 1) / (2 * k3::kReq))};
+    if (kHeads * blocks16 <= sm_count) return {1, k3::kReq, k3::kReq, dim3(kHeads, blocks16)};
+    return {1, 2 * k3::kReq, 2 * k3::kReq, dim3(kHeads, (batch + 2 * k3::kReq - 1) / (2 * k3::kReq))};
 }
 
 template <int kCl, int kRq, bool kFuse>
-cudaError_t k3_launch_form(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, dim3 grid, int pairs,
+cudaError_t k3_launch_form(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, dim3 grid, int pairs, int rpb,
                            cudaStream_t stream, bool query_only, bool* resident) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -877,18 +885,18 @@ cudaError_t k3_launch_form(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb
         }
         return e;
     }
-    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl, kRq, kFuse>, p, tmap_kvb, pairs);
+    return cudaLaunchKernelEx(&cfg, k3_merge_uv<kCl, kRq, kFuse>, p, tmap_kvb, pairs, rpb);
 }
 
 template <bool kFuse>
 cudaError_t k3_dispatch(const MlaDecodeParams& p, const CUtensorMap& tmap_kvb, const K3Launch& l, int pairs,
                         cudaStream_t stream, bool query_only, bool* resident) {
     if (l.cl > 1)
-        return k3_launch_form<k3::kClusterCtas, k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, stream, query_only,
-                                                                resident);
+        return k3_launch_form<k3::kClusterCtas, k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, l.rpb, stream,
+                                                                query_only, resident);
     if (l.rq == k3::kReq)
-        return k3_launch_form<1, k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, stream, query_only, resident);
-    return k3_launch_form<1, 2 * k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, stream, query_only, resident);
+        return k3_launch_form<1, k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, l.rpb, stream, query_only, resident);
+    return k3_launch_form<1, 2 * k3::kReq, kFuse>(p, tmap_kvb, l.grid, pairs, l.rpb, stream, query_only, resident);
 }
 
 }  // namespace
