@@ -509,9 +509,6 @@ def run_gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
             for n in others:
                 others[n]["stack"] = stack_summary(n, dev, max(10, args.steps), peak0)
                 torch.cuda.empty_cache()
-                if others[n]["batch"] == 1:  # one request: also as the one-kernel step
-                    others[n]["fused_step"] = fused_summary(n, dev, max(10, args.steps), peak0)
-                    torch.cuda.empty_cache()
             stack = stack_summary(args.workload, dev, max(5, args.steps // 2), peak0)
             torch.cuda.empty_cache()
         others["clocks"] = oclocks.summary()
@@ -818,8 +815,7 @@ def run_sequence_sharded(args, rank: int, world: int, local_rank: int, dev: torc
 STACK_LAYERS = 27  # DeepSeek-V2-Lite's decoder layers
 
 
-def stack_summary(name: str, dev: torch.device, steps: int, peak: float, layers: int = STACK_LAYERS,
-                  fused: bool = False) -> dict:
+def stack_summary(name: str, dev: torch.device, steps: int, peak: float, layers: int = STACK_LAYERS) -> dict:
     """The attention slice of `layers` layers as one CUDA graph (LayerStackGraph, slice
     mode): each layer has its own weights (seeded per layer) and its own cache with the
     workload's shape, as in a decoder, so the step reads layers x the KV bytes. Device time
@@ -836,7 +832,7 @@ def stack_summary(name: str, dev: torch.device, steps: int, peak: float, layers:
         lw = workloads.make_layer_weights(wl.seed + 1000 * (l + 1))
         w = fleet.LayerWeights(*(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm,
                                                        lw.kv_b_proj)))
-        r = fleet.MlaDecodeAttention(cfg, w, cos, sin, fused_step=fused)
+        r = fleet.MlaDecodeAttention(cfg, w, cos, sin)
         c = fleet.PagedLatentCache.for_lengths(lengths, permute=wl.permute, zero=False,
                                                generator=torch.Generator().manual_seed(wl.seed + l), device=dev)
         workloads.fill_pool_random(c.pages, wl.seed + 7919 * (l + 1))
@@ -899,38 +895,6 @@ def other_config_summary(name: str, dev: torch.device, steps: int, peak: float) 
                           "merge_uv": round(k3 * 1e3, 2)},
             "attention_frac_of_hbm_peak": round(kv_b / (k2 * 1e-3) / 1e9 / peak, 4),
             "l2": "flushed before every timed call" if timer.flush is not None else "no flush (> 4x L2 per step)"}
-
-
-def fused_summary(name: str, dev: torch.device, steps: int, peak: float) -> dict:
-    """A one-request configuration as the one-kernel step (MLA_FLAG_FUSED_STEP): the
-    single-layer graph step after an L2 flush and the 27-layer stack, as for K1-K3. The
-    fused output is checked against the three-kernel step's (max rel <= 5e-3) first."""
-    wl, lengths, runner, cache, x_n, q, kv_a = build_workload(name, dev, 0)
-    if len(lengths) != 1:
-        raise ValueError("the one-kernel step serves one request")
-    kv_b = workloads.kv_bytes(lengths)
-    stream = torch.cuda.current_stream(dev)
-    fused = fleet.MlaDecodeAttention(runner.cfg, runner.w, runner.cos, runner.sin, fused_step=True)
-    ref = runner.attend(q, kv_a, cache)
-    out = torch.empty_like(ref)
-    graph = fleet.DecodeGraph(fused, cache, inputs="qkv", q=q, kv_a=kv_a, out=out)
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    fused.check_errors()
-    rel = float((out.float() - ref.float()).abs().max() / ref.float().abs().max())
-    if rel > 5e-3:
-        raise RuntimeError(f"{name}: the one-kernel step differs from K1-K3 (max rel {rel:.3e})")
-    timer = StepTimer(stream, kv_b, dev)
-    ms = timer(graph.replay, steps)
-    torch.cuda.synchronize()
-    fused.check_errors()
-    gbs = kv_b / (ms * 1e-3) / 1e9
-    return {"kernel": "k2_attention_mma<fused> (prologue, split-KV attention, merge + W_UV in one launch)",
-            "us_per_layer_step": round(ms * 1e3, 2), "kv_gbs": round(gbs, 1),
-            "kv_frac_of_hbm_peak": round(gbs / peak, 4), "max_rel_vs_three_kernels": round(rel, 6),
-            "l2": "flushed before every timed call" if timer.flush is not None else "no flush (> 4x L2 per step)",
-            "stack": stack_summary(name, dev, steps, peak, fused=True)}
 
 
 def run_split_sweep(args, runner, cache, q, kv_a, lengths, stream) -> None:

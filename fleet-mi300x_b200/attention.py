@@ -75,14 +75,11 @@ class MlaDecodeAttention:
 
     def __init__(self, cfg: ModelConfig, w: LayerWeights, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
                  *, num_ctas: int = 0, check_kernel: bool = False, kernel: str = "mma", qc_hilo: bool = False,
-                 p_hilo: bool = False, fused_step: bool = False):
+                 p_hilo: bool = False):
         """qc_hilo / p_hilo (default kernel only): keep the absorbed query, and the
         probabilities of P c_kv, as bf16 hi/lo pairs instead of rounding them to bf16
         (MLA_FLAG_QC_HILO / MLA_FLAG_P_HILO), closer to the reference's fp32 q_c and P
-        (reference_decode.py:250-253) at the cost of more tensor-core issue in K2.
-        fused_step (default kernel and precision): steps of one request run as one kernel
-        (MLA_FLAG_FUSED_STEP: prologue, split-KV attention and merge in one launch);
-        larger batches keep the three kernels."""
+        (reference_decode.py:250-253) at the cost of more tensor-core issue in K2."""
         cfg.check_supported()
         self.cfg = cfg
         self.lib = native.load_library()
@@ -104,9 +101,6 @@ class MlaDecodeAttention:
         if (qc_hilo or p_hilo) and self.flags:
             raise ValueError("qc_hilo / p_hilo exist in the default (mma) kernel only")
         self.flags |= (native.FLAG_QC_HILO if qc_hilo else 0) | (native.FLAG_P_HILO if p_hilo else 0)
-        if fused_step and self.flags:
-            raise ValueError("fused_step runs the default kernel at default precision only")
-        self.fused_step = bool(fused_step)
         self.error_word = torch.zeros(1, dtype=torch.int32, device=dev)
         # pinned host copy of the error word: the kernels store a code into it when they
         # record one (MlaDecodeParams.error_host), so the host sees a failed step
@@ -152,8 +146,6 @@ class MlaDecodeAttention:
         p.error_host = _ptr(self.error_host)
         p.num_ctas = self.num_ctas
         p.flags = self.flags | (0 if new_row else native.FLAG_NO_NEW_ROW)
-        if self.fused_step and B == 1:
-            p.flags |= native.FLAG_FUSED_STEP
         p.rope_pos = _ptr(rope_pos)
         p.shard_out = _ptr(shard_out)
         if exchange is not None:
@@ -167,8 +159,7 @@ class MlaDecodeAttention:
         need = ctypes.c_uint64()
         native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
         if self._ws is None or self._ws.numel() < need.value:
-            # zero-filled: the one-kernel step's counters at its start must read zero
-            self._ws = torch.zeros(int(need.value), dtype=torch.uint8, device=self.device)
+            self._ws = torch.empty(int(need.value), dtype=torch.uint8, device=self.device)
         p.workspace = _ptr(self._ws)
         p.workspace_bytes = self._ws.numel()
         return p
@@ -356,7 +347,7 @@ class MlaDecodeAttention:
         p = native.new_params()
         p.batch = batch
         p.num_ctas = self.num_ctas
-        p.flags = self.flags | (native.FLAG_FUSED_STEP if self.fused_step and batch == 1 else 0)
+        p.flags = self.flags
         need = ctypes.c_uint64()
         native.check(self.lib.mla_workspace_size(ctypes.byref(p), ctypes.byref(need)), "mla_workspace_size")
         return int(need.value)

@@ -27,9 +27,6 @@ cudaError_t launch_combine_shards(const float* parts, int n_shards, int batch, v
 cudaError_t launch_exchange_combine(const MlaDecodeParams& p, cudaStream_t stream);
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,
                                  int sm_count, cudaStream_t stream);
-int fused_step_grid(const MlaDecodeParams& p, int sm_count);
-cudaError_t launch_fused_step(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2, int sm_count,
-                              cudaStream_t stream);
 cudaError_t k2_configure();
 cudaError_t k2_mma_configure();
 cudaError_t k3_configure();
@@ -313,11 +310,8 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
         if (!aligned(p->x_n, 16) || (p->x_stride & 7) || !aligned(p->w_qkv, 16)) return MLA_E_MISALIGNED;
     }
     if (p->flags & ~(MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05 | MLA_FLAG_NO_NEW_ROW | MLA_FLAG_EXCHANGE_SPLIT |
-                     MLA_FLAG_QC_HILO | MLA_FLAG_P_HILO | MLA_FLAG_FUSED_STEP))
+                     MLA_FLAG_QC_HILO | MLA_FLAG_P_HILO))
         return MLA_E_INVALID_ARG;
-    if ((p->flags & MLA_FLAG_FUSED_STEP) &&
-        (p->batch != 1 || (p->flags & (MLA_FLAG_QC_HILO | MLA_FLAG_P_HILO | MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05))))
-        return MLA_E_INVALID_ARG;  // the one-kernel step: one request, default kernel and precision
     if ((p->flags & (MLA_FLAG_QC_HILO | MLA_FLAG_P_HILO)) && (p->flags & (MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05)))
         return MLA_E_INVALID_ARG;  // the hi/lo forms exist in the default kernel only
     if (p->world < 0 || p->world > MLA_MAX_RANKS) return MLA_E_INVALID_ARG;
@@ -373,23 +367,6 @@ int prepare(const MlaDecodeParams* p, MlaDecodeParams* out) {
 
 int run_exchange_combine(const MlaDecodeParams& q, cudaStream_t s) {
     return launch_exchange_combine(q, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
-}
-
-// The one-kernel step (MLA_FLAG_FUSED_STEP): prologue, split-KV attention and merge in
-// one launch; refused where its whole grid cannot be resident at once.
-int run_fused(const MlaDecodeParams& q, cudaStream_t s) {
-    int sms = 0;
-    int st = device_info(&sms);
-    if (st != MLA_OK) return st;
-    if (fused_step_grid(q, sms) == 0) {
-        cudaGetLastError();
-        return MLA_E_INVALID_ARG;
-    }
-    CUtensorMap tkv;
-    st = make_tmap_blocks(&tkv, q.kv_cache, (uint64_t)q.n_pages, true, kPage / 2);
-    if (st != MLA_OK) return st;
-    const float scale_log2 = (float)((double)q.softmax_scale * 1.4426950408889634);
-    return launch_fused_step(q, tkv, scale_log2, sms, s) == cudaSuccess ? MLA_OK : MLA_E_LAUNCH;
 }
 
 int run_attention(const MlaDecodeParams& q, cudaStream_t s) {
@@ -470,8 +447,7 @@ int mla_workspace_size(const MlaDecodeParams* p, uint64_t* bytes) {
     int ctas = 0;
     st = resolve_ctas(p, &ctas);
     if (st != MLA_OK) return st;
-    *bytes = ws_layout(p->batch, ctas, p->x_n != nullptr, (p->flags & MLA_FLAG_QC_HILO) != 0,
-                       (p->flags & MLA_FLAG_FUSED_STEP) != 0).total;
+    *bytes = ws_layout(p->batch, ctas, p->x_n != nullptr, (p->flags & MLA_FLAG_QC_HILO) != 0).total;
     return MLA_OK;
 }
 
@@ -482,8 +458,7 @@ int mla_plan_info(const MlaDecodeParams* p, int32_t* num_ctas, int32_t* num_slot
     st = resolve_ctas(p, &ctas);
     if (st != MLA_OK) return st;
     if (num_ctas) *num_ctas = ctas;
-    if (num_slots) *num_slots = ws_layout(p->batch, ctas, p->x_n != nullptr, (p->flags & MLA_FLAG_QC_HILO) != 0,
-                                           (p->flags & MLA_FLAG_FUSED_STEP) != 0).slots;
+    if (num_slots) *num_slots = ws_layout(p->batch, ctas, p->x_n != nullptr, (p->flags & MLA_FLAG_QC_HILO) != 0).slots;
     return MLA_OK;
 }
 
@@ -549,7 +524,6 @@ int mla_prologue(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;
     int st = prepare(p, &q);
     if (st != MLA_OK) return st;
-    if (q.flags & MLA_FLAG_FUSED_STEP) return MLA_E_INVALID_ARG;  // its work runs inside the one kernel
     return run_prologue(q, (cudaStream_t)stream);
 }
 
@@ -557,7 +531,6 @@ int mla_attention(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;
     int st = prepare(p, &q);
     if (st != MLA_OK) return st;
-    if (q.flags & MLA_FLAG_FUSED_STEP) return run_fused(q, (cudaStream_t)stream);  // the one kernel alone
     return run_attention(q, (cudaStream_t)stream);
 }
 
@@ -565,7 +538,6 @@ int mla_merge_uv(const MlaDecodeParams* p, void* stream) {
     MlaDecodeParams q;
     int st = prepare(p, &q);
     if (st != MLA_OK) return st;
-    if (q.flags & MLA_FLAG_FUSED_STEP) return MLA_E_INVALID_ARG;  // its work runs inside the one kernel
     return run_merge(q, (cudaStream_t)stream);
 }
 
@@ -585,15 +557,6 @@ int mla_decode_step(const MlaDecodeParams* p, void* stream) {
     if (q.x_n) {
         st = run_project(q, s);
         if (st != MLA_OK) return st;
-    }
-    if (q.flags & MLA_FLAG_FUSED_STEP) {
-        st = run_fused(q, s);
-        if (st != MLA_OK) return st;
-        if (q.world > 0) {
-            st = run_exchange_combine(q, s);
-            if (st != MLA_OK) return st;
-        }
-        return q.w_o ? run_o_proj(q, s) : MLA_OK;
     }
     st = run_prologue(q, s);
     if (st != MLA_OK) return st;

@@ -48,7 +48,6 @@
 #include "mla_common.cuh"
 #include "mla_tiles.cuh"
 #include "mla_mma.cuh"
-#include "mla_fused.cuh"
 
 namespace mla {
 
@@ -108,7 +107,7 @@ __device__ __forceinline__ int p_offset(int head, int u) { return head * 64 + ((
 
 }  // namespace mmak
 
-template <bool kQLo, bool kPLo, bool kFused = false>
+template <bool kQLo, bool kPLo>
 __global__ void __launch_bounds__(mmak::kThreads, 1)
     k2_attention_mma(const MlaDecodeParams p, const __grid_constant__ CUtensorMap tmap_kv, float scale_log2,
                      int pairs) {
@@ -133,10 +132,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     float* part_ml = reinterpret_cast<float*>(wsb + ws.part_ml);
     float* part_acc = reinterpret_cast<float*>(wsb + ws.part_acc);
 
-    // The one-kernel step lets the next kernel launch only after its prologue wait (the
-    // next step may read the row this one appends, and must not take an SM before every
-    // CTA of this grid is resident).
-    if constexpr (!kFused) pdl_trigger();
+    pdl_trigger();
     int vc = blockIdx.x + gridDim.x * grp;  // this group's CTA of the plan (group 1 only if the plan has
                                             // more CTAs than the grid; adjacent to group 0's when paired)
     bool paired = false;                    // adjacent plan CTAs, merged across their boundary (k2_pairs)
@@ -183,41 +179,6 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
     // on K1. It equals K1's plan (the same rule, plan_tiles), and the leader already
     // requests its first half pages, except one that holds the row K1 appends, so
     // that those copies overlap K1. Larger batches read K1's plan after the wait.
-    // One-kernel step: the 65 prologue CTAs do K1's work first, before anything of the
-    // split-KV kernel (its plan, barriers and tile requests): the inputs that no kernel
-    // writes before the wait, the rest after it, then they count themselves in `ready`.
-    // The other CTAs meanwhile plan and request their first tiles.
-    if constexpr (kFused) {
-        FusedSync* sy = reinterpret_cast<FusedSync*>(wsb + ws.sync);
-        __nv_bfloat16* qa_w = reinterpret_cast<__nv_bfloat16*>(wsb + ws.qa);
-        float* scratch = reinterpret_cast<float*>(smem + kOffStash);
-        if (blockIdx.x < fused::kAbsorbCtas) {
-            fused::AbsorbPre apre;
-            fused::absorb_pre(p, blockIdx.x, apre);
-            pdl_wait();  // q comes from the previous kernel
-            MLA_TL_SCOPE_AT(0);
-            fused::absorb_finish(p, blockIdx.x, apre, qa_w, scratch);
-            fused::signal(&sy->ready);
-            MLA_TL_WAITED(0);
-        } else if (blockIdx.x == fused::kRowCta) {
-            RowPre rpre;
-            if (warp == 0) {
-                request_rows_pre(p, 0, lane, rpre);
-                if (lane == 0 && rpre.ok) {  // the raw kv_a row into L2 (written by the previous kernel)
-                    const char* kv = reinterpret_cast<const char*>(p.kv_a);
-                    for (int o = 0; o < kRow * 2; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(kv + o));
-                }
-            }
-            pdl_wait();  // q and kv_a come from the previous kernel
-            MLA_TL_SCOPE_AT(0);
-            if (warp == 0) {
-                if (!rpre.ok && lane == 0) record_error(err_sink(p), MLA_DEV_BAD_POSITION);
-                request_rows(p, qa_w, 0, lane, rpre);
-            }
-            fused::signal(&sy->ready);
-            MLA_TL_WAITED(0);
-        }
-    }
     __shared__ int32_t pre_cum[kPrePlan + 1];
     __shared__ int32_t pre_tot[kThreads / 32];
     const bool pre = p.batch <= kPrePlan;
@@ -259,30 +220,12 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
             if (leader) {
                 init_group();
                 la.init_at(cumv, p.seq_lens, p.batch, pe, new_row_count(p));
-                const uint32_t early = kPreSlots;
-                while (issued < early && la.valid() && !holds_new_row()) issue_next();
+                while (issued < kPreSlots && la.valid() && !holds_new_row()) issue_next();
             }
         }
     }
     pdl_wait();  // the plan, absorbed queries and new rows come from K1
     MLA_TL_WAITED(1);
-    if constexpr (kFused) {
-        // every CTA waits for the prologue CTAs' work
-        FusedSync* sy = reinterpret_cast<FusedSync*>(wsb + ws.sync);
-        __shared__ int ready_ok;
-        if (threadIdx.x == 0) ready_ok = fused::wait_count(sy, &sy->ready, fused::kPrologueCtas, err_sink(p));
-        __syncthreads();
-        MLA_TL_SCOPE_AT(2);
-        fused::fence_proxy_async_global();  // the new row, written by generic stores, before any TMA of it
-        pdl_trigger();
-        if (!ready_ok) {  // gave up (the error is recorded): drain the early copies, then no tiles, no partials
-            if (leader) {
-                for (uint32_t sl = 0; sl < kNSlot; ++sl)
-                    if (sl < issued) mbar_drain(&S.full[sl], 0, err_sink(p));
-            }
-            G = 0;
-        }
-    }
     if (!pre) {
         // G, and both candidate entries (plain and paired numbering) in one round trip to the plan
         const PlanEntry* ents = reinterpret_cast<const PlanEntry*>(wsb + ws.plan + sizeof(PlanHeader));
@@ -586,11 +529,6 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         }
     }
     __syncthreads();
-    if constexpr (kFused) {
-        MLA_TL_WAITED(2);
-        const int n = G == 0 ? 0 : (paired ? 1 + (G - 1) / 2 : G);
-        fused::merge_phase(p, wsb, ws, n, paired, reinterpret_cast<float*>(smem + kOffStash));
-    }
 }
 
 int k2_mma_smem_bytes() { return mmak::kSmemBytes; }
@@ -607,34 +545,7 @@ cudaError_t k2_mma_configure() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k2_attention_mma<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  mmak::smem_bytes(true));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k2_attention_mma<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 mmak::smem_bytes(false));
     return e;
-}
-
-// The one-kernel step's grid for these params, or 0 where it cannot run: every CTA
-// must be resident at once (one per SM), the grid must hold the prologue and merge
-// CTAs, and the merge weighs at most fused::kMaxParts partials.
-int fused_step_grid(const MlaDecodeParams& p, int sm_count) {
-    const int grid = k2_grid(p.num_ctas, sm_count);
-    if (grid < fused::kMinCtas || p.num_ctas > fused::kMaxParts) return 0;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k2_attention_mma<false, false, true>, mmak::kThreads,
-                                                      mmak::smem_bytes(false)) != cudaSuccess)
-        return 0;
-    return (int64_t)per_sm * sm_count >= grid ? grid : 0;
-}
-
-cudaError_t launch_fused_step(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2, int sm_count,
-                              cudaStream_t stream) {
-    const int grid = fused_step_grid(p, sm_count);
-    if (grid == 0) return cudaErrorInvalidConfiguration;
-    const cudaError_t e = launch_pdl(k2_attention_mma<false, false, true>, dim3(grid), dim3(mmak::kThreads),
-                                     mmak::smem_bytes(false), stream, p, tmap_kv, scale_log2,
-                                     k2_pairs(p, sm_count) ? 1 : 0);
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
 }
 
 cudaError_t launch_attention_mma(const MlaDecodeParams& p, const CUtensorMap& tmap_kv, float scale_log2,

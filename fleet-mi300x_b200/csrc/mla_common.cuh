@@ -32,8 +32,6 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // ---------------------------------------------------------------------------
 // Workspace layout (bytes, each region 256-byte aligned).
-//   sync       FusedSync (256 bytes)      counters of the one-kernel step (MLA_FLAG_FUSED_STEP); no
-//                                         other kernel writes them, and that step leaves them zero
 //   tiles_cum  int32 [batch + 1]          prefix sum of 64-token tiles per request (split plan)
 //   plan       PlanHeader, PlanEntry [num_ctas]   the split plan per CTA, ready to use (K1 writes it)
 //   qa         bf16  [batch][16][576]     absorbed query q_c (512) | roped q_pe (64), per head
@@ -41,24 +39,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 //   part_acc   f32   [slots][16][512]     split partial: unnormalised sum_t p_t * c_t
 //   qkv        bf16  [batch][3648]        q | kv_a, when the step projects x_n itself (K0)
 //   qa_lo      bf16  [batch][16][512]     q_c - bf16(q_c), with MLA_FLAG_QC_HILO
-//   fy         f32   [16][8][128]         one-kernel step: W_UV partial products per (head, 64 latent columns)
 // slots = num_ctas + batch: CTA c writes the partial of request b at slot c + b.
 // ---------------------------------------------------------------------------
 struct WsLayout {
-    uint64_t sync, tiles_cum, plan, qa, part_ml, part_acc, qkv, qa_lo, fy, total;
+    uint64_t tiles_cum, plan, qa, part_ml, part_acc, qkv, qa_lo, total;
     int32_t slots;
 };
-
-// The one-kernel step's counters (all zero between steps).
-struct FusedSync {
-    uint32_t ready;      // prologue CTAs done (absorb slices, q_pe and the new row)
-    uint32_t done;       // CTAs whose split-KV partials are written
-    uint32_t exitc;      // CTAs finished; the last one zeroes the counters
-    uint32_t abort;      // a CTA gave up a wait: the others stop waiting
-    uint32_t head[16];   // W_UV partial products written per head
-};
-static_assert(sizeof(FusedSync) <= 256, "the sync region is 256 bytes");
-constexpr int kFyParts = 8;  // latent slices of 64 columns per head in the one-kernel merge
 
 // The split plan as K1's planner leaves it for the split-KV kernel: the total tile
 // count U, the number of CTAs with work G = min(U, num_ctas), and per plan CTA its
@@ -78,12 +64,10 @@ __host__ __device__ inline uint64_t align256(uint64_t x) { return (x + 255) & ~u
 // with_qkv: the step projects x_n itself (MlaDecodeParams.x_n set), and q | kv_a
 // of every request live in the workspace as [batch][3648] bf16.
 // with_qlo: MLA_FLAG_QC_HILO, the low half of q_c lives in qa_lo.
-__host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with_qkv = false, bool with_qlo = false,
-                                              bool fused = false) {
+__host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with_qkv = false, bool with_qlo = false) {
     WsLayout w;
     w.slots = num_ctas + batch;
     uint64_t off = 0;
-    w.sync = off;      off = 256;
     w.tiles_cum = off; off = align256(off + uint64_t(batch + 1) * 4);
     w.plan = off;      off = align256(off + sizeof(PlanHeader) + uint64_t(num_ctas) * sizeof(PlanEntry));
     w.qa = off;        off = align256(off + uint64_t(batch) * kQRows * kRow * 2);
@@ -91,14 +75,12 @@ __host__ __device__ inline WsLayout ws_layout(int batch, int num_ctas, bool with
     w.part_acc = off;  off = align256(off + uint64_t(w.slots) * kHeads * kLora * 4);
     w.qkv = off;       off = align256(off + (with_qkv ? uint64_t(batch) * kQkvRows * 2 : 0));
     w.qa_lo = off;     off = align256(off + (with_qlo ? uint64_t(batch) * kQRows * kLora * 2 : 0));
-    w.fy = off;        off = align256(off + (fused ? uint64_t(kHeads) * kFyParts * kV * 4 : 0));
     w.total = off;
     return w;
 }
 
 __host__ __device__ inline WsLayout ws_layout(const MlaDecodeParams& p) {
-    return ws_layout(p.batch, p.num_ctas, p.x_n != nullptr, (p.flags & MLA_FLAG_QC_HILO) != 0,
-                     (p.flags & MLA_FLAG_FUSED_STEP) != 0);
+    return ws_layout(p.batch, p.num_ctas, p.x_n != nullptr, (p.flags & MLA_FLAG_QC_HILO) != 0);
 }
 
 
@@ -665,8 +647,6 @@ __device__ __forceinline__ void tl_mark(int k, int slot) {  // slot 4 or 5; lane
 #define MLA_TL_SCOPE(k) ::mla::TlScope mla_tl_scope_(k)
 #define MLA_TL_WAITED(k) ::mla::tl_stamp(k, 1)
 #define MLA_TL_MARK(k, slot) ::mla::tl_mark(k, slot)
-#define MLA_TL_SCOPE_AT(k) ::mla::tl_stamp(k, 0)  // an entry stamp without the exit stamp
-#define MLA_TL_EXIT(k) ::mla::tl_stamp(k, 2)
 #else
 #define MLA_TL_MARK(k, slot) \
     do {                     \
@@ -676,12 +656,6 @@ __device__ __forceinline__ void tl_mark(int k, int slot) {  // slot 4 or 5; lane
     } while (0)
 #define MLA_TL_WAITED(k) \
     do {                 \
-    } while (0)
-#define MLA_TL_SCOPE_AT(k) \
-    do {                   \
-    } while (0)
-#define MLA_TL_EXIT(k) \
-    do {               \
     } while (0)
 #endif
 

@@ -121,6 +121,81 @@ __device__ void plan_entries(const MlaDecodeParams& p, const int32_t* cum, const
     }
 }
 
+// The per-request warp's inputs that no earlier kernel writes: the row count and RoPE
+// position, the RoPE table rows of that position, the block-table entry of the new
+// row and kv_a_layernorm's weight. They are loaded before the wait on the previous
+// kernel (positions, tables and weights are the step's inputs, as for the split
+// plan that K2 derives before its own wait), so that after the wait only q_pe and
+// the raw kv_a row, the previous kernel's output, remain to be loaded.
+struct RowPre {
+    int pos, rp, page;
+    bool ok, append;
+    float c0, c1, s0, s1;
+    __align__(16) __nv_bfloat16 gw[16];
+};
+
+__device__ void request_rows_pre(const MlaDecodeParams& p, int b, int lane, RowPre& r) {
+    r.pos = p.seq_lens[b];
+    r.rp = p.rope_pos ? p.rope_pos[b] : r.pos;
+    r.append = new_row_count(p) != 0;
+    const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(p.kv_a_norm_w);
+    if (r.append) {
+        if ((reinterpret_cast<uintptr_t>(gam) & 15) == 0) {
+            reinterpret_cast<uint4*>(r.gw)[0] = reinterpret_cast<const uint4*>(gam)[2 * lane];
+            reinterpret_cast<uint4*>(r.gw)[1] = reinterpret_cast<const uint4*>(gam)[2 * lane + 1];
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) r.gw[k] = gam[16 * lane + k];
+        }
+    }
+    // request_ok on the loaded values (an invalid request is recorded by the planner)
+    r.ok = r.pos >= 0 && r.rp >= 0 && r.rp < p.max_pos && r.pos + new_row_count(p) <= p.max_blocks * kPage;
+    r.page = 0;
+    if (!r.ok) return;
+    const float* cs = p.rope_cos + (int64_t)r.rp * kRope;
+    const float* sn = p.rope_sin + (int64_t)r.rp * kRope;
+    r.c0 = cs[lane]; r.c1 = cs[32 + lane]; r.s0 = sn[lane]; r.s1 = sn[32 + lane];
+    if (r.append) r.page = p.block_table[(int64_t)b * p.max_blocks + r.pos / kPage];
+}
+
+// One warp, after the wait: q_pe RoPE of request b, then (unless the call stores no
+// row) kv_post + the cache append at local row seq_lens[b].
+__device__ void request_rows(const MlaDecodeParams& p, __nv_bfloat16* qa, int b, int lane, const RowPre& r) {
+    if (!r.ok) return;
+    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(p.q) + (int64_t)b * p.q_stride;
+    __nv_bfloat162 xq[kHeads];
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) xq[h] = reinterpret_cast<const __nv_bfloat162*>(q + h * kQHead + kNope)[lane];
+    KvPostIn kin;
+    if (r.append) {
+        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.kv_a) + (int64_t)b * p.kv_a_stride;
+        kv_post_load(src, nullptr, lane, kin);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) kin.gw[k] = r.gw[k];
+    }
+
+    // q_pe of all 16 heads: lane j rotates pair j
+    __nv_bfloat16* qrow = qa + (int64_t)b * kQRows * kRow;
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) {
+        float lo, hi;
+        rope_pair_r(__low2float(xq[h]), __high2float(xq[h]), r.c0, r.s0, r.c1, r.s1, lo, hi);
+        qrow[h * kRow + kLora + lane] = __float2bfloat16_rn(lo);
+        qrow[h * kRow + kLora + 32 + lane] = __float2bfloat16_rn(hi);
+    }
+    if (!r.append) return;
+
+    __align__(16) __nv_bfloat16 outc[16];
+    float lo, hi;
+    kv_post_finish_r(kin, p.rms_eps, r.c0, r.s0, r.c1, r.s1, lane, outc, lo, hi);
+    if (r.page < 0 || r.page >= p.n_pages) {
+        if (lane == 0) record_error(err_sink(p), MLA_DEV_BAD_PAGE);
+        return;
+    }
+    kv_post_store(reinterpret_cast<__nv_bfloat16*>(p.kv_cache) + ((int64_t)r.page * kPage + r.pos % kPage) * kRow,
+                  outc, lo, hi, lane);
+}
+
 __global__ void __launch_bounds__(kK1Threads) k1_prologue(const MlaDecodeParams p,
                                                             const __grid_constant__ CUtensorMap tmap_wuk) {
     MLA_TL_SCOPE(0);

@@ -231,10 +231,8 @@ def emulate_exchange_step(runner: MlaDecodeAttention, q: torch.Tensor, kv_a: tor
     nothing waits on a kernel that runs at the same time. Returns every rank's R(out)."""
     world = len(caches)
     outs = [torch.empty(q.shape[0], 2048, dtype=torch.bfloat16, device=q.device) for _ in range(world)]
-    # the one-kernel step (MlaDecodeAttention(fused_step=True), one request) is its "attention" stage
-    stages = ("attention",) if runner.fused_step and q.shape[0] == 1 else ("prologue", "attention", "merge")
     for r in range(world):
-        for stage in stages:
+        for stage in ("prologue", "attention", "merge"):
             runner.attend(q, kv_a, caches[r], outs[r], stage, rope_pos=global_pos, new_row=(r == world - 1),
                           exchange=exchange[r])
     for r in range(world):

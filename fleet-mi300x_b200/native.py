@@ -24,7 +24,6 @@ FLAG_NO_NEW_ROW = 0x8
 FLAG_EXCHANGE_SPLIT = 0x10  # peer exchange as K3 + K4 even where the fused K3 applies
 FLAG_QC_HILO = 0x20  # q_c as a bf16 hi/lo pair in the score MMAs (default kernel)
 FLAG_P_HILO = 0x40   # probabilities as a bf16 hi/lo pair in P c_kv, row sums unrounded (default kernel)
-FLAG_FUSED_STEP = 0x80  # one-request step as one kernel (prologue, split-KV attention, merge)
 SHARD_STRIDE = 132
 MAX_PROJECT_BATCH = 64  # MLA_MAX_PROJECT_BATCH: weight-stream projection up to here, tcgen05 GEMM beyond
 STATIC_SCRATCH_BYTES = 32 << 20  # MLA_STATIC_SCRATCH_BYTES, the workspace of mla_decode_step_static

@@ -110,16 +110,6 @@ typedef enum {
                                   of the fp32 q_c instead of 8); the workspace grows by batch x 16 KB */
 #define MLA_FLAG_P_HILO 0x40   /* the probabilities of P c_kv as a bf16 hi/lo pair (two MMAs per step) and the row
                                   sums over the unrounded fp32 values, instead of bf16-rounded probabilities */
-/* One-request steps as a single kernel (batch 1, default precision, the default kernel;
- * mla_decode_step runs K0 / K4 / K5 around it as usual, mla_attention runs the one kernel
- * alone, mla_prologue and mla_merge_uv refuse the flag): the prologue (q_pe RoPE, the appended row, the q-absorb), the split-KV
- * attention and the merge + W_UV run in one launch whose CTAs are all resident at once,
- * ordered by counters in the first 256 bytes of the workspace (bounded waits). Those bytes
- * must be zero before the first call with this flag (allocate the workspace zero-filled);
- * every call leaves them zero. A peer exchange (world > 0) then runs K4 for the combine.
- * Refused (MLA_E_INVALID_ARG) for batch > 1, with the precision, check or tcgen05 flags,
- * and where fewer than 128 CTAs of the split-KV kernel fit on the device at once. */
-#define MLA_FLAG_FUSED_STEP 0x80
 
 typedef struct MlaDecodeParams {
     uint32_t struct_size; /* sizeof(MlaDecodeParams) */

@@ -48,16 +48,13 @@ def test_params_struct_layout(lib):
     assert p.abi_version == native.ABI_VERSION
 
 
-def expected_workspace(batch: int, ctas: int, fused: bool = False) -> int:
+def expected_workspace(batch: int, ctas: int) -> int:
     a = lambda x: (x + 255) // 256 * 256
-    off = 256  # the one-kernel step's counters
-    off = a(off + (batch + 1) * 4)
+    off = a((batch + 1) * 4)
     off = a(off + 16 + ctas * 32)  # the split plan: header (U, G) and one 32-byte entry per CTA
     off = a(off + batch * 16 * 576 * 2)
     off = a(off + (ctas + batch) * 16 * 2 * 4)
     off = a(off + (ctas + batch) * 16 * 512 * 4)
-    if fused:
-        off = a(off + 16 * 8 * 128 * 4)  # W_UV partial products per (head, 64 latent columns)
     return off
 
 

@@ -21,8 +21,7 @@ def _a256(x):
 
 
 def qkv_offset(batch, ctas):
-    off = 256  # the one-kernel step's counters come first
-    off = _a256(off + (batch + 1) * 4)
+    off = _a256((batch + 1) * 4)
     off = _a256(off + 16 + ctas * 32)  # the split plan: header and one 32-byte entry per CTA
     off = _a256(off + batch * 16 * 576 * 2)
     off = _a256(off + (ctas + batch) * 16 * 2 * 4)
