@@ -269,9 +269,9 @@ def _peer_worker(rank, world, port, T, q_out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_peer_exchange_gpus(world):
-    """One process per GPU (2, and 4 where the box has them), buffers mapped through IPC."""
+    """One process per GPU (2, and 4 or 8 where the box has them), buffers mapped through IPC."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
