@@ -151,8 +151,9 @@ def test_large_batch_merge_blocks(cuda_device, B):
 
 
 @pytest.mark.parametrize("lengths", [[18880], [40000], [9000, 20, 12000, 0, 3000, 64, 8000, 1],
+                                     [5000, 64, 1, 12000, 0, 700, 9000, 33, 2048, 65, 3000, 128],
                                      [127] * 40 + [30000] + [5] * 30],
-                         ids=["one-296-tiles", "one-626-tiles", "ragged-8", "ragged-71"])
+                         ids=["one-296-tiles", "one-626-tiles", "ragged-8", "ragged-12", "ragged-71"])
 def test_pair_merge(cuda_device, lengths):
     """Plans of at least 296 tiles with the default 296 plan CTAs: each split-KV CTA runs two
     adjacent plan CTAs and, where their boundary falls inside a request, merges the two
