@@ -442,26 +442,13 @@ __device__ __forceinline__ void dsmem_push2(uint32_t addr, float2 v, uint32_t re
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
                  ::"r"(addr), "f"(v.x), "f"(v.y), "r"(remote_bar) : "memory");
 }
-__device__ __forceinline__ void dsmem_push1(uint32_t addr, uint32_t v, uint32_t remote_bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
-                 ::"r"(addr), "r"(v), "r"(remote_bar) : "memory");
-}
 
 // ---------------------------------------------------------------------------
-// TMA: 2-D tiled load global -> shared, completion on an mbarrier. Never
-// with .multicast::cluster.
+// TMA: tiled loads global -> shared, completion on an mbarrier. Never with
+// .multicast::cluster.
 // ---------------------------------------------------------------------------
 constexpr uint64_t kCacheEvictFirst = 0x12F0000000000000ull;
 constexpr uint64_t kCacheEvictLast = 0x14F0000000000000ull;
-
-__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y,
-                                            uint64_t cache_hint) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(cache_hint)
-        : "memory");
-}
 
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y, int z,
                                             uint64_t cache_hint) {
