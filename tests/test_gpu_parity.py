@@ -134,11 +134,16 @@ def test_ragged_paged_batch(cuda_device, num_ctas, kernel):
         np.testing.assert_allclose(r, rows[b], rtol=1e-2, atol=1e-6)
 
 
-@pytest.mark.parametrize("B", [150, 200, 300])
+@pytest.mark.parametrize("B", [64, 65, 150, 200, 300, 1000])
 def test_large_batch_merge_blocks(cuda_device, B):
-    """Batches past one wave of 16-request K3 blocks (16 heads x ceil(B/16) > 148 SMs)
-    run K3 in 32-request blocks, two m16 tiles on one staged W_UV[h]; partial last
-    blocks (B = 150: 22 requests, B = 200: 8) leave whole tiles empty."""
+    """The batch thresholds of the plan and of K3's forms:
+    - 64: the largest batch whose split-KV kernel and K3 derive the plan themselves before
+      their waits; K3's cluster form in four 16-request blocks (256 CTAs, two waves);
+    - 65: the plan from K1's per-CTA entries; K3's plain form in 16-request blocks;
+    - 150-300: past one wave of 16-request blocks (16 heads x ceil(B/16) > 148 SMs), K3 runs
+      in 32-request blocks, two m16 tiles on one staged W_UV[h]; partial last blocks (B = 150:
+      22 requests, B = 200: 8) leave whole tiles empty;
+    - 1000: 512 K3 CTAs in several waves, about three requests per plan CTA."""
     rng = np.random.default_rng(B)
     lengths = [int(x) for x in rng.integers(0, 400, size=B)]
     d = ragged_batch(cuda_device, lengths)
