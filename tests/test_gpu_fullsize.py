@@ -113,6 +113,32 @@ def test_config5b_one_gpu(cuda_device):
     print(f"config5b: worst max rel {worst:.3e}")
 
 
+def test_one_request_of_524288_rows(cuda_device):
+    """The longest sequence in the suite: 524,288 cached rows (604 MB, four times config 5b) on
+    permuted pages, 8,193 tiles over the default 296 plan CTAs (about 28 per CTA, pair-merged),
+    K3's cluster form; the RoPE position and the appended row at 524,288."""
+    T = 524288
+    cfg = O.Config()
+    cos, sin = cfg.cos_sin(T + 8)
+    lw = workloads.make_layer_weights(9)
+    w = oracle_weights(lw)
+    dev = cuda_device
+    cache = fleet.PagedLatentCache.for_lengths([T], permute=True, zero=False,
+                                               generator=torch.Generator().manual_seed(9), device=dev)
+    workloads.fill_pool_random(cache.pages, 9)
+    x_n = workloads.make_hidden(10, 1).float().numpy()[0]
+    qn, kvn = O.project(cfg, w, x_n)
+    runner = fleet.MlaDecodeAttention(fleet.ModelConfig(), fleet.LayerWeights(
+        *(t.to(dev) for t in (lw.q_proj, lw.kv_a_proj_with_mqa, lw.kv_a_layernorm, lw.kv_b_proj))),
+        torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev))
+    out = runner.attend(torch.from_numpy(qn.reshape(1, -1)).to(BF).to(dev), torch.from_numpy(kvn[None]).to(BF).to(dev),
+                        cache)
+    runner.check_errors()
+    d = dict(cfg=cfg, w=w, cos=cos, sin=sin, cache=cache, q=qn.reshape(1, -1), kv_a=kvn[None], lengths=[T])
+    worst = _check_all_requests(d, out.float().cpu().numpy(), "524,288 rows")
+    print(f"524,288 rows: max rel {worst:.3e}")
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_config5b_sequence_sharded_emulated(cuda_device, world):
     """Config 5b split over `world` ranks by page-aligned KV ranges (distributed.
