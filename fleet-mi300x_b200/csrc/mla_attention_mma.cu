@@ -31,8 +31,9 @@
 //             16 latent tiles), accumulated in registers (rescale = multiply).
 // Loads: the group's leader thread issues half page j+2 into the slot of half
 // page j as soon as all four warps have released it (mbarrier, bounded wait).
-// A page whose valid tokens fit in its first half is loaded and computed as
-// that half only.
+// The split plan's tiles are these half pages (plan_unit_rows), so a request's
+// rows split between plan CTAs at 32-row granularity and a request with up to
+// 32 rows in its last page loads only that half.
 // Start: batches of up to 64 requests derive the split plan from the step's
 // inputs before the wait on K1 and request their first half page early (except
 // one holding the row K1 appends); larger batches read K1's per-CTA plan entry.
@@ -148,23 +149,22 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
 
     // The leader's look-ahead over half pages (loads run two half pages ahead).
     TileCursor la{};
-    int la_half = 0;
     uint32_t issued = 0;
     auto issue_next = [&]() {
-        int page = p.block_table[(int64_t)la.b * p.max_blocks + la.page_index()];
+        const int h = la.index();  // half page h of the request: page h / 2, rows 32 (h % 2) ..
+        int page = p.block_table[(int64_t)la.b * p.max_blocks + (h >> 1)];
         if (page < 0 || page >= p.n_pages) { record_error(err_sink(p), MLA_DEV_BAD_PAGE); page = 0; }
         const uint32_t slot = issued % kNSlot;
         mbar_arrive_expect_tx(&S.full[slot], kTileBytes);
-        tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.full[slot], 0, kHalf * la_half, 0, page,
+        tma_load_4d(tile_s + slot * kTileBytes, &tmap_kv, &S.full[slot], 0, kHalf * (h & 1), 0, page,
                     kCacheEvictFirst);
         ++issued;
-        if (la_half == 0 && la.tokens() > kHalf) la_half = 1;
-        else { la_half = 0; la.next(); }
+        la.next();
     };
     // Would the half page the leader loads next hold the row K1 appends in this step?
     auto holds_new_row = [&]() -> bool {
         if (!new_row_count(p)) return false;
-        const int row0 = la.page_index() * kPage + kHalf * la_half, nr = p.seq_lens[la.b];
+        const int row0 = kHalf * la.index(), nr = p.seq_lens[la.b];
         return nr >= row0 && nr < row0 + kHalf;
     };
     auto init_group = [&]() {
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
         for (; ok && cur.valid(); cur.next()) {
             const bool first = cur.first(), last = cur.last();
             if (first) rows_b = p.seq_lens[cur.b] + new_row_count(p);
-            const int valid = min(kPage, rows_b - cur.page_index() * kPage);
+            const int hvalid = min(kHalf, rows_b - kHalf * cur.index());  // valid tokens of this half page
             if (first) {
                 const __nv_bfloat16* qrow = qa + (int64_t)cur.b * kQRows * kRow + 144 * w + 2 * t4;
 #pragma unroll
@@ -313,10 +313,8 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 m_run[0] = m_run[1] = -INFINITY;
                 l_run[0] = l_run[1] = 0.f;
             }
-            const int halves = valid > kHalf ? 2 : 1;
-            for (int hh = 0; hh < halves; ++hh, ++i) {
-                const int hvalid = min(kHalf, valid - kHalf * hh);  // valid tokens of this half page
-                const bool tile_first = first && hh == 0;
+            {
+                const bool tile_first = first;
                 const uint32_t slot = i % kNSlot;
                 if (!mbar_wait(&S.full[slot], (i / kNSlot) & 1, abort, err_sink(p))) { ok = false; break; }
                 if (i == 0 && w == 0) MLA_TL_MARK(1, 5);  // first half page landed
@@ -466,8 +464,8 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                     if (refill_ok) issue_next();
                 }
                 if (!__shfl_sync(0xffffffffu, refill_ok, 0)) { ok = false; break; }  // reconverges the warp
+                ++i;
             }
-            if (!ok) break;
 
             if (last) {
                 // ---- partial of (request, this virtual CTA): m, l, unnormalised O ----

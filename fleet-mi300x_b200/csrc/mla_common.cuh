@@ -32,7 +32,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // ---------------------------------------------------------------------------
 // Workspace layout (bytes, each region 256-byte aligned).
-//   tiles_cum  int32 [batch + 1]          prefix sum of 64-token tiles per request (split plan)
+//   tiles_cum  int32 [batch + 1]          prefix sum of plan tiles per request (plan_unit_rows)
 //   plan       PlanHeader, PlanEntry [num_ctas]   the split plan per CTA, ready to use (K1 writes it)
 //   qa         bf16  [batch][16][576]     absorbed query q_c (512) | roped q_pe (64), per head
 //   part_ml    f32   [slots][16][2]       split partial: running max (log2 domain), sum of exps
@@ -161,10 +161,17 @@ __device__ __forceinline__ bool request_ok(const MlaDecodeParams& p, int b) {
     return rows >= 0 && rp >= 0 && rp < p.max_pos && rows + new_row_count(p) <= p.max_blocks * kPage;
 }
 
-// 64-token tiles request b attends in the split plan: 0 for an invalid request
-// (K1's planner records it), so that no kernel reads outside the block table.
+// Rows per tile of the split plan: the default split-KV kernel walks 32-row half
+// pages (its TMA box), the CUDA-core and tensor-memory kernels whole 64-row pages.
+__host__ __device__ inline int plan_unit_rows(const MlaDecodeParams& p) {
+    return (p.flags & (MLA_FLAG_CHECK_KERNEL | MLA_FLAG_TCGEN05)) ? kPage : kPage / 2;
+}
+
+// Tiles request b attends in the split plan: 0 for an invalid request (K1's
+// planner records it), so that no kernel reads outside the block table.
 __device__ __forceinline__ int plan_tiles(const MlaDecodeParams& p, int b) {
-    return request_ok(p, b) ? (p.seq_lens[b] + new_row_count(p) + kPage - 1) / kPage : 0;
+    const int unit = plan_unit_rows(p);
+    return request_ok(p, b) ? (p.seq_lens[b] + new_row_count(p) + unit - 1) / unit : 0;
 }
 
 // ---------------------------------------------------------------------------

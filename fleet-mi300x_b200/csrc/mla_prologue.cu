@@ -12,7 +12,8 @@
 //    and W_UK are bf16 already, so the products are exact; q_c is stored bf16 as
 //    an operand of the attention kernel's score contraction (with
 //    MLA_FLAG_QC_HILO also its remainder, as a second bf16 operand);
-//  * the split plan: prefix sum of 64-token tiles per request, consumed by K2/K3.
+//  * the split plan: prefix sum of tiles per request (plan_unit_rows: 32-row half
+//    pages for the default split-KV kernel, 64-row pages for the others), consumed by K2/K3.
 //
 // One 1-D grid with two kinds of CTA:
 //   [0, n_absorb)  absorb: (request block of 64, head, quarter of the latent

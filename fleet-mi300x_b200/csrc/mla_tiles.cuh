@@ -34,7 +34,8 @@ struct TileCursor {
         b = e.b; cb0 = e.cb0; cb1 = e.cb1;
     }
     __device__ bool valid() const { return u < u_end; }
-    __device__ int page_index() const { return (int)(u - cb0); }
+    __device__ int index() const { return (int)(u - cb0); }       // tile of the current request
+    __device__ int page_index() const { return (int)(u - cb0); }  // the same, for 64-row tiles
     __device__ int tokens() const {  // valid tokens in this 64-token tile
         const int L = seq_lens[b] + extra;
         return min(kPage, L - page_index() * kPage);

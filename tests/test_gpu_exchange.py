@@ -64,7 +64,7 @@ def _inputs(B, dev, seed):
 @pytest.mark.parametrize("lengths,world", [([5000], 3), ([130], 4), ([64], 2), ([4095], 8), ([300] * 5, 2),
                                            ([37 * i + 5 for i in range(70)], 3),
                                            ([411 * i + 7 for i in range(13)], 2),  # K3 in two blocks of 8
-                                           ([40000], 2)])  # shards of 313 tiles: pair-merged partials
+                                           ([40000], 2)])  # shards of 626 half-page tiles: pair-merged partials
 def test_emulated_exchange_equals_gathered_combine(cuda_device, lengths, world):
     runner, *_ = _runner(cuda_device, max_pos=max(8192, max(lengths) + 8))
     B = len(lengths)

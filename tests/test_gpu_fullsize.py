@@ -75,7 +75,8 @@ def _check_all_requests(d, got, what):
 
 def test_config5a_every_request_eager_and_graph(cuda_device):
     """The timed configuration: 256 x 4,096 with the default plan (296 plan CTAs, every CTA
-    pair-merged, 552 -> 404 partials per head for K3) and K3's 32-request blocks (B > 144).
+    pair-merged: 33,024 half-page tiles, 544 -> 400 partials per head for K3) and K3's
+    32-request blocks (B > 144).
     The bench replays the step as a CUDA graph; the graph's output must equal the eager
     call's bit for bit, and both must match the oracle on all 256 requests."""
     d = _bench_inputs("config5a", cuda_device)
@@ -94,8 +95,8 @@ def test_config5a_every_request_eager_and_graph(cuda_device):
 
 @pytest.mark.parametrize("name", ["config4", "config3"])
 def test_every_request_vs_oracle(cuda_device, name):
-    """Config 4 (8 x 32,768: ~1,024 tiles over 296 plan CTAs, pair-merged, ~39 partials per
-    request) and config 3 (32 ragged requests, permuted pages): every request."""
+    """Config 4 (8 x 32,768: 8,200 half-page tiles over 296 plan CTAs, pair-merged, 19
+    partials per request) and config 3 (32 ragged requests, permuted pages): every request."""
     d = _bench_inputs(name, cuda_device)
     out = d["runner"].attend(d["q_t"], d["kv_a_t"], d["cache"])
     d["runner"].check_errors()
@@ -104,7 +105,7 @@ def test_every_request_vs_oracle(cuda_device, name):
 
 
 def test_config5b_one_gpu(cuda_device):
-    """One sequence of 131,072 cached rows on one GPU: 2,049 tiles over 296 plan CTAs, 148
+    """One sequence of 131,072 cached rows on one GPU: 4,097 half-page tiles over 296 plan CTAs, 148
     pair-merged partials per head, K3's 4-CTA cluster form."""
     d = _bench_inputs("config5b", cuda_device)
     out = d["runner"].attend(d["q_t"], d["kv_a_t"], d["cache"])
@@ -115,7 +116,8 @@ def test_config5b_one_gpu(cuda_device):
 
 def test_one_request_of_524288_rows(cuda_device):
     """The longest sequence in the suite: 524,288 cached rows (604 MB, four times config 5b) on
-    permuted pages, 8,193 tiles over the default 296 plan CTAs (about 28 per CTA, pair-merged),
+    permuted pages, 16,385 half-page tiles over the default 296 plan CTAs (about 55 per CTA,
+    pair-merged),
     K3's cluster form; the RoPE position and the appended row at 524,288."""
     T = 524288
     cfg = O.Config()

@@ -155,14 +155,14 @@ def test_large_batch_merge_blocks(cuda_device, B):
         assert_close(got[b], want[b], f"request {b} of {B} (T={lengths[b]})")
 
 
-@pytest.mark.parametrize("lengths", [[18880], [40000], [9000, 20, 12000, 0, 3000, 64, 8000, 1],
+@pytest.mark.parametrize("lengths", [[9440], [40000], [9000, 20, 12000, 0, 3000, 64, 8000, 1],
                                      [5000, 64, 1, 12000, 0, 700, 9000, 33, 2048, 65, 3000, 128],
                                      [127] * 40 + [30000] + [5] * 30],
-                         ids=["one-296-tiles", "one-626-tiles", "ragged-8", "ragged-12", "ragged-71"])
+                         ids=["one-296-tiles", "one-1251-tiles", "ragged-8", "ragged-12", "ragged-71"])
 def test_pair_merge(cuda_device, lengths):
-    """Plans of at least 296 tiles with the default 296 plan CTAs: each split-KV CTA runs two
-    adjacent plan CTAs and, where their boundary falls inside a request, merges the two
-    partials of that request in shared memory before K3 (k2_pairs). One request of exactly
+    """Plans of at least 296 tiles (32-row half pages) with the default 296 plan CTAs: each
+    split-KV CTA runs two adjacent plan CTAs and, where their boundary falls inside a request,
+    merges the two partials of that request in shared memory before K3 (k2_pairs). One request of exactly
     296 tiles (the last holding only the new row) merges at every CTA; ragged batches merge
     at some boundaries and not at others (empty requests, requests inside one plan CTA).
     Checked against the oracle, against plans that do not pair (148 CTAs, the check kernel),

@@ -2,7 +2,8 @@
 
 The plan (fleet-mi300x_b200/csrc/mla_common.cuh: plan_begin / plan_cta_of, the cursor in
 mla_attention.cu, the partial lookup in mla_merge.cu) is restated here in Python and
-checked for exact coverage: every 64-token tile is owned by exactly one CTA, every
+checked for exact coverage: every tile (UNIT rows: the default split-KV kernel's 32-row
+half pages) is owned by exactly one CTA, every
 (CTA, request) segment gets its own partial slot c + b, and the merge finds exactly
 the CTAs that wrote a request's partials.
 """
@@ -16,6 +17,14 @@ fleet = importlib.import_module("fleet-mi300x_b200")
 workloads = importlib.import_module("fleet-mi300x_b200.workloads")
 
 
+UNIT = 32  # mla_common.cuh:plan_unit_rows for the default split-KV kernel
+
+
+def tiles_of(seq_lens, unit=UNIT):
+    """plan_tiles: the cached rows plus the new one, in tiles of `unit` rows."""
+    return [(t + 1 + unit - 1) // unit for t in seq_lens]
+
+
 def plan_begin(c, U, G):
     return c * U // G
 
@@ -25,7 +34,7 @@ def plan_cta_of(u, U, G):
 
 
 def simulate(seq_lens, num_ctas):
-    tiles = [(t + 1 + 63) // 64 for t in seq_lens]
+    tiles = tiles_of(seq_lens)
     cum = [0]
     for n in tiles:
         cum.append(cum[-1] + n)
@@ -57,7 +66,7 @@ def simulate(seq_lens, num_ctas):
 
 @pytest.mark.parametrize("num_ctas", [1, 2, 3, 7, 148, 296, 4096])
 def test_plan_edge_lengths(num_ctas):
-    simulate([0, 1, 62, 63, 64, 65, 127, 128, 129, 200, 1000, 1023, 4095], num_ctas)
+    simulate([0, 1, 30, 31, 32, 33, 62, 63, 64, 65, 127, 128, 129, 200, 1000, 1023, 4095], num_ctas)
 
 
 def test_plan_random():
@@ -71,9 +80,10 @@ def test_plan_random():
 def test_plan_baseline_configs():
     for name in ("config1", "config3", "config4"):
         simulate(workloads.WORKLOADS[name].seq_lens(), 148)
-    # config 5a: 256 x 4097 rows -> 65 tiles each over 148 CTAs
+    # config 5a: 256 x 4097 rows -> 129 half-page tiles each over 148 CTAs
     G, seg = simulate([4096] * 256, 148)
     assert G == 148 and len(seg) <= 148 + 256
+    assert tiles_of([4096]) == [129] and tiles_of([4096], 64) == [65]
 
 
 def k2_grid(num_ctas, sm_count):
@@ -92,7 +102,7 @@ def paired_slots(seq_lens, num_ctas):
     where their boundary falls inside a request, 2k + 1's first segment is merged into
     2k's last one. Returns, per request, the slots written, in tile order."""
     G, segments = simulate(seq_lens, num_ctas)
-    tiles = [(t + 1 + 63) // 64 for t in seq_lens]
+    tiles = tiles_of(seq_lens)
     cum = [0]
     for n in tiles:
         cum.append(cum[-1] + n)
@@ -119,10 +129,10 @@ def part_idx(c0, c1, paired):
 
 
 @pytest.mark.parametrize("T,num_ctas,sms,expect", [
-    (131071, 296, 148, True), (65535, 296, 148, True), (18880, 296, 148, True),  # 296 tiles: G = num_ctas
-    (18879, 296, 148, False),  # 295 tiles: G < num_ctas
+    (131071, 296, 148, True), (65535, 296, 148, True), (9440, 296, 148, True),  # 296 tiles: G = num_ctas
+    (9439, 296, 148, False),  # 295 tiles: G < num_ctas
     (1023, 296, 148, False), (131071, 148, 148, False), (131071, 200, 148, False), (131071, 400, 148, True),
-    (9000, 296, 148, False)])
+    (9000, 296, 148, False), (18880, 296, 148, True)])
 def test_pair_merge_single_request(T, num_ctas, sms, expect):
     """One request: every boundary between 2k and 2k + 1 is inside it, so the slots are 0, 2, 4, ..."""
     G, cum, written = paired_slots([T], num_ctas)
