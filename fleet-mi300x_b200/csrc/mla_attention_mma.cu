@@ -279,35 +279,41 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 *reinterpret_cast<float2*>(acc + (g + 8) * kLora + 8 * n) = make_float2(o[n][2], o[n][3]);
             }
         };
-        for (; ok && cur.valid(); cur.next()) {
-            const bool first = cur.first(), last = cur.last();
-            if (first) rows_b = p.seq_lens[cur.b] + new_row_count(p);
-            const int hvalid = min(kHalf, rows_b - kHalf * cur.index());  // valid tokens of this half page
-            if (first) {
-                const __nv_bfloat16* qrow = qa + (int64_t)cur.b * kQRows * kRow + 144 * w + 2 * t4;
+        // Row count and Q fragments of request b (the first half page of each segment needs them).
+        auto load_query = [&](int b) {
+            rows_b = p.seq_lens[b] + new_row_count(p);
+            const __nv_bfloat16* qrow = qa + (int64_t)b * kQRows * kRow + 144 * w + 2 * t4;
+#pragma unroll
+            for (int j = 0; j < 9; ++j) {
+                const __nv_bfloat16* q0 = qrow + 16 * j;
+                qf[j][0] = *reinterpret_cast<const uint32_t*>(q0 + g * kRow);
+                qf[j][1] = *reinterpret_cast<const uint32_t*>(q0 + (g + 8) * kRow);
+                qf[j][2] = *reinterpret_cast<const uint32_t*>(q0 + g * kRow + 8);
+                qf[j][3] = *reinterpret_cast<const uint32_t*>(q0 + (g + 8) * kRow + 8);
+            }
+            if constexpr (kQLo) {
+                const __nv_bfloat16* lrow = qa_lo + (int64_t)b * kQRows * kLora + 144 * w + 2 * t4;
 #pragma unroll
                 for (int j = 0; j < 9; ++j) {
-                    const __nv_bfloat16* q0 = qrow + 16 * j;
-                    qf[j][0] = *reinterpret_cast<const uint32_t*>(q0 + g * kRow);
-                    qf[j][1] = *reinterpret_cast<const uint32_t*>(q0 + (g + 8) * kRow);
-                    qf[j][2] = *reinterpret_cast<const uint32_t*>(q0 + g * kRow + 8);
-                    qf[j][3] = *reinterpret_cast<const uint32_t*>(q0 + (g + 8) * kRow + 8);
-                }
-                if constexpr (kQLo) {
-                    const __nv_bfloat16* lrow = qa_lo + (int64_t)cur.b * kQRows * kLora + 144 * w + 2 * t4;
-#pragma unroll
-                    for (int j = 0; j < 9; ++j) {
-                        if (144 * w + 16 * j < kLora) {
-                            const __nv_bfloat16* l0 = lrow + 16 * j;
-                            ql[j][0] = *reinterpret_cast<const uint32_t*>(l0 + g * kLora);
-                            ql[j][1] = *reinterpret_cast<const uint32_t*>(l0 + (g + 8) * kLora);
-                            ql[j][2] = *reinterpret_cast<const uint32_t*>(l0 + g * kLora + 8);
-                            ql[j][3] = *reinterpret_cast<const uint32_t*>(l0 + (g + 8) * kLora + 8);
-                        } else {
-                            ql[j][0] = ql[j][1] = ql[j][2] = ql[j][3] = 0u;
-                        }
+                    if (144 * w + 16 * j < kLora) {
+                        const __nv_bfloat16* l0 = lrow + 16 * j;
+                        ql[j][0] = *reinterpret_cast<const uint32_t*>(l0 + g * kLora);
+                        ql[j][1] = *reinterpret_cast<const uint32_t*>(l0 + (g + 8) * kLora);
+                        ql[j][2] = *reinterpret_cast<const uint32_t*>(l0 + g * kLora + 8);
+                        ql[j][3] = *reinterpret_cast<const uint32_t*>(l0 + (g + 8) * kLora + 8);
+                    } else {
+                        ql[j][0] = ql[j][1] = ql[j][2] = ql[j][3] = 0u;
                     }
                 }
+            }
+        };
+        bool q_next = false;  // this segment's query was requested in the previous segment's epilogue
+        for (; ok && cur.valid(); cur.next()) {
+            const bool first = cur.first(), last = cur.last();
+            if (first && !q_next) load_query(cur.b);
+            q_next = false;
+            const int hvalid = min(kHalf, rows_b - kHalf * cur.index());  // valid tokens of this half page
+            if (first) {
 #pragma unroll
                 for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
                 m_run[0] = m_run[1] = -INFINITY;
@@ -468,6 +474,14 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
             }
 
             if (last) {
+                // The next segment's row count and query, requested now (the fragments are dead
+                // after this half page's score MMAs) so that their latency overlaps this epilogue.
+                if (cur.u + 1 < cur.u_end) {
+                    TileCursor nx = cur;
+                    nx.next();
+                    load_query(nx.b);
+                    q_next = true;
+                }
                 // ---- partial of (request, this virtual CTA): m, l, unnormalised O ----
                 float l0 = l_run[0], l1 = l_run[1];
                 l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
