@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 // the leader refills this slot with the half page two ahead once all four warps released it
                 bool refill_ok = true;
                 if (leader && la.valid()) {
-                    refill_ok = mbar_wait_idle(&S.empty[slot], (i / kNSlot) & 1, abort, err_sink(p));
+                    refill_ok = mbar_wait(&S.empty[slot], (i / kNSlot) & 1, abort, err_sink(p));
                     if (refill_ok) issue_next();
                 }
                 if (!__shfl_sync(0xffffffffu, refill_ok, 0)) { ok = false; break; }  // reconverges the warp

@@ -260,20 +260,6 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// try_wait with a suspend-time hint: the thread sleeps until the phase completes
-// or about `hint_ns` pass, instead of returning after a system-dependent time.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-        : "memory");
-    return ok != 0;
-}
-
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -363,25 +349,6 @@ __device__ __forceinline__ float line_hi(const ulonglong2& v) { return __uint_as
 // MLA_DEV_TIMEOUT, raises *abort and returns false. The limit is per wait: a
 // healthy pipeline completes each phase in microseconds.
 constexpr uint64_t kWaitLimitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s
-
-// The same bounded wait for a thread that has nothing else to do (a TMA
-// producer waiting for a slot): each probe sleeps up to 20 us, so the waiting
-// thread takes no issue slots from the compute warps on its scheduler.
-__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               const ErrSink& err) {
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-        if ((i & 7) == 0) {
-            if (*abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                record_error(err, MLA_DEV_TIMEOUT);
-                *abort = 1;
-                return false;
-            }
-        }
-    }
-}
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           const ErrSink& err) {
