@@ -377,10 +377,42 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                     s[2] = col < hvalid ? hi.x * scale_log2 : -INFINITY;
                     s[3] = col + 1 < hvalid ? hi.y * scale_log2 : -INFINITY;
                 }
+                // ---- probabilities (bf16) for this warp's 8 tokens -> P buffer ----
+                uint8_t* pb = p_s + (i & 1) * kPBytes;
+                float lsum0 = 0.f, lsum1 = 0.f;  // this thread's row-sum terms, heads g, g+8
+                auto write_p = [&]() {
+                    if constexpr (kPLo) {
+                        const float e0 = fast_exp2(s[0] - m_run[0]), e1 = fast_exp2(s[1] - m_run[0]);
+                        const float e2 = fast_exp2(s[2] - m_run[1]), e3 = fast_exp2(s[3] - m_run[1]);
+                        const float h0 = bf16_round(e0), h1 = bf16_round(e1), h2 = bf16_round(e2),
+                                    h3 = bf16_round(e3);
+                        lsum0 = e0 + e1;
+                        lsum1 = e2 + e3;
+                        uint8_t* pl = plo_s + (i & 1) * kPBytes;
+                        *reinterpret_cast<uint32_t*>(pb + p_offset(g, w) + 4 * t4) = pack_bf16(h0, h1);
+                        *reinterpret_cast<uint32_t*>(pb + p_offset(g + 8, w) + 4 * t4) = pack_bf16(h2, h3);
+                        *reinterpret_cast<uint32_t*>(pl + p_offset(g, w) + 4 * t4) = pack_bf16(e0 - h0, e1 - h1);
+                        *reinterpret_cast<uint32_t*>(pl + p_offset(g + 8, w) + 4 * t4) = pack_bf16(e2 - h2, e3 - h3);
+                    } else {
+                        const float e0 = bf16_round(fast_exp2(s[0] - m_run[0]));
+                        const float e1 = bf16_round(fast_exp2(s[1] - m_run[0]));
+                        const float e2 = bf16_round(fast_exp2(s[2] - m_run[1]));
+                        const float e3 = bf16_round(fast_exp2(s[3] - m_run[1]));
+                        lsum0 = e0 + e1;
+                        lsum1 = e2 + e3;
+                        *reinterpret_cast<uint32_t*>(pb + p_offset(g, w) + 4 * t4) = pack_bf16(e0, e1);
+                        *reinterpret_cast<uint32_t*>(pb + p_offset(g + 8, w) + 4 * t4) = pack_bf16(e2, e3);
+                    }
+                };
                 // ---- running max (log2 domain), lazy rescale ----
+                // Past a segment's first half page the probabilities are written with the running
+                // max first; one barrier with an OR-reduction then both publishes them and says
+                // whether any score exceeded the max by more than 2^8. Only then (rare) the group
+                // exchanges the tile maxima, rescales, and writes them again behind one more barrier.
                 bool exchange = tile_first;
                 if (!tile_first) {
                     const bool ex = fmaxf(s[0], s[1]) > m_run[0] + 8.f || fmaxf(s[2], s[3]) > m_run[1] + 8.f;
+                    write_p();
                     exchange = bar_red_or(bar_id, kGroupWarps * 32, ex);
                 }
                 if (exchange) {
@@ -404,31 +436,11 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                     }
                     m_run[0] = n0;
                     m_run[1] = n1;
+                    write_p();
+                    named_bar_sync(bar_id, kGroupWarps * 32);
                 }
-                // ---- probabilities (bf16) for this warp's 8 tokens -> P buffer ----
-                uint8_t* pb = p_s + (i & 1) * kPBytes;
-                if constexpr (kPLo) {
-                    const float e0 = fast_exp2(s[0] - m_run[0]), e1 = fast_exp2(s[1] - m_run[0]);
-                    const float e2 = fast_exp2(s[2] - m_run[1]), e3 = fast_exp2(s[3] - m_run[1]);
-                    const float h0 = bf16_round(e0), h1 = bf16_round(e1), h2 = bf16_round(e2), h3 = bf16_round(e3);
-                    l_run[0] += e0 + e1;
-                    l_run[1] += e2 + e3;
-                    uint8_t* pl = plo_s + (i & 1) * kPBytes;
-                    *reinterpret_cast<uint32_t*>(pb + p_offset(g, w) + 4 * t4) = pack_bf16(h0, h1);
-                    *reinterpret_cast<uint32_t*>(pb + p_offset(g + 8, w) + 4 * t4) = pack_bf16(h2, h3);
-                    *reinterpret_cast<uint32_t*>(pl + p_offset(g, w) + 4 * t4) = pack_bf16(e0 - h0, e1 - h1);
-                    *reinterpret_cast<uint32_t*>(pl + p_offset(g + 8, w) + 4 * t4) = pack_bf16(e2 - h2, e3 - h3);
-                } else {
-                    const float e0 = bf16_round(fast_exp2(s[0] - m_run[0]));
-                    const float e1 = bf16_round(fast_exp2(s[1] - m_run[0]));
-                    const float e2 = bf16_round(fast_exp2(s[2] - m_run[1]));
-                    const float e3 = bf16_round(fast_exp2(s[3] - m_run[1]));
-                    l_run[0] += e0 + e1;
-                    l_run[1] += e2 + e3;
-                    *reinterpret_cast<uint32_t*>(pb + p_offset(g, w) + 4 * t4) = pack_bf16(e0, e1);
-                    *reinterpret_cast<uint32_t*>(pb + p_offset(g + 8, w) + 4 * t4) = pack_bf16(e2, e3);
-                }
-                named_bar_sync(bar_id, kGroupWarps * 32);
+                l_run[0] += lsum0;
+                l_run[1] += lsum1;
 
                 // ---- O_w += P C[:, 128w : 128w+128] ----
                 const uint32_t pbase = p_addr + (i & 1) * kPBytes;
