@@ -139,7 +139,8 @@ typedef struct MlaDecodeParams {
     void* workspace;          /* device scratch, >= mla_workspace_size() bytes, 256-byte aligned */
     uint64_t workspace_bytes;
     int32_t* error_word;      /* optional device int32 (0 = no error); may be NULL */
-    int32_t num_ctas;         /* CTAs of the split-KV kernel; 0 = one per SM */
+    int32_t num_ctas;         /* CTAs of the split plan; 0 = the default: two per SM (the default
+                                 kernel runs two plan CTAs per CTA), one per SM with MLA_FLAG_TCGEN05 */
     int32_t flags;            /* MLA_FLAG_* */
 
     /* Sequence-sharded decode (one long sequence split over GPUs by KV range). */
