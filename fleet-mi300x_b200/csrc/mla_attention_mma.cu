@@ -25,12 +25,16 @@
 //   exchange  the 4 partial S through shared memory; warp w sums the 8 tokens
 //             [8w, 8w+8) and runs the softmax on them;
 //   softmax   lazy rescale: the running max per head is kept unless a score
-//             exceeds it by more than 2^8 (one barrier-reduction decides),
-//             probabilities rounded to bf16 and shared through shared memory;
+//             exceeds it by more than 2^8; probabilities are rounded to bf16 and
+//             written with the running max, and one barrier-reduction both
+//             publishes them and decides whether to rescale and write them again;
 //   output    O_w[16 x 128] += P[16 x 32] C[:, 128w : 128w+128] (2 k-steps x
 //             16 latent tiles), accumulated in registers (rescale = multiply).
 // Loads: the group's leader thread issues half page j+2 into the slot of half
 // page j as soon as all four warps have released it (mbarrier, bounded wait).
+// Segment ends: the last half page of a request's segment requests the next
+// segment's query fragments before writing its partial, so that their latency
+// overlaps the partial's stores.
 // The split plan's tiles are these half pages (plan_unit_rows), so a request's
 // rows split between plan CTAs at 32-row granularity and a request with up to
 // 32 rows in its last page loads only that half.
