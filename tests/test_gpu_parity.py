@@ -113,13 +113,14 @@ def run_gpu(d, dev, num_ctas=0, check_kernel=False, kernel="mma"):
     return out.float().cpu().numpy()
 
 
-EDGE_LENGTHS = [0, 1, 62, 63, 64, 65, 127, 128, 129, 200, 1000, 1023, 4095]
+# around the 64-row pages and the 32-row half pages (the default kernel's plan tiles)
+EDGE_LENGTHS = [0, 1, 30, 31, 32, 33, 62, 63, 64, 65, 95, 96, 97, 127, 128, 129, 200, 1000, 1023, 4095]
 
 
 @pytest.mark.parametrize("kernel", ["mma", "tcgen05"])
 @pytest.mark.parametrize("num_ctas", [0, 1, 3, 7, 64, 500])
 def test_ragged_paged_batch(cuda_device, num_ctas, kernel):
-    """Edge lengths around page boundaries (0 cached rows = only the new token), a
+    """Edge lengths around page and half-page boundaries (0 cached rows = only the new token), a
     permuted block table, and split plans from 1 CTA to more CTAs than tiles."""
     d = ragged_batch(cuda_device, EDGE_LENGTHS)
     pages_np = d["cache"].pages.float().cpu().numpy()
@@ -247,6 +248,35 @@ def test_device_errors_are_reported(cuda_device):
     # the context stays usable
     d3 = ragged_batch(cuda_device, [100])
     run_gpu(d3, cuda_device)
+
+
+@pytest.mark.parametrize("num_ctas", [0, 3, 7])
+def test_requests_without_tiles_between_segments(cuda_device, num_ctas):
+    """Requests whose position lies outside the RoPE table get no tiles in the split plan
+    (zero output, MLA_DEV_BAD_POSITION). A warp group whose range runs from the request
+    before such a request to the one after it skips it when it requests the next segment's
+    query and row count ahead of time; the valid requests still match the oracle."""
+    lengths = [3000, 100, 5000, 64, 2000]
+    d = ragged_batch(cuda_device, lengths)
+    pages_np = d["cache"].pages.float().cpu().numpy()
+    bt = d["cache"].block_table.cpu().numpy()
+    want, _ = oracle_paged(bt, pages_np, d, requests=[0, 2, 4], fast=True)
+    for b in (1, 3):
+        d["cache"].seq_lens[b] = d["cos"].shape[0] + 10
+    runner = fleet.MlaDecodeAttention(fleet.ModelConfig(), to_dev(d["lw"], cuda_device),
+                                      torch.from_numpy(d["cos"]).to(cuda_device),
+                                      torch.from_numpy(d["sin"]).to(cuda_device), num_ctas=num_ctas)
+    q = torch.from_numpy(d["q"]).to(BF).to(cuda_device)
+    kv_a = torch.from_numpy(d["kv_a"]).to(BF).to(cuda_device)
+    out = runner.attend(q, kv_a, d["cache"])
+    with pytest.raises(fleet.MlaError) as e:
+        runner.check_errors()
+    assert e.value.code == 2
+    got = out.float().cpu().numpy()
+    for b in (1, 3):
+        assert np.count_nonzero(got[b]) == 0
+    for b in (0, 2, 4):
+        assert_close(got[b], want[b], f"request {b} (T={lengths[b]}, ctas={num_ctas})")
 
 
 @pytest.mark.parametrize("cfg_name,subset", [("config3", [0, 13, 31]), ("config4", [2])])
