@@ -419,7 +419,7 @@ __device__ __forceinline__ void dsmem_push2(uint32_t addr, float2 v, uint32_t re
 
 // ---------------------------------------------------------------------------
 // TMA: tiled loads global -> shared, completion on an mbarrier. Never with
-// .multicast::cluster.
+// cluster multicast.
 // ---------------------------------------------------------------------------
 constexpr uint64_t kCacheEvictFirst = 0x12F0000000000000ull;
 constexpr uint64_t kCacheEvictLast = 0x14F0000000000000ull;
