@@ -65,9 +65,12 @@ constexpr int kHalf = kPage / 2;                      // tokens per half page
 constexpr int kNSlot = 2;                             // half-page ring per group
 constexpr int kChunkBytes = kHalf * 128;              // [32 tokens][64 columns] bf16
 constexpr int kTileBytes = 9 * kChunkBytes;           // 36,864
-constexpr int kSPitch = 40;                           // floats per head row of a partial-score block
+constexpr int kSRow = 20;                             // 16-byte cells per row of a partial-score block: 16
+                                                      // column pairs + 4 of padding (a quarter-warp's 16-byte
+                                                      // accesses fall in distinct banks)
                                                       // (64-bit accesses by a half-warp hit 32 banks)
-constexpr int kSPartBytes = kGroupWarps * kHeads * kSPitch * 4;  // 10,240
+constexpr int kSPartBytes = kGroupWarps * 8 * kSRow * 16;  // 10,240: [warp][g][column pair] float4 cells
+                                                           // {head g: cols 2c, 2c+1; head g+8: cols 2c, 2c+1}
 constexpr int kPBytes = kHeads * 64;                  // [16 heads][32 tokens] bf16, 64-byte rows, swizzled
 constexpr int kPrePlan = 64;                          // batches up to this plan before the K1 wait (larger
                                                       // batches fill the SMs with K1, so K2 becomes resident
@@ -355,14 +358,10 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                 }
                 // ---- exchange: every warp publishes its partials, then sums its 8 tokens ----
                 {
-                    float* mine = spart + w * (kHeads * kSPitch);
+                    float4* mine = reinterpret_cast<float4*>(spart) + w * (8 * kSRow) + g * kSRow;
 #pragma unroll
-                    for (int n = 0; n < 4; ++n) {
-                        *reinterpret_cast<float2*>(mine + g * kSPitch + 8 * n + 2 * t4) =
-                            make_float2(sacc[n][0], sacc[n][1]);
-                        *reinterpret_cast<float2*>(mine + (g + 8) * kSPitch + 8 * n + 2 * t4) =
-                            make_float2(sacc[n][2], sacc[n][3]);
-                    }
+                    for (int n = 0; n < 4; ++n)  // column pair 4n + t4: cols 8n + 2t4, +1
+                        mine[4 * n + t4] = make_float4(sacc[n][0], sacc[n][1], sacc[n][2], sacc[n][3]);
                 }
                 named_bar_sync(bar_id, kGroupWarps * 32);
                 float s[4];  // tokens 8w + 2t4 + {0,1}: [0..1] head g, [2..3] head g+8
@@ -371,10 +370,8 @@ __global__ void __launch_bounds__(mmak::kThreads, 1)
                     float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
 #pragma unroll
                     for (int v = 0; v < kGroupWarps; ++v) {
-                        const float* part = spart + v * (kHeads * kSPitch);
-                        const float2 x0 = *reinterpret_cast<const float2*>(part + g * kSPitch + col);
-                        const float2 x1 = *reinterpret_cast<const float2*>(part + (g + 8) * kSPitch + col);
-                        lo.x += x0.x; lo.y += x0.y; hi.x += x1.x; hi.y += x1.y;
+                        const float4 x = reinterpret_cast<const float4*>(spart)[(v * 8 + g) * kSRow + 4 * w + t4];
+                        lo.x += x.x; lo.y += x.y; hi.x += x.z; hi.y += x.w;
                     }
                     s[0] = col < hvalid ? lo.x * scale_log2 : -INFINITY;
                     s[1] = col + 1 < hvalid ? lo.y * scale_log2 : -INFINITY;
